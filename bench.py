@@ -1,0 +1,390 @@
+"""Benchmark: OPUS candidate scoring + selection throughput on B200.
+
+Workload (one "step" = one selection round over one candidate batch), the
+isolated single-layer operator: A [256 x 1024 x 768] bf16 ~ N(0,1),
+dL/dZ [256 x 1024 x 3072] bf16 ~ N(0, 1e-3), proxy target direction
+V [768 x 3072] f32 ~ N(0, 1/768), AdamW diagonal f32 ~ U(1e-6, 1e-3),
+CountSketch k = 16384 with the seed-42 bucket/sign tables; 256 candidates are
+scored and 64 (25%) are kept by Boltzmann sampling at temperature 1.0.
+Synthetic seeded data stands in for real activations.  The stage chain per
+step: AdamW table (diag folded with signs) -> target sketch CS(V^T) ->
+fused per-sample GEMM + CountSketch (the dominant kernel) -> scores phi.tau
+-> similarity phi phi^T -> Boltzmann draw.  Inputs (2 GB) exceed the 126 MB
+L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Multi-GPU (torchrun, one rank per GPU): every rank scores its own 256
+candidates and draws its own picks (the reference's default local selection
+mode), so the work per GPU is fixed (weak scaling) and no data crosses GPUs
+in the timed region.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, T, D_IN, D_OUT, K_SKETCH = 256, 1024, 768, 3072, 16384
+N_SELECT, TEMPERATURE, SEED = 64, 1.0, 42
+METRIC = "candidate seqs scored+selected/sec"
+UNIT = "candidates/s"
+WORKLOAD = "isolated single-layer operator: 256 seqs x 1024 tokens, d_in 768 -> d_out 3072, k=16384, AdamW diag"
+# dram__bytes_read.sum + dram__bytes_write.sum per sketch_gemm launch (ncu, this workload);
+# see profiles/sketch_gemm_c2_ncu.md.  None until measured.
+SKETCH_GEMM_DRAM_BYTES = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="opus_b200", choices=["opus_b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(device, rank):
+    """Seeded synthetic inputs of the workload shapes, generated on the device."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    a = torch.randn(B, T, D_IN, generator=g, device=device).to(torch.bfloat16)
+    dz = (torch.randn(B, T, D_OUT, generator=g, device=device) * 1e-3).to(torch.bfloat16)
+    V = torch.randn(D_IN, D_OUT, generator=g, device=device) * (1.0 / D_IN) ** 0.5
+    diag = torch.rand(D_OUT, D_IN, generator=g, device=device) * (1e-3 - 1e-6) + 1e-6
+    return a, dz, V, diag
+
+
+def run_gpu(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from opus_b200 import ops
+    from opus_b200.train import data_selection as ds
+    from opus_b200.train.random_projection import GradientProjector
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    a, dz, V, diag = make_inputs(dev, rank)
+    proj = GradientProjector(sketch_dim=K_SKETCH, seed=SEED, device="cuda")
+    pid = 0
+    packed = proj.packed_table(D_OUT * D_IN, pid, dev)
+    uni = torch.from_numpy(np.random.default_rng(99 + rank).random(N_SELECT)).to(dev)
+    phi = torch.empty(B, K_SKETCH, device=dev)
+    tau = torch.empty(K_SKETCH, device=dev)
+    score = torch.empty(B, device=dev)
+    sim = torch.empty(B, B, device=dev)
+    ev = {}
+
+    def step(time_kernel=False):
+        table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
+        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau)
+        phi.zero_()
+        if time_kernel:
+            ev["s"].append(torch.cuda.Event(enable_timing=True))
+            ev["e"].append(torch.cuda.Event(enable_timing=True))
+            ev["s"][-1].record()
+        ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi, accumulate=True)
+        if time_kernel:
+            ev["e"][-1].record()
+        ops.sketch_dot(phi, tau, out=score)
+        ops.sketch_gram(phi, out=sim)
+        return ops.boltzmann_select(score, sim, N_SELECT, TEMPERATURE, uni)
+
+    for _ in range(args.warmup):
+        step()
+    ops.check_device_error("bench warm-up")
+    ev["s"], ev["e"] = [], []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(time_kernel=True)
+        end.record()
+        torch.cuda.synchronize()
+    ops.check_device_error("bench timed region")
+    ms = start.elapsed_time(end)
+    kern_ms = sum(s.elapsed_time(e) for s, e in zip(ev["s"], ev["e"])) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, kern_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, kern_ms = float(t[0]), float(t[1])
+        dist.barrier()
+    ms_per_step = ms / args.steps
+
+    # per-stage breakdown (untimed for the headline; events around each stage)
+    stages = {}
+    if rank == 0:
+        names = ["table", "target_sketch", "sketch_gemm", "score", "gram", "select"]
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        reps = 5
+        acc = [0.0] * len(names)
+        for _ in range(reps):
+            evs[0].record()
+            table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
+            evs[1].record()
+            ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau)
+            evs[2].record()
+            ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi)
+            evs[3].record()
+            ops.sketch_dot(phi, tau, out=score)
+            evs[4].record()
+            ops.sketch_gram(phi, out=sim)
+            evs[5].record()
+            ops.boltzmann_select(score, sim, N_SELECT, TEMPERATURE, uni)
+            evs[6].record()
+            torch.cuda.synchronize()
+            for i in range(len(names)):
+                acc[i] += evs[i].elapsed_time(evs[i + 1]) / reps
+        stages = {n: round(x, 4) for n, x in zip(names, acc)}
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        a_h = a.cpu().pin_memory()
+        dz_h = dz.cpu().pin_memory()
+        V_h = V.cpu().pin_memory()
+        diag_h = diag.cpu().pin_memory()
+        np.random.seed(7 + rank)
+
+        def e2e_step():
+            a_d = a_h.to(dev, non_blocking=True)
+            dz_d = dz_h.to(dev, non_blocking=True)
+            V_d = V_h.to(dev, non_blocking=True)
+            diag_d = diag_h.to(dev, non_blocking=True)
+            phi_e = proj.project_full_gradient(dz_d, a_d, pid, diagonal_preconditioner=diag_d)
+            tau_e = proj.project_vector(V_d.T, pid)
+            sc = ops.sketch_dot(phi_e, tau_e)
+            sm = ops.sketch_gram(phi_e)
+            return ds.stochastic_greedy_selection(sc, sm, N_SELECT, temperature=TEMPERATURE)
+
+        e2e_steps = max(3, min(args.steps, 10))
+        for _ in range(2):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        e_ms = s2.elapsed_time(e2)
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t[0])
+        h2d = sum(x.numel() * x.element_size() for x in (a_h, dz_h, V_h, diag_h))
+        e2e = {"value": round(B * world / (e_ms / e2e_steps / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": N_SELECT * 8, "api": "GradientProjector.project_full_gradient + "
+               "project_vector + stochastic_greedy_selection", "steps": e2e_steps}
+    return ms_per_step, kern_ms, stages, e2e, clk.summary()
+
+
+def cpu_sample(budget_s=10.0, chunk=4, max_cand=B):
+    """The NumPy oracle (a port of the reference's CPU path) on a bounded sample of the workload.
+
+    Candidates are scored in chunks of `chunk` (f32 per-sample GEMM, AdamW
+    diagonal, CountSketch, dot with the target sketch) until `budget_s` of
+    work or `max_cand` candidates; the per-candidate time is extrapolated to
+    the 256-candidate step and one 64-of-256 Boltzmann draw is added.
+    Returns (candidates/s, seconds per candidate, seconds per draw, candidates sampled).
+    """
+    import numpy as np
+
+    from oracle import opus_oracle as orc
+
+    rng = np.random.default_rng(5)
+    V = (rng.standard_normal((D_IN, D_OUT)) / D_IN ** 0.5).astype(np.float32)
+    diag = rng.uniform(1e-6, 1e-3, (D_OUT, D_IN)).astype(np.float32)
+    h, s = orc.hash_sign_tables(D_OUT * D_IN, 0, K_SKETCH, seed=SEED)
+    a = rng.standard_normal((chunk, T, D_IN)).astype(np.float32)
+    dz = (rng.standard_normal((chunk, T, D_OUT)) * 1e-3).astype(np.float32)
+    sc_all = rng.standard_normal(B).astype(np.float32)
+    sim_all = (rng.standard_normal((B, B)) * 1e-3).astype(np.float32)
+    t0 = time.perf_counter()
+    tau = orc.dense_sketch(V.T, h, s, K_SKETCH)
+    phis = []
+    done = 0
+    while done < max_cand and (time.perf_counter() - t0) < budget_s:
+        phi = orc.project_full_gradient(dz, a, h, s, K_SKETCH, diag=diag, precision="f32")
+        _ = phi @ tau
+        phis.append(phi)
+        done += chunk
+    allphi = np.concatenate(phis)
+    _ = allphi @ allphi.T
+    t_score = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    orc.stochastic_greedy_selection(sc_all, sim_all, N_SELECT, TEMPERATURE, uniforms=rng.random(N_SELECT))
+    t_select = time.perf_counter() - t1
+    per_cand = t_score / done
+    step_s = per_cand * B + t_select
+    return B / step_s, per_cand, t_select, done
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    """CPU arm: the oracle port of the reference's path on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    if args.warmup > 0:
+        cpu_sample(budget_s=0.5, max_cand=4)
+    vals, counts = [], []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, _, _, done = cpu_sample(budget_s=5.0)
+        vals.append(v)
+        counts.append(done)
+        if time.perf_counter() - t0 > 150:
+            break
+    value = statistics.median(vals)
+    cores = cpu_threads()
+    sample = (f"per step: up to 5 s of candidates scored in chunks of 4 (f32 per-sample GEMM + AdamW diag + "
+              f"CountSketch + dots; {min(counts)}-{max(counts)} candidates) plus one 64-of-256 draw, "
+              "extrapolated to the 256-candidate step")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": len(vals), "warmup": args.warmup, "ms_per_step": round(B / value * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    try:
+        ms_per_step, kern_ms, stages, e2e, clocks = run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.barrier()
+    if rank == 0:
+        burst, sustained, hbm, src = measured_peaks()
+        flops = 2.0 * B * T * D_OUT * D_IN
+        achieved = flops / (kern_ms * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "sketch_gemm", "achieved": round(achieved, 2),
+                    "peak": sustained, "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
+                    "peak_kind": f"bf16 sustained ({src})", "frac_of_burst": round(achieved / burst, 4),
+                    "kernel_ms": round(kern_ms, 4), "flops_per_launch": flops,
+                    "traffic": SKETCH_GEMM_DRAM_BYTES}
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            v, per_cand, t_sel, done = cpu_sample(budget_s=10.0)
+            cpu = {"value": round(v, 4), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                   "sample": f"{done} of 256 candidates ({per_cand:.3f} s each, f32 GEMM + AdamW diag + CountSketch "
+                             f"+ dots) + one 64-of-256 draw ({t_sel:.3f} s), extrapolated to 256"}
+        value = B * world / (ms_per_step / 1e3)
+        line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": T, "k": K_SKETCH,
+                           "select": f"{N_SELECT} of {B} per GPU, Boltzmann T={TEMPERATURE}",
+                           "parallelism": f"dp{world} (candidates sharded, local selection)",
+                           "l2": "inputs 2.0 GB per GPU > 126 MB L2, no flush"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+                "gpu_launches": 6 * args.steps, "stage_ms": stages}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,180 @@
+/*
+ * opus_b200.h — C ABI of libopus_b200.so, the B200 (sm_100a) kernels behind
+ * the OPUS per-iteration data-selection path.
+ *
+ * Conventions
+ *   - Every entry point returns int: 0 (OPUS_OK) on success, otherwise an
+ *     OPUS_ERR_* code; opus_last_error() returns the message of the last
+ *     failure on the calling thread.  No C++ exception crosses this boundary.
+ *   - All array arguments are device pointers owned by the caller (unless
+ *     stated otherwise); nothing is retained after the call returns.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     asynchronous with respect to the host; results are valid after the
+ *     stream is synchronised.
+ *   - Device-side failures (a bounded wait that expired) are recorded in a
+ *     per-device error word; opus_device_error() synchronises the device and
+ *     returns and clears it.
+ *   - Matrices are row-major.  A layer weight is [d_out, d_in]; its per-sample
+ *     gradient is G_b = sum_t dLdZ[b,t,:]^T a[b,t,:], flattened row-major,
+ *     which is the element order of the CountSketch tables.
+ *
+ * Reference interfaces (gszfwsb/OPUS) each entry point replaces are cited as
+ * path:line.
+ */
+#ifndef OPUS_B200_H_
+#define OPUS_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OPUS_API __attribute__((visibility("default")))
+#else
+#define OPUS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OPUS_ABI_VERSION 1
+
+#define OPUS_OK 0
+#define OPUS_ERR_INVALID 1     /* bad argument (maps to ValueError) */
+#define OPUS_ERR_CUDA 2        /* CUDA runtime/driver failure (RuntimeError) */
+#define OPUS_ERR_UNSUPPORTED 3 /* shape/dtype outside what the kernels handle */
+#define OPUS_ERR_DEVICE 4      /* device-side error word was set */
+
+#define OPUS_DTYPE_BF16 0
+#define OPUS_DTYPE_F32 1
+
+/* Library version (OPUS_ABI_VERSION). */
+OPUS_API int opus_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+OPUS_API const char* opus_last_error(void);
+
+/* Synchronise the current device, store its device error word in *code
+ * (0 = none) and clear it.  Returns OPUS_ERR_DEVICE when *code != 0. */
+OPUS_API int opus_device_error(int* code);
+
+/*
+ * H1 — pack the reference's CountSketch tables.
+ * Replaces the tensors built by GradientProjector._get_hash_and_sign
+ * (OPUS/train/random_projection.py:51-70): hash int64 in [0,k) and sign
+ * float32 in {-1,+1}, one per weight element.  Output: one uint32 per element,
+ * bucket in bits [0,31), bit 31 set when the sign is -1 (4 B/elem instead of
+ * 12).  Fails with OPUS_ERR_INVALID if a bucket is outside [0,k) or a sign is
+ * not +-1 (checked on the device; reported through opus_device_error).
+ */
+OPUS_API int opus_pack_hash_sign(const int64_t* hash, const float* sign, int64_t numel, int64_t k,
+                        uint32_t* packed, void* stream);
+
+/* Number of 16-byte entries of the tiled epilogue table for a [d_out,d_in] layer. */
+OPUS_API int64_t opus_sketch_table_entries(int d_out, int d_in);
+
+/*
+ * P3 + H1 — per-layer epilogue table for opus_sketch_gemm: for every weight
+ * element (o,c) the bucket h(o,c) and the weight s(o,c)*D(o,c), where D is
+ *   - diag[o,c]                          if diag != NULL,
+ *   - 1/(sqrt(exp_avg_sq[o,c]) + eps)    if exp_avg_sq != NULL (AdamW),
+ *   - 1                                  otherwise (SGD / Muon / proxy side).
+ * Replaces _inv_rms_tensor_for_param (OPUS/train/data_selection.py:208-214)
+ * and the per-chunk `grad_chunk * diag` / `* s` products of
+ * project_full_gradient (OPUS/train/random_projection.py:186-190).
+ */
+OPUS_API int opus_build_sketch_table(const uint32_t* packed, const float* diag, const float* exp_avg_sq,
+                            float eps, int d_out, int d_in, void* table, int64_t table_entries,
+                            void* stream);
+
+/*
+ * S-proj (stage 3) — per-sample CountSketch of preconditioned per-sample
+ * gradients, fused: a tcgen05 GEMM forms each 128x256 tile of
+ * G_b = dLdZ_b^T a_b in TMEM and its epilogue scatters w(o,c)*G_b[o,c] into
+ * the sketch row of candidate b; G_b never reaches HBM.
+ *   dLdZ: [n_rows, seq_len, d_out], a: [n_rows, seq_len, d_in], contiguous;
+ *         dtype must be OPUS_DTYPE_BF16 (f32 operands: split each with
+ *         opus_split_bf16 and accumulate hi*hi + hi*lo + lo*hi, CountSketch
+ *         being linear).  d_out and d_in must be multiples of 8.
+ *   phi:  [ceil(n_rows/rows_div), k] f32; row b/rows_div receives candidate b
+ *         (rows_div = n_rows sums the proxy batch into one row).
+ *   accumulate = 0 zeroes phi first.
+ * Replaces GradientProjector.project_full_gradient
+ * (OPUS/train/random_projection.py:134-193) on 3-D inputs.
+ */
+OPUS_API int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
+                     int d_in, const void* table, int64_t table_entries, int64_t k, int rows_div,
+                     float* phi, int accumulate, void* stream);
+
+/*
+ * K1 — dense CountSketch of one [d_out,d_in] f32 matrix (the proxy target
+ * direction): sketch[h(o,c)] += s(o,c) * diag(o,c) * w(o,c), with w read as
+ * w[o*d_in+c] (transposed = 0) or w[c*d_out+o] (transposed = 1); diag may be
+ * NULL.  Replaces GradientProjector.project_vector
+ * (OPUS/train/random_projection.py:72-99).
+ */
+OPUS_API int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, const float* diag,
+                      int d_out, int d_in, int64_t k, float* sketch, int accumulate, void* stream);
+
+/*
+ * K2 — de-sketched target for the ghost contraction:
+ * v[o,c] = scale * D(o,c) * s(o,c) * tau[h(o,c)] written as a bf16 pair
+ * v_bf16 = [2, d_out, d_in] (hi = bf16(v), lo = bf16(v - hi)), D as in
+ * opus_build_sketch_table.  With it, <D o G_b, s . tau[h]> over the
+ * sketch equals the dense inner product <G_b, v> (CountSketch is linear), the
+ * identity behind data_selection.py:509-523.
+ */
+OPUS_API int opus_desketch(const float* tau, const uint32_t* packed, const float* diag, const float* exp_avg_sq,
+                  float eps, int d_out, int d_in, int64_t k, float scale, void* v_bf16, void* stream);
+
+/*
+ * K3 (stage 2) — ghost per-sample inner products against a dense target:
+ * score[b] (+)= alpha * sum_t dLdZ[b,t,:] . (v a[b,t,:]), i.e. <G_b, v>,
+ * without forming G_b.  tcgen05 GEMM U = a v^T per 128-token x 256-output
+ * tile with a fused row-dot epilogue against the dLdZ tile; U never reaches
+ * HBM.  a, dLdZ: bf16 [n_rows, seq_len, d_in|d_out]; v_bf16: the bf16 pair
+ * [2, d_out, d_in] (hi, lo) of the f32 target, both multiplied (two MMAs per
+ * K step) so the target keeps ~16 mantissa bits.  accumulate = 0 zeroes
+ * score[0:n_rows] first.
+ * Replaces the score side of weighted_grad_dotprod / grad_dotprod
+ * (OPUS/train/data_selection.py:255-292, 597-619) with the target averaged
+ * over the proxy batch.
+ */
+OPUS_API int opus_ghost_score(const void* a, const void* dLdZ, int dtype, int n_rows, int seq_len, int d_in,
+                     int d_out, const void* v_bf16, float alpha, float* score, int accumulate,
+                     void* stream);
+
+/* score[b] (+)= alpha * phi[b,:] . tau[:]  (data_selection.py:523, 531-536). */
+OPUS_API int opus_sketch_dot(const float* phi, const float* tau, int n_rows, int64_t k, float alpha, float* score,
+                    int accumulate, void* stream);
+
+/* out[i,j] (+)= alpha * phi_a[i,:] . phi_b[j,:]; out is [rows_a, rows_b]
+ * (data_selection.py:523 per_val, 579 + 587-588 similarity). */
+OPUS_API int opus_sketch_gram(const float* phi_a, int rows_a, const float* phi_b, int rows_b, int64_t k, float alpha,
+                     float* out, int accumulate, void* stream);
+
+/*
+ * S1 (stage 5) — Boltzmann sampling of n_select of n candidates with the
+ * interaction penalty, on one CTA.  uniforms[i] is the double the reference's
+ * i-th np.random.choice call draws (np.random.random_sample()).  Same float32
+ * arithmetic as stochastic_greedy_selection (data_selection.py:641-675):
+ * scaled = score/T, max-shift only above 700, float32 exp, numpy pairwise
+ * float32 sum, uniform fallback for a zero/non-finite sum, float64 cumsum and
+ * searchsorted(side='right').  n <= 8192; n_select <= n.  out_idx: int64.
+ */
+OPUS_API int opus_boltzmann_select(const float* scores, const float* sim, int n, int n_select, double temperature,
+                          const double* uniforms, int64_t* out_idx, void* stream);
+
+/* S2 — greedy_selection (data_selection.py:622-638): argmax (first max; NaN
+ * wins as in np.argmax), scores -= sim[idx], scores[idx] = -inf. */
+OPUS_API int opus_greedy_select(const float* scores, const float* sim, int n, int n_select, int64_t* out_idx,
+                       void* stream);
+
+/* f32 -> bf16 pair: hi = bf16_rn(x), lo = bf16_rn(x - hi), n elements.
+ * Used to feed f32 activations/gradients to the bf16 tensor-core kernels. */
+OPUS_API int opus_split_bf16(const float* x, int64_t n, void* hi, void* lo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OPUS_B200_H_ */

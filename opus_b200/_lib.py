@@ -1,0 +1,100 @@
+"""ctypes binding of libopus_b200.so (the C ABI declared in include/opus_b200.h).
+
+The library is built in-tree (``python -m opus_b200.csrc.build``).  Loading
+fails loudly when it is missing: the selection path has no host fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libopus_b200.so")
+HEADER_PATH = Path(__file__).resolve().parent.parent / "include" / "opus_b200.h"
+
+OPUS_OK = 0
+OPUS_ERR_INVALID = 1
+OPUS_ERR_CUDA = 2
+OPUS_ERR_UNSUPPORTED = 3
+OPUS_ERR_DEVICE = 4
+
+DTYPE_BF16 = 0
+DTYPE_F32 = 1
+
+_c_int, _c_i64, _c_f32, _c_f64, _c_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_double, ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/opus_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "opus_abi_version": (_c_int, []),
+    "opus_last_error": (ctypes.c_char_p, []),
+    "opus_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
+    "opus_pack_hash_sign": (_c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p]),
+    "opus_sketch_table_entries": (_c_i64, [_c_int, _c_int]),
+    "opus_build_sketch_table": (_c_int, [_c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_p, _c_i64, _c_p]),
+    "opus_sketch_gemm": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_i64, _c_int,
+                                  _c_p, _c_int, _c_p]),
+    "opus_sketch_dense": (_c_int, [_c_p, _c_int, _c_p, _c_p, _c_int, _c_int, _c_i64, _c_p, _c_int, _c_p]),
+    "opus_desketch": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_i64, _c_f32, _c_p, _c_p]),
+    "opus_ghost_score": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_f32, _c_p, _c_int,
+                                  _c_p]),
+    "opus_sketch_dot": (_c_int, [_c_p, _c_p, _c_int, _c_i64, _c_f32, _c_p, _c_int, _c_p]),
+    "opus_sketch_gram": (_c_int, [_c_p, _c_int, _c_p, _c_int, _c_i64, _c_f32, _c_p, _c_int, _c_p]),
+    "opus_boltzmann_select": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_f64, _c_p, _c_p, _c_p]),
+    "opus_greedy_select": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_p, _c_p]),
+    "opus_split_bf16": (_c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def header_symbols() -> list[str]:
+    """Every entry point declared with OPUS_API in include/opus_b200.h."""
+    text = HEADER_PATH.read_text()
+    return sorted(set(re.findall(r"OPUS_API\s+[\w\s\*]+?\b(opus_\w+)\s*\(", text)))
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library with argument types declared."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is not built; run `python -m opus_b200.csrc.build` "
+                "(the OPUS selection path has no fallback without its CUDA kernels)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().opus_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    """Map a non-zero status to the exception type the reference raises."""
+    if rc == OPUS_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc == OPUS_ERR_INVALID:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def device_error() -> int:
+    """Synchronise the current device and return (and clear) its error word."""
+    code = _c_int(0)
+    rc = load().opus_device_error(ctypes.byref(code))
+    if rc not in (OPUS_OK, OPUS_ERR_DEVICE):
+        check(rc, "opus_device_error")
+    return int(code.value)

@@ -1,0 +1,166 @@
+// Memory-bound kernels of the selection path:
+//   opus_sketch_dense  K1: CountSketch of one dense matrix (proxy target)
+//   opus_sketch_dot    score[b] (+)= alpha * phi[b] . tau
+//   opus_split_bf16    f32 -> bf16 hi + bf16 lo (x ~= hi + lo to 2^-16)
+#include "opus_common.cuh"
+
+namespace opus {
+namespace {
+
+constexpr int kDenseThreads = 256;
+constexpr int kDenseTile = 32;  // 32 x 32 (o, c) tiles
+
+// Grid-stride over 32x32 tiles of the [d_out, d_in] grid.  The weight tile is
+// read in its stored orientation (coalesced either way) and staged through
+// shared memory; the packed table is read row-major.  Scatter goes to a
+// CTA-private shared sketch (flushed with vector reductions) when it fits,
+// otherwise straight to global memory.
+__global__ void __launch_bounds__(kDenseThreads) dense_sketch_kernel(const float* __restrict__ w, int transposed,
+                                                                     const uint32_t* __restrict__ packed,
+                                                                     const float* __restrict__ diag, int d_out,
+                                                                     int d_in, int64_t k, float* __restrict__ out,
+                                                                     int smem_sketch) {
+  extern __shared__ float sk[];
+  __shared__ float tile_w[kDenseTile][kDenseTile + 1];
+  if (smem_sketch)
+    for (int64_t i = threadIdx.x; i < k; i += kDenseThreads) sk[i] = 0.0f;
+  __syncthreads();
+  float* dst = smem_sketch ? sk : out;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const int n_to = (d_out + kDenseTile - 1) / kDenseTile, n_tc = (d_in + kDenseTile - 1) / kDenseTile;
+  const int64_t n_tiles = (int64_t)n_to * n_tc;
+  for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const int o0 = static_cast<int>(t / n_tc) * kDenseTile, c0 = static_cast<int>(t % n_tc) * kDenseTile;
+    for (int rr = ty; rr < kDenseTile; rr += 8) {
+      if (!transposed) {
+        const int o = o0 + rr, c = c0 + tx;
+        tile_w[rr][tx] = (o < d_out && c < d_in) ? w[(int64_t)o * d_in + c] : 0.0f;
+      } else {
+        const int c = c0 + rr, o = o0 + tx;
+        tile_w[tx][rr] = (o < d_out && c < d_in) ? w[(int64_t)c * d_out + o] : 0.0f;
+      }
+    }
+    __syncthreads();
+    for (int rr = ty; rr < kDenseTile; rr += 8) {
+      const int o = o0 + rr, c = c0 + tx;
+      if (o < d_out && c < d_in) {
+        const int64_t idx = (int64_t)o * d_in + c;
+        const uint32_t hv = packed[idx];
+        float x = tile_w[rr][tx];
+        if (diag != nullptr) x = x * diag[idx];
+        if (hv & 0x80000000u) x = -x;
+        const uint32_t bucket = hv & 0x7FFFFFFFu;
+        if (bucket < static_cast<uint64_t>(k)) atomicAdd(dst + bucket, x);
+      }
+    }
+    __syncthreads();
+  }
+  if (smem_sketch) {
+    if ((k & 3) == 0) {
+      const float4* s4 = reinterpret_cast<const float4*>(sk);
+      for (int64_t i = threadIdx.x; i < k / 4; i += kDenseThreads) {
+        const float4 x = s4[i];
+        if (x.x != 0.0f || x.y != 0.0f || x.z != 0.0f || x.w != 0.0f) red_add_v4(out + 4 * i, x.x, x.y, x.z, x.w);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < k; i += kDenseThreads)
+        if (sk[i] != 0.0f) atomicAdd(out + i, sk[i]);
+    }
+  }
+}
+
+// One CTA per row: 128-bit loads, warp shuffle + shared reduction.
+__global__ void __launch_bounds__(256) sketch_dot_kernel(const float* __restrict__ phi, const float* __restrict__ tau,
+                                                         int64_t k, float alpha, float* __restrict__ score,
+                                                         int accumulate) {
+  const int64_t row = blockIdx.x;
+  const float* p = phi + row * k;
+  float acc = 0.0f;
+  if ((k & 3) == 0) {
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    const float4* t4 = reinterpret_cast<const float4*>(tau);
+    for (int64_t i = threadIdx.x; i < k / 4; i += 256) {
+      const float4 a = p4[i], b = t4[i];
+      acc = fmaf(a.x, b.x, acc);
+      acc = fmaf(a.y, b.y, acc);
+      acc = fmaf(a.z, b.z, acc);
+      acc = fmaf(a.w, b.w, acc);
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < k; i += 256) acc = fmaf(p[i], tau[i], acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  __shared__ float part[8];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < 8; ++i) s += part[i];
+    score[row] = accumulate ? score[row] + alpha * s : alpha * s;
+  }
+}
+
+__global__ void split_bf16_kernel(const float* __restrict__ x, int64_t n, __nv_bfloat16* __restrict__ hi,
+                                  __nv_bfloat16* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
+}  // namespace
+}  // namespace opus
+
+using namespace opus;
+
+extern "C" {
+
+int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, const float* diag, int d_out, int d_in,
+                      int64_t k, float* sketch, int accumulate, void* stream) {
+  if (d_out <= 0 || d_in <= 0 || k <= 0 || k > 0x7FFFFFFF) return set_error(OPUS_ERR_INVALID, "sketch_dense: bad sizes");
+  if (!w || !packed || !sketch) return set_error(OPUS_ERR_INVALID, "sketch_dense: NULL pointer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (!accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(sketch, 0, (size_t)k * sizeof(float), st));
+  const int64_t numel = (int64_t)d_out * d_in;
+  const size_t sk_bytes = (size_t)k * sizeof(float);
+  const int smem_sketch = sk_bytes <= 96 * 1024 ? 1 : 0;
+  const int64_t n_tiles = (int64_t)((d_out + kDenseTile - 1) / kDenseTile) * ((d_in + kDenseTile - 1) / kDenseTile);
+  int64_t grid = smem_sketch ? numel / (2 * k) : (int64_t)sm_count() * 4;
+  if (grid < 1) grid = 1;
+  if (grid > 2 * sm_count()) grid = 2 * sm_count();
+  if (grid > n_tiles) grid = n_tiles;
+  const size_t dyn = smem_sketch ? sk_bytes : 0;
+  if (dyn > 48 * 1024)
+    OPUS_CUDA_TRY(cudaFuncSetAttribute(dense_sketch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
+  dense_sketch_kernel<<<(int)grid, kDenseThreads, dyn, st>>>(w, transposed, packed, diag, d_out, d_in, k, sketch,
+                                                              smem_sketch);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+int opus_sketch_dot(const float* phi, const float* tau, int n_rows, int64_t k, float alpha, float* score,
+                    int accumulate, void* stream) {
+  if (n_rows < 0 || k <= 0) return set_error(OPUS_ERR_INVALID, "sketch_dot: bad sizes");
+  if (n_rows == 0) return OPUS_OK;
+  if (!phi || !tau || !score) return set_error(OPUS_ERR_INVALID, "sketch_dot: NULL pointer");
+  sketch_dot_kernel<<<n_rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(phi, tau, k, alpha, score, accumulate);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+int opus_split_bf16(const float* x, int64_t n, void* hi, void* lo, void* stream) {
+  if (n < 0) return set_error(OPUS_ERR_INVALID, "split_bf16: bad size");
+  if (n == 0) return OPUS_OK;
+  if (!x || !hi || !lo) return set_error(OPUS_ERR_INVALID, "split_bf16: NULL pointer");
+  int64_t grid = (n + 255) / 256;
+  if (grid > (int64_t)sm_count() * 16) grid = (int64_t)sm_count() * 16;
+  split_bf16_kernel<<<(int)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, n, reinterpret_cast<__nv_bfloat16*>(hi), reinterpret_cast<__nv_bfloat16*>(lo));
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+}  // extern "C"

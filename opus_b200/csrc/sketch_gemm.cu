@@ -1,0 +1,365 @@
+// Fused per-sample gradient GEMM + CountSketch scatter (stage 3 of the
+// selection path), sm_100a.
+//
+// For candidate b and weight tile (ob, cb) the CTA computes the 128 x 256
+// tile of G_b = dLdZ_b^T a_b (K = the candidate's tokens) with tcgen05.mma
+// (bf16 x bf16 -> f32 in TMEM), then its epilogue multiplies every element by
+// w(o,c) = s(o,c) * D(o,c) from the precomputed table and adds it into bucket
+// h(o,c) of candidate b's sketch.  G_b is never written to HBM.
+//
+// Warp roles (192 threads, persistent, one CTA per SM):
+//   warp 0      TMA producer: 3-D tile loads of dLdZ and a into a ring of
+//               shared-memory stages (128-byte swizzle, MN-major operands);
+//   warp 1      TMEM allocation + single-thread UMMA issue into one of two
+//               256-column accumulators (double-buffered against the epilogue);
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, table lookup,
+//               shared-memory atomic scatter into the CTA's private sketch,
+//               flushed to HBM with vector reductions when the candidate row
+//               changes (or scattered straight to HBM when k is too large for
+//               shared memory).
+// Work units (b, ob, cb) are numbered candidate-major and split into equal
+// contiguous ranges, one per CTA.
+#include <cstdio>
+
+#include "opus_common.cuh"
+#include "sketch_layout.cuh"
+
+namespace opus {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr int kBoxMN = 64;                           // bf16 elements per 128-byte swizzle row
+constexpr int kBK = 64;                              // tokens per pipeline stage
+constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
+constexpr int kKSteps = kBK / kUmmaK;                // 4 MMAs per stage
+constexpr int kGBoxes = kTileM / kBoxMN;             // 2 boxes for the 128 weight rows
+constexpr int kABoxes = kTileN / kBoxMN;             // 4 boxes for the 256 weight columns
+constexpr int kBoxBytes = kBoxMN * 2 * kBK;          // 8 KB
+constexpr int kGTileBytes = kGBoxes * kBoxBytes;     // 16 KB
+constexpr int kATileBytes = kABoxes * kBoxBytes;     // 32 KB
+constexpr int kStageBytes = kGTileBytes + kATileBytes;  // 48 KB
+// MN-major SW128 canonical layout: 64 contiguous MN elements x 8 K rows per
+// 1024-B atom; atoms along K at SBO = 1024 B, along MN (next box) at LBO.
+constexpr uint32_t kLBO = kBoxBytes;
+constexpr uint32_t kSBO = 1024;
+constexpr uint32_t kKStepBytes = (kUmmaK / 8) * 1024;  // 2 atoms per MMA
+constexpr uint32_t kIdesc = make_idesc(/*bf16*/ 1, /*a MN-major*/ 1, /*b MN-major*/ 1, kTileM, kTileN);
+constexpr int kTmemCols = 2 * kTileN;  // two accumulators
+
+struct SmemPlan {
+  int stages;
+  int smem_sketch;   // 1: CTA-private sketch in shared memory
+  size_t bytes;      // dynamic shared memory to request
+};
+
+__device__ __forceinline__ uint4 ld_nc_na(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Bounded barrier over the 128 epilogue threads (an mbarrier, so that a
+// thread that gave up cannot leave the others blocked forever).
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatile int* abort_flag, int* err) {
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase, abort_flag, err, kDevTimeoutGroup);
+  phase ^= 1;
+  return ok;
+}
+
+__device__ bool flush_sketch(float* sk, float* dst, int64_t k, int et, uint64_t* bar, uint32_t& phase,
+                             volatile int* abort_flag, int* err) {
+  if (!epi_sync(bar, phase, abort_flag, err)) return false;
+  if ((k & 3) == 0) {
+    float4* s4 = reinterpret_cast<float4*>(sk);
+    for (int64_t i = et; i < k / 4; i += kEpiThreads) {
+      const float4 x = s4[i];
+      if (x.x != 0.0f || x.y != 0.0f || x.z != 0.0f || x.w != 0.0f) {
+        red_add_v4(dst + 4 * i, x.x, x.y, x.z, x.w);
+        s4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    }
+  } else {
+    for (int64_t i = et; i < k; i += kEpiThreads) {
+      const float x = sk[i];
+      if (x != 0.0f) {
+        atomicAdd(dst + i, x);
+        sk[i] = 0.0f;
+      }
+    }
+  }
+  return epi_sync(bar, phase, abort_flag, err);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
+                       const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
+                       int n_cb, int64_t k, int rows_div, int stages, int smem_sketch, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* stage_mem = smem;
+  float* sk = reinterpret_cast<float*>(smem + (size_t)stages * kStageBytes);
+  uint8_t* tail = smem + (size_t)stages * kStageBytes + (smem_sketch ? (size_t)k * 4 : 0);
+  tail = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tail) + 15) & ~uintptr_t(15));
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* epi_bar = tempty + 2;
+  uint64_t* drain_bar = epi_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tiles_per_row = (int64_t)n_ob * n_cb;
+  const int64_t units = (int64_t)n_rows * tiles_per_row;
+  const int64_t u_begin = units * blockIdx.x / gridDim.x;
+  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
+  const int n_kb = (seq_len + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpiThreads);
+    }
+    mbar_init(epi_bar, kEpiThreads);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_g);
+    prefetch_tmap(&tm_a);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (smem_sketch) {
+    for (int64_t i = threadIdx.x; i < k; i += kThreads) sk[i] = 0.0f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int64_t u = u_begin; u < u_end; ++u) {
+        const int b = static_cast<int>(u / tiles_per_row);
+        const int rem = static_cast<int>(u % tiles_per_row);
+        const int ob = rem / n_cb, cb = rem % n_cb;
+        bool ok = true;
+        for (int kb = 0; kb < n_kb; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          uint8_t* sg = stage_mem + (size_t)s * kStageBytes;
+          uint8_t* sa = sg + kGTileBytes;
+          const int t0 = kb * kBK;
+#pragma unroll
+          for (int i = 0; i < kGBoxes; ++i) tma_load_3d(sg + i * kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b);
+#pragma unroll
+          for (int i = 0; i < kABoxes; ++i) tma_load_3d(sa + i * kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int64_t u = u_begin; u < u_end && ok; ++u) {
+        if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, err, kDevTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
+        for (int kb = 0; kb < n_kb; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, err, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ag = smem_u32(stage_mem + (size_t)s * kStageBytes);
+          const uint32_t aa = ag + kGTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kKSteps; ++kk) {
+            const uint64_t da = make_sdesc_sw128(ag + kk * kKStepBytes, kLBO, kSBO);
+            const uint64_t db = make_sdesc_sw128(aa + kk * kKStepBytes, kLBO, kSBO);
+            umma_bf16(d_tmem, da, db, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          aph ^= 1;
+        }
+      }
+      // Drain: every MMA issued above must be complete before TMEM is freed.
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0, nullptr, err, kDevTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x - 64;          // 0..127
+    const int q = warp & 3;                   // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;              // tile row owned by this thread
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    int acc = 0;
+    uint32_t aph = 0;
+    uint32_t epi_phase = 0;
+    int64_t cur_row = -1;
+    bool bad = false;
+    bool ok = true;
+    for (int64_t u = u_begin; u < u_end; ++u) {
+      const int b = static_cast<int>(u / tiles_per_row);
+      const int64_t tile = u % tiles_per_row;
+      const int64_t row = b / rows_div;
+      if (smem_sketch && row != cur_row) {
+        if (cur_row >= 0 && !flush_sketch(sk, phi + cur_row * k, k, et, epi_bar, epi_phase, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        cur_row = row;
+      }
+      if (!mbar_wait(&tfull[acc], aph, abort_flag, err, kDevTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float* dst = smem_sketch ? sk : phi + row * k;
+      const uint4* tp = table + tile * kEntriesPerTile + r;
+      const uint32_t kk32 = static_cast<uint32_t>(k);
+#pragma unroll 1
+      for (int j = 0; j < kChunksPerTile; ++j) {
+        uint32_t v[32];
+        tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTileN + j * kChunkCols), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int p = 0; p < kPairsPerChunk; ++p) {
+          const uint4 e = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
+          const float x0 = __uint_as_float(v[2 * p]) * __uint_as_float(e.z);
+          const float x1 = __uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w);
+          if (e.x < kk32) atomicAdd(dst + e.x, x0); else bad = true;
+          if (e.y < kk32) atomicAdd(dst + e.y, x1); else bad = true;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        aph ^= 1;
+      }
+    }
+    if (ok && smem_sketch && cur_row >= 0) flush_sketch(sk, phi + cur_row * k, k, et, epi_bar, epi_phase, abort_flag, err);
+    if (bad) record_device_error(err, kDevBadBucket);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+SmemPlan plan_smem(int64_t k) {
+  const size_t limit = static_cast<size_t>(max_smem_optin());
+  const size_t fixed = 1024 /*alignment slack*/ + 16 + 8 * (2 * 8 + 6) + 16;
+  SmemPlan p{0, 0, 0};
+  for (int st = 6; st >= 2; --st) {
+    const size_t need = fixed + (size_t)st * kStageBytes + (size_t)k * 4;
+    if (need <= limit) {
+      p = {st, 1, need};
+      return p;
+    }
+  }
+  // Sketch does not fit next to two stages: scatter straight into HBM/L2.
+  for (int st = 4; st >= 2; --st) {
+    const size_t need = fixed + (size_t)st * kStageBytes;
+    if (need <= limit) return {st, 0, need};
+  }
+  return p;
+}
+
+}  // namespace
+}  // namespace opus
+
+using namespace opus;
+
+extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
+                                int d_in, const void* table, int64_t table_entries_given, int64_t k, int rows_div,
+                                float* phi, int accumulate, void* stream) {
+  if (dtype != OPUS_DTYPE_BF16)
+    return set_error(OPUS_ERR_UNSUPPORTED,
+                     "sketch_gemm: operands must be bf16 (split f32 operands into bf16 hi/lo with opus_split_bf16)");
+  if (n_rows < 0 || seq_len < 0 || d_out <= 0 || d_in <= 0 || k <= 0 || k > 0x7FFFFFFF || rows_div <= 0)
+    return set_error(OPUS_ERR_INVALID, "sketch_gemm: bad sizes (n=%d T=%d d_out=%d d_in=%d k=%lld rows_div=%d)",
+                     n_rows, seq_len, d_out, d_in, (long long)k, rows_div);
+  if (!table || !phi || (n_rows > 0 && (!dLdZ || !a))) return set_error(OPUS_ERR_INVALID, "sketch_gemm: NULL pointer");
+  if (table_entries_given < table_entries(d_out, d_in))
+    return set_error(OPUS_ERR_INVALID, "sketch_gemm: table holds %lld entries, need %lld",
+                     (long long)table_entries_given, (long long)table_entries(d_out, d_in));
+  if (d_out % 8 != 0 || d_in % 8 != 0)
+    return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: d_out and d_in must be multiples of 8 (got %d, %d)", d_out,
+                     d_in);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t out_rows = n_rows == 0 ? 0 : (n_rows + rows_div - 1) / rows_div;
+  if (!accumulate && out_rows > 0) OPUS_CUDA_TRY(cudaMemsetAsync(phi, 0, (size_t)out_rows * k * sizeof(float), st));
+  if (n_rows == 0 || seq_len == 0) return OPUS_OK;
+
+  CUtensorMap tm_g, tm_a;
+  {
+    const uint64_t dims[3] = {(uint64_t)d_out, (uint64_t)seq_len, (uint64_t)n_rows};
+    const uint64_t strides[2] = {(uint64_t)d_out * 2, (uint64_t)seq_len * d_out * 2};
+    const uint32_t box[3] = {kBoxMN, kBK, 1};
+    int rc = encode_tmap(&tm_g, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dLdZ, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)d_in, (uint64_t)seq_len, (uint64_t)n_rows};
+    const uint64_t strides[2] = {(uint64_t)d_in * 2, (uint64_t)seq_len * d_in * 2};
+    const uint32_t box[3] = {kBoxMN, kBK, 1};
+    int rc = encode_tmap(&tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  const SmemPlan plan = plan_smem(k);
+  if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small");
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(plan.bytes)));
+  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
+  const int64_t units = (int64_t)n_rows * n_ob * n_cb;
+  const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
+  int* err = device_error_word();
+  sketch_gemm_kernel<<<grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows,
+                                                        seq_len, n_ob, n_cb, k, rows_div, plan.stages, plan.smem_sketch,
+                                                        err);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}

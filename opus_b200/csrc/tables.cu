@@ -1,0 +1,154 @@
+// CountSketch tables and preconditioner folding (memory-bound, one pass each).
+//
+//   opus_pack_hash_sign     int64 bucket + f32 sign  ->  uint32 (bucket | neg<<31)
+//   opus_build_sketch_table packed + AdamW diag      ->  tiled epilogue table
+//   opus_desketch           tau + packed + diag      ->  dense bf16 hi/lo target
+#include "opus_common.cuh"
+#include "sketch_layout.cuh"
+
+namespace opus {
+namespace {
+
+__global__ void pack_kernel(const int64_t* __restrict__ hash, const float* __restrict__ sign, int64_t numel,
+                            int64_t k, uint32_t* __restrict__ out, int* err) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < numel; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t h = hash[i];
+    const float s = sign[i];
+    uint32_t v = 0;
+    if (h < 0 || h >= k || !(s == 1.0f || s == -1.0f)) {
+      record_device_error(err, kDevBadBucket);
+    } else {
+      v = static_cast<uint32_t>(h) | (s < 0.0f ? 0x80000000u : 0u);
+    }
+    out[i] = v;
+  }
+}
+
+// AdamW diagonal exactly as torch evaluates (v.sqrt() + eps).reciprocal() in
+// f32: correctly rounded sqrt, f32 add, correctly rounded reciprocal.
+__device__ __forceinline__ float adam_diag(float v, float eps) {
+  return __frcp_rn(__fadd_rn(__fsqrt_rn(v), eps));
+}
+
+__device__ __forceinline__ float element_weight(const float* diag, const float* v, float eps, int64_t idx) {
+  if (diag != nullptr) return diag[idx];
+  if (v != nullptr) return adam_diag(v[idx], eps);
+  return 1.0f;
+}
+
+// One CTA per (tile, 32-column chunk): stage 128 rows x 32 columns of the
+// packed table and weights in shared memory with coalesced row reads, then
+// write them in the epilogue's lane-fastest order with coalesced 16-B stores.
+__global__ void __launch_bounds__(256) build_table_kernel(const uint32_t* __restrict__ packed,
+                                                          const float* __restrict__ diag,
+                                                          const float* __restrict__ v, float eps, int d_out,
+                                                          int d_in, int n_cb, uint4* __restrict__ table) {
+  __shared__ uint32_t sh[kTileM][kChunkCols + 1];
+  __shared__ float sw[kTileM][kChunkCols + 1];
+  const int tile = blockIdx.x / kChunksPerTile;
+  const int j = blockIdx.x % kChunksPerTile;
+  const int ob = tile / n_cb, cb = tile % n_cb;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = cb * kTileN + j * kChunkCols + lane;
+  for (int r = warp; r < kTileM; r += 8) {
+    const int o = ob * kTileM + r;
+    uint32_t hv = 0;
+    float wv = 0.0f;
+    if (o < d_out && c < d_in) {
+      const int64_t idx = (int64_t)o * d_in + c;
+      hv = packed[idx];
+      const float d = element_weight(diag, v, eps, idx);
+      wv = (hv & 0x80000000u) ? -d : d;
+      hv &= 0x7FFFFFFFu;
+    }
+    sh[r][lane] = hv;
+    sw[r][lane] = wv;
+  }
+  __syncthreads();
+  uint4* out = table + ((int64_t)tile * kChunksPerTile + j) * (kPairsPerChunk * kTileM);
+  for (int e = threadIdx.x; e < kPairsPerChunk * kTileM; e += 256) {
+    const int p = e / kTileM, r = e % kTileM;
+    uint4 q;
+    q.x = sh[r][2 * p];
+    q.y = sh[r][2 * p + 1];
+    q.z = __float_as_uint(sw[r][2 * p]);
+    q.w = __float_as_uint(sw[r][2 * p + 1]);
+    out[e] = q;
+  }
+}
+
+__global__ void desketch_kernel(const float* __restrict__ tau, const uint32_t* __restrict__ packed,
+                                const float* __restrict__ diag, const float* __restrict__ v, float eps,
+                                int64_t numel, float scale, __nv_bfloat16* __restrict__ hi,
+                                __nv_bfloat16* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < numel; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t hv = packed[i];
+    const float d = element_weight(diag, v, eps, i);
+    float x = __fmul_rn(__fmul_rn(scale, d), tau[hv & 0x7FFFFFFFu]);
+    if (hv & 0x80000000u) x = -x;
+    const __nv_bfloat16 h = __float2bfloat16_rn(x);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(x - __bfloat162float(h));
+  }
+}
+
+int grid_for(int64_t n, int threads) {
+  int64_t g = (n + threads - 1) / threads;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+}  // namespace opus
+
+using namespace opus;
+
+extern "C" {
+
+int opus_pack_hash_sign(const int64_t* hash, const float* sign, int64_t numel, int64_t k, uint32_t* packed,
+                        void* stream) {
+  if (numel < 0 || k <= 0 || k > 0x7FFFFFFF) return set_error(OPUS_ERR_INVALID, "pack: bad numel/k");
+  if (numel == 0) return OPUS_OK;
+  if (!hash || !sign || !packed) return set_error(OPUS_ERR_INVALID, "pack: NULL pointer");
+  int* err = device_error_word();
+  pack_kernel<<<grid_for(numel, 256), 256, 0, (cudaStream_t)stream>>>(hash, sign, numel, k, packed, err);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+int64_t opus_sketch_table_entries(int d_out, int d_in) {
+  if (d_out <= 0 || d_in <= 0) return 0;
+  return table_entries(d_out, d_in);
+}
+
+int opus_build_sketch_table(const uint32_t* packed, const float* diag, const float* exp_avg_sq, float eps,
+                            int d_out, int d_in, void* table, int64_t table_entries_given, void* stream) {
+  if (d_out <= 0 || d_in <= 0) return set_error(OPUS_ERR_INVALID, "table: bad shape %d x %d", d_out, d_in);
+  if (!packed || !table) return set_error(OPUS_ERR_INVALID, "table: NULL pointer");
+  if (table_entries_given < table_entries(d_out, d_in))
+    return set_error(OPUS_ERR_INVALID, "table: buffer holds %lld entries, need %lld",
+                     (long long)table_entries_given, (long long)table_entries(d_out, d_in));
+  if ((reinterpret_cast<uintptr_t>(table) & 15) != 0) return set_error(OPUS_ERR_INVALID, "table: not 16-B aligned");
+  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
+  const int blocks = n_ob * n_cb * kChunksPerTile;
+  build_table_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(packed, diag, exp_avg_sq, eps, d_out, d_in, n_cb,
+                                                              reinterpret_cast<uint4*>(table));
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+int opus_desketch(const float* tau, const uint32_t* packed, const float* diag, const float* exp_avg_sq, float eps,
+                  int d_out, int d_in, int64_t k, float scale, void* v_bf16, void* stream) {
+  if (d_out <= 0 || d_in <= 0 || k <= 0) return set_error(OPUS_ERR_INVALID, "desketch: bad shape");
+  if (!tau || !packed || !v_bf16) return set_error(OPUS_ERR_INVALID, "desketch: NULL pointer");
+  const int64_t numel = (int64_t)d_out * d_in;
+  __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(v_bf16);
+  desketch_kernel<<<grid_for(numel, 256), 256, 0, (cudaStream_t)stream>>>(tau, packed, diag, exp_avg_sq, eps, numel,
+                                                                          scale, hi, hi + numel);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+}  // extern "C"

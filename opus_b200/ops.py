@@ -1,0 +1,285 @@
+"""Torch-tensor front end of the C ABI (include/opus_b200.h).
+
+Every function here takes CUDA tensors, launches on the current CUDA stream of
+the tensors' device and returns CUDA tensors.  There is no CPU path: a CPU
+tensor or a missing libopus_b200.so raises.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_ERR_BAD_PROBS = 0x301
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _cuda(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the OPUS B200 path runs on the GPU only)")
+    return t
+
+
+def _contig(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def check_device_error(what: str = "opus kernel") -> None:
+    """Synchronise and raise if a kernel recorded a device-side error."""
+    code = _lib.device_error()
+    if code == _ERR_BAD_PROBS:
+        raise ValueError(f"{what}: probabilities do not sum to 1")
+    if code:
+        raise RuntimeError(f"{what}: device error 0x{code:x}")
+
+
+# --------------------------------------------------------------------- tables
+def pack_hash_sign(hash_: torch.Tensor, sign: torch.Tensor, k: int, validate: bool = True) -> torch.Tensor:
+    """int64 buckets + float32 +-1 signs -> uint32 (stored as int32) packed table."""
+    _cuda(hash_, "hash")
+    _cuda(sign, "sign")
+    if hash_.dtype != torch.int64 or sign.dtype != torch.float32:
+        raise ValueError("hash must be int64 and sign float32")
+    if hash_.numel() != sign.numel():
+        raise ValueError("hash and sign must have the same number of elements")
+    h, s = _contig(hash_.reshape(-1)), _contig(sign.reshape(-1))
+    out = torch.empty(h.numel(), dtype=torch.int32, device=h.device)
+    _lib.check(_lib.load().opus_pack_hash_sign(_ptr(h), _ptr(s), h.numel(), int(k), _ptr(out), _stream(h)),
+               "opus_pack_hash_sign")
+    if validate:
+        check_device_error("opus_pack_hash_sign (bucket outside [0,k) or sign not +-1)")
+    return out
+
+
+def sketch_table_entries(d_out: int, d_in: int) -> int:
+    return int(_lib.load().opus_sketch_table_entries(int(d_out), int(d_in)))
+
+
+def build_sketch_table(packed: torch.Tensor, d_out: int, d_in: int, diag: torch.Tensor | None = None,
+                       exp_avg_sq: torch.Tensor | None = None, eps: float = 1e-8,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tiled (bucket, sign*D) epilogue table for sketch_gemm; 16 bytes per entry."""
+    _cuda(packed, "packed")
+    n = sketch_table_entries(d_out, d_in)
+    if packed.numel() != d_out * d_in:
+        raise ValueError(f"packed table has {packed.numel()} elements, layer has {d_out * d_in}")
+    for name, t in (("diag", diag), ("exp_avg_sq", exp_avg_sq)):
+        if t is not None:
+            _cuda(t, name)
+            if t.numel() != d_out * d_in:
+                raise ValueError(f"{name} has {t.numel()} elements, layer has {d_out * d_in}")
+    diag = None if diag is None else _contig(diag.to(torch.float32))
+    exp_avg_sq = None if exp_avg_sq is None else _contig(exp_avg_sq.to(torch.float32))
+    if out is None or out.numel() * out.element_size() < n * 16:
+        out = torch.empty(n * 4, dtype=torch.int32, device=packed.device)
+    _lib.check(_lib.load().opus_build_sketch_table(_ptr(packed), _ptr(diag), _ptr(exp_avg_sq), float(eps), int(d_out),
+                                                  int(d_in), _ptr(out), n, _stream(packed)),
+               "opus_build_sketch_table")
+    return out
+
+
+# --------------------------------------------------------------------- stage 3
+def split_bf16(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    _cuda(x, "x")
+    x = _contig(x.to(torch.float32))
+    hi = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    lo = torch.empty_like(hi)
+    _lib.check(_lib.load().opus_split_bf16(_ptr(x), x.numel(), _ptr(hi), _ptr(lo), _stream(x)), "opus_split_bf16")
+    return hi, lo
+
+
+def _as3d(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() == 2:
+        return t.unsqueeze(0)
+    if t.dim() != 3:
+        raise ValueError(f"Unexpected {name} shape: {tuple(t.shape)}")
+    return t
+
+
+def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int, rows_div: int = 1,
+                out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """phi[b // rows_div] (+)= CountSketch(w o (dLdZ_b^T a_b)) for every candidate b.
+
+    dLdZ [B, T, d_out] and a [B, T, d_in] in bf16 (tensor cores directly) or
+    f32 (split into bf16 hi/lo; hi*hi + hi*lo + lo*hi accumulated).
+    """
+    _cuda(dLdZ, "dLdZ")
+    _cuda(a, "a")
+    if dLdZ.dim() != 3 or a.dim() != 3 or dLdZ.shape[:2] != a.shape[:2]:
+        raise ValueError(f"Unexpected dLdZ/a shapes: {tuple(dLdZ.shape)}, {tuple(a.shape)}")
+    B, T, d_out = dLdZ.shape
+    d_in = a.shape[2]
+    rows = 0 if B == 0 else (B + rows_div - 1) // rows_div
+    if out is None:
+        out = torch.empty(rows, k, dtype=torch.float32, device=dLdZ.device)
+        accumulate = False
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < rows * k:
+        raise ValueError("out must be a contiguous float32 tensor of at least [rows, k]")
+    n_entries = table.numel() * table.element_size() // 16
+    lib = _lib.load()
+
+    def launch(g: torch.Tensor, x: torch.Tensor, acc: bool) -> None:
+        _lib.check(lib.opus_sketch_gemm(_ptr(g), _ptr(x), _lib.DTYPE_BF16, B, T, d_out, d_in, _ptr(table), n_entries,
+                                        int(k), int(rows_div), _ptr(out), int(acc), _stream(g)),
+                   "opus_sketch_gemm")
+
+    if dLdZ.dtype == torch.bfloat16 and a.dtype == torch.bfloat16:
+        launch(_contig(dLdZ), _contig(a), accumulate)
+    else:
+        g_hi, g_lo = split_bf16(dLdZ)
+        a_hi, a_lo = split_bf16(a)
+        launch(g_hi, a_hi, accumulate)
+        launch(g_hi, a_lo, True)
+        launch(g_lo, a_hi, True)
+    return out
+
+
+def sketch_dense(w: torch.Tensor, packed: torch.Tensor, d_out: int, d_in: int, k: int, transposed: bool = False,
+                 diag: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 accumulate: bool = False) -> torch.Tensor:
+    """sketch[h] += s * diag * W for a dense [d_out, d_in] (or [d_in, d_out] if transposed) matrix."""
+    _cuda(w, "w")
+    _cuda(packed, "packed")
+    if w.numel() != d_out * d_in:
+        raise ValueError(f"w has {w.numel()} elements, expected {d_out * d_in}")
+    w = _contig(w.to(torch.float32))
+    diag = None if diag is None else _contig(diag.to(torch.float32))
+    if out is None:
+        out = torch.empty(k, dtype=torch.float32, device=w.device)
+        accumulate = False
+    _lib.check(_lib.load().opus_sketch_dense(_ptr(w), int(bool(transposed)), _ptr(packed), _ptr(diag), int(d_out),
+                                            int(d_in), int(k), _ptr(out), int(accumulate), _stream(w)),
+               "opus_sketch_dense")
+    return out
+
+
+# --------------------------------------------------------------------- stage 2
+def desketch(tau: torch.Tensor, packed: torch.Tensor, d_out: int, d_in: int, scale: float = 1.0,
+             diag: torch.Tensor | None = None, exp_avg_sq: torch.Tensor | None = None,
+             eps: float = 1e-8) -> torch.Tensor:
+    """Dense target v = scale * D * s * tau[h] as a bf16 (hi, lo) pair [2, d_out, d_in]."""
+    _cuda(tau, "tau")
+    tau = _contig(tau.to(torch.float32))
+    diag = None if diag is None else _contig(diag.to(torch.float32))
+    exp_avg_sq = None if exp_avg_sq is None else _contig(exp_avg_sq.to(torch.float32))
+    out = torch.empty(2, d_out, d_in, dtype=torch.bfloat16, device=tau.device)
+    _lib.check(_lib.load().opus_desketch(_ptr(tau), _ptr(packed), _ptr(diag), _ptr(exp_avg_sq), float(eps), int(d_out),
+                                        int(d_in), tau.numel(), float(scale), _ptr(out), _stream(tau)),
+               "opus_desketch")
+    return out
+
+
+def dense_target_pair(v: torch.Tensor) -> torch.Tensor:
+    """f32 [d_out, d_in] target -> bf16 (hi, lo) pair [2, d_out, d_in] for ghost_score."""
+    hi, lo = split_bf16(v)
+    return torch.stack([hi, lo])
+
+
+def ghost_score(a: torch.Tensor, dLdZ: torch.Tensor, v_pair: torch.Tensor, alpha: float = 1.0,
+                out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """score[b] (+)= alpha * <dLdZ_b^T a_b, v> without forming per-sample gradients."""
+    _cuda(a, "a")
+    _cuda(dLdZ, "dLdZ")
+    if a.dim() != 3 or dLdZ.dim() != 3 or a.shape[:2] != dLdZ.shape[:2]:
+        raise ValueError(f"Unexpected a/dLdZ shapes: {tuple(a.shape)}, {tuple(dLdZ.shape)}")
+    B, T, d_in = a.shape
+    d_out = dLdZ.shape[2]
+    if v_pair.shape != (2, d_out, d_in) or v_pair.dtype != torch.bfloat16:
+        raise ValueError(f"v_pair must be bf16 [2, {d_out}, {d_in}], got {v_pair.dtype} {tuple(v_pair.shape)}")
+    if out is None:
+        out = torch.empty(B, dtype=torch.float32, device=a.device)
+        accumulate = False
+    lib = _lib.load()
+    v_pair = _contig(v_pair)
+
+    def launch(x: torch.Tensor, g: torch.Tensor, acc: bool) -> None:
+        _lib.check(lib.opus_ghost_score(_ptr(x), _ptr(g), _lib.DTYPE_BF16, B, T, d_in, d_out, _ptr(v_pair),
+                                        float(alpha), _ptr(out), int(acc), _stream(x)), "opus_ghost_score")
+
+    if a.dtype == torch.bfloat16 and dLdZ.dtype == torch.bfloat16:
+        launch(_contig(a), _contig(dLdZ), accumulate)
+    else:
+        a_hi, a_lo = split_bf16(a)
+        g_hi, g_lo = split_bf16(dLdZ)
+        launch(a_hi, g_hi, accumulate)
+        launch(a_lo, g_hi, True)
+        launch(a_hi, g_lo, True)
+    return out
+
+
+# --------------------------------------------------------------------- dots
+def sketch_dot(phi: torch.Tensor, tau: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None,
+               accumulate: bool = False) -> torch.Tensor:
+    _cuda(phi, "phi")
+    phi, tau = _contig(phi), _contig(tau)
+    B, k = phi.shape
+    if tau.numel() != k:
+        raise ValueError("tau length must equal the sketch dimension")
+    if out is None:
+        out = torch.empty(B, dtype=torch.float32, device=phi.device)
+        accumulate = False
+    _lib.check(_lib.load().opus_sketch_dot(_ptr(phi), _ptr(tau), B, k, float(alpha), _ptr(out), int(accumulate),
+                                          _stream(phi)), "opus_sketch_dot")
+    return out
+
+
+def sketch_gram(phi_a: torch.Tensor, phi_b: torch.Tensor | None = None, alpha: float = 1.0,
+                out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    _cuda(phi_a, "phi_a")
+    phi_a = _contig(phi_a)
+    phi_b = phi_a if phi_b is None else _contig(phi_b)
+    ra, k = phi_a.shape
+    rb = phi_b.shape[0]
+    if phi_b.shape[1] != k:
+        raise ValueError("sketch dimensions differ")
+    if out is None:
+        out = torch.empty(ra, rb, dtype=torch.float32, device=phi_a.device)
+        accumulate = False
+    _lib.check(_lib.load().opus_sketch_gram(_ptr(phi_a), ra, _ptr(phi_b), rb, k, float(alpha), _ptr(out),
+                                           int(accumulate), _stream(phi_a)), "opus_sketch_gram")
+    return out
+
+
+# --------------------------------------------------------------------- stage 5
+def boltzmann_select(scores: torch.Tensor, sim: torch.Tensor, n_select: int, temperature: float,
+                     uniforms: torch.Tensor) -> torch.Tensor:
+    """Stochastic greedy selection on the device; uniforms: float64 [n_select] (one per draw)."""
+    _cuda(scores, "scores")
+    scores = _contig(scores.to(torch.float32).reshape(-1))
+    n = scores.numel()
+    sim = _contig(sim.to(torch.float32))
+    if sim.shape != (n, n):
+        raise ValueError(f"interaction matrix must be [{n}, {n}]")
+    if n_select > n:
+        raise ValueError(f"cannot select {n_select} of {n} candidates")
+    uniforms = _contig(uniforms.to(device=scores.device, dtype=torch.float64).reshape(-1))
+    if uniforms.numel() < n_select:
+        raise ValueError("need one uniform per draw")
+    out = torch.empty(n_select, dtype=torch.int64, device=scores.device)
+    _lib.check(_lib.load().opus_boltzmann_select(_ptr(scores), _ptr(sim), n, int(n_select), float(temperature),
+                                                _ptr(uniforms), _ptr(out), _stream(scores)), "opus_boltzmann_select")
+    return out
+
+
+def greedy_select(scores: torch.Tensor, sim: torch.Tensor, n_select: int) -> torch.Tensor:
+    _cuda(scores, "scores")
+    scores = _contig(scores.to(torch.float32).reshape(-1))
+    n = scores.numel()
+    sim = _contig(sim.to(torch.float32))
+    if sim.shape != (n, n):
+        raise ValueError(f"interaction matrix must be [{n}, {n}]")
+    out = torch.empty(n_select, dtype=torch.int64, device=scores.device)
+    _lib.check(_lib.load().opus_greedy_select(_ptr(scores), _ptr(sim), n, int(n_select), _ptr(out), _stream(scores)),
+               "opus_greedy_select")
+    return out

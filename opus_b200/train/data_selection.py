@@ -1,0 +1,665 @@
+"""OPUS scoring and selection (drop-in for OPUS/train/data_selection.py).
+
+Same public functions, arguments, return types and exceptions as the
+reference module; the numeric work runs in the sm_100a kernels of
+libopus_b200.so:
+
+  stage 1  capture        GCLinear stashes (A, Z); autograd gives G = dL/dZ
+  stage 2  ghost scores   ops.ghost_score         (projection off)
+  stage 3  CountSketch    ops.sketch_gemm         (fused per-sample GEMM + scatter)
+  stage 4  precondition   folded into the sketch table (AdamW diagonal) or
+                          applied to G (Muon S) / to the dense target
+  stage 5  selection      ops.boltzmann_select / ops.greedy_select
+
+Scores use one sketch pass per layer for the candidates: the reference
+sketches the candidates twice (once for the scores, data_selection.py:509,
+once for the similarity, :572) with identical inputs, and averages the
+proxy-side dot products, which equals one dot with the summed proxy sketch
+(CountSketch is linear), so the proxy batch is reduced to one sketch row.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .. import ops
+from .random_projection import GradientProjector
+
+_RANDOM_PROJECTION_AVAILABLE = True
+
+# Global projector instance (data_selection.py:27-28)
+_GLOBAL_PROJECTOR: GradientProjector | None = None
+
+
+def initialize_projector(sketch_dim: int = 16384, seed: int = 42, device: str = "cuda", enabled: bool = True):
+    """Create (or disable) the global CountSketch projector (data_selection.py:31-68)."""
+    global _GLOBAL_PROJECTOR
+    if enabled and sketch_dim > 0:
+        _GLOBAL_PROJECTOR = GradientProjector(sketch_dim=sketch_dim, seed=seed, device=device, enabled=True)
+        max_grad_dim = 10_240_000  # largest GPT-2 XL layer (MLP), as the reference reports
+        print(f"[Random Projection] Initialized: dim={sketch_dim}, compression≈{max_grad_dim / sketch_dim:.0f}x, "
+              f"seed={seed}")
+    else:
+        _GLOBAL_PROJECTOR = None
+        print("[Random Projection] Disabled (using full-dimensional gradients)")
+
+
+def get_projector():
+    """The global projector, or None when projection is disabled (data_selection.py:71-73)."""
+    return _GLOBAL_PROJECTOR
+
+
+_GBG_CALL_ID = 0
+
+
+def make_window_generator(step: int, rank: int, base_seed: int = 12345, device: str = "cuda"):
+    """Deterministic generator for window starts (data_selection.py:79-83)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(base_seed + step * 100003 + rank * 1009)
+    return g
+
+
+def _as_opt_list(optimizer_or_list):
+    return list(optimizer_or_list) if isinstance(optimizer_or_list, (list, tuple)) else [optimizer_or_list]
+
+
+def _build_param2opt_map(optimizers):
+    """param -> owning optimizer (data_selection.py:93-100); later optimizers win."""
+    return {p: opt for opt in optimizers for g in opt.param_groups for p in g["params"]}
+
+
+def _group_kind(group):
+    """adamw if the group has betas, muon if it has momentum (data_selection.py:103-109)."""
+    if "betas" in group:
+        return "adamw"
+    if "momentum" in group:
+        return "muon"
+    return "unknown"
+
+
+def _get_rank_safe():
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        return torch.distributed.get_rank()
+    return 0
+
+
+def _copy_batch_dict(batch):
+    return dict(batch.items())
+
+
+def _next_batch(loader):
+    try:
+        return next(loader._it)
+    except StopIteration:
+        loader._it = iter(loader)
+        return next(loader._it)
+
+
+def _sample_proxy_batch_for_step(validation_loader):
+    """One proxy batch per selection round (data_selection.py:124-157).
+
+    A batch pinned in ``_fixed_batch`` wins; otherwise ``_proxy_mode`` "fixed"
+    reuses the first batch drawn and "refresh" draws a new one every
+    ``_proxy_refresh_interval`` calls.
+    """
+    fixed = getattr(validation_loader, "_fixed_batch", None)
+    if fixed is not None:
+        return _copy_batch_dict(fixed)
+    if not hasattr(validation_loader, "_it"):
+        validation_loader._it = iter(validation_loader)
+    mode = getattr(validation_loader, "_proxy_mode", "refresh")
+    interval = max(1, int(getattr(validation_loader, "_proxy_refresh_interval", 1)))
+    cached = getattr(validation_loader, "_cached_proxy_batch", None)
+    calls = int(getattr(validation_loader, "_proxy_call_count", 0))
+    if mode == "fixed":
+        if cached is None:
+            cached = _next_batch(validation_loader)
+            validation_loader._cached_proxy_batch = cached
+        return _copy_batch_dict(cached)
+    if cached is None or calls % interval == 0:
+        cached = _next_batch(validation_loader)
+        validation_loader._cached_proxy_batch = cached
+    validation_loader._proxy_call_count = calls + 1
+    return _copy_batch_dict(cached)
+
+
+def _get_step_from_optimizer(optimizer):
+    """Largest state['step'] over the optimizer's params, at least 1 (data_selection.py:160-168)."""
+    t = 1
+    for g in optimizer.param_groups:
+        for p in g["params"]:
+            st = optimizer.state.get(p, None)
+            if st is not None and "step" in st:
+                t = max(t, int(st["step"]))
+    return t
+
+
+def _find_group_for_param(optimizer, p):
+    """Param group holding p by identity, else the first group (data_selection.py:171-179)."""
+    for g in optimizer.param_groups:
+        if any(gp is p for gp in g.get("params", ())):
+            return g
+    return optimizer.param_groups[0]
+
+
+def global_C_t(optimizer, p):
+    """AdamW scalar lr*(1-b1)*sqrt(1-b2^t)/(1-b1^t) as a float32 tensor (data_selection.py:182-195)."""
+    g = _find_group_for_param(optimizer, p)
+    beta1, beta2 = g["betas"]
+    t = _get_step_from_optimizer(optimizer)
+    num = max(1e-16, 1.0 - beta2 ** t) ** 0.5
+    den = max(1e-16, 1.0 - beta1 ** t)
+    return torch.tensor(g["lr"] * (1.0 - beta1) * num / den, dtype=torch.float32, device=p.device)
+
+
+def _inv_rms_scalar_for_param(p, group, state):
+    """Mean of the AdamW diagonal (data_selection.py:198-205)."""
+    v = state.get("exp_avg_sq", None)
+    if v is None:
+        return torch.tensor(1.0, dtype=torch.float32, device=p.device)
+    return (v.sqrt() + group.get("eps", 1e-8)).reciprocal().to(dtype=torch.float32).mean()
+
+
+def _inv_rms_tensor_for_param(group, state):
+    """AdamW diagonal 1/(sqrt(v)+eps) in float32, or None (data_selection.py:208-214)."""
+    v = state.get("exp_avg_sq", None)
+    if v is None:
+        return None
+    return (v.sqrt() + group.get("eps", 1e-8)).reciprocal().to(dtype=torch.float32)
+
+
+def global_C_t_muon(optimizer, p):
+    """Muon scalar eff_lr * (1 - momentum^2) (data_selection.py:217-225)."""
+    g = _find_group_for_param(optimizer, p)
+    lr = g["lr"] * max(1, p.size(-2) / p.size(-1)) ** 0.5 * getattr(p, "lr_mul", 1.0)
+    mu = g.get("momentum", 0.0)
+    return torch.tensor(lr * (1.0 - mu ** 2), dtype=torch.float32, device=p.device)
+
+
+_MUON_COEFFS = (3.4445, -4.7750, 2.0315)
+
+
+def _get_muon_S_matrix(p, optimizer):
+    """S = a I + b A + c A^2 with A = m~ m~^T, m~ = m/||m|| in bf16 (data_selection.py:228-252).
+
+    Identity when the parameter has no momentum buffer or ||m|| < 1e-7.
+    """
+    state = optimizer.state.get(p, None)
+    n = p.shape[0]
+    eye = torch.eye(n, dtype=torch.bfloat16, device=p.device)
+    if state is None or "momentum_buffer" not in state:
+        return eye
+    m = state["momentum_buffer"].to(dtype=torch.bfloat16)
+    norm = torch.norm(m)
+    if norm < 1e-7:
+        return eye
+    mt = m / norm
+    A = mt @ mt.T
+    a, b, c = _MUON_COEFFS
+    return a * eye + b * A + c * (A @ A)
+
+
+def weighted_grad_dotprod(A1, B1, A2, B2, diagonal_weight: torch.Tensor, weight_rhs: bool = False,
+                          chunk_rows: int = 32) -> torch.Tensor:
+    """<D o G1_i, G2_j> (or <D o G1_i, D o G2_j>) for all pairs (data_selection.py:255-292).
+
+    A* are dL/dZ factors [B, D_out] / [B, T, D_out], B* activations.  The
+    per-sample gradients are formed once per side by the sketch kernel with an
+    identity table (bucket = flat index), then contracted with one Gram pass.
+    """
+    if diagonal_weight.ndim != 2:
+        raise ValueError(f"Expected diagonal_weight with shape [D_out, D_in], got {tuple(diagonal_weight.shape)}")
+    if A1.dim() != B1.dim() or A1.dim() not in (2, 3):
+        raise ValueError(f"Unexpected input shape: {A1.size()}, grad_output shape: {B1.size()}")
+    D = diagonal_weight.to(device=A1.device, dtype=torch.float32)
+    lhs = _materialize(A1, B1, D)
+    rhs = _materialize(A2, B2, D if weight_rhs else None)
+    return ops.sketch_gram(lhs, rhs)
+
+
+def _identity_projector(numel: int) -> GradientProjector:
+    return _IdentityTables(numel)
+
+
+class _IdentityTables(GradientProjector):
+    """Projector whose bucket is the flat weight index and sign +1 (exact materialisation)."""
+
+    def __init__(self, numel: int):
+        super().__init__(sketch_dim=numel, seed=0, device="cpu", enabled=True)
+
+    def _generate(self, param_numel: int, param_id: int):
+        h = torch.arange(param_numel, dtype=torch.long)
+        return h, torch.ones(param_numel, dtype=torch.float32)
+
+
+def _materialize(dLdZ, a, diag=None):
+    """Per-sample gradients D o (dLdZ_b^T a_b) flattened to [B, D_out*D_in] in f32."""
+    if dLdZ.dim() == 2:
+        dLdZ, a = dLdZ.unsqueeze(1), a.unsqueeze(1)
+    d_out, d_in = dLdZ.shape[2], a.shape[2]
+    proj = _identity_projector(d_out * d_in)
+    return proj.sketch(dLdZ, a, 0, diag=diag)
+
+
+def find_GClayers(model):
+    """All GCLinear / GCLoRALinear modules of the model (data_selection.py:295-299)."""
+    from ..layers.linear import GCLinear
+    from ..layers.lora_layers import GCLoRALinear
+    return [m for m in model.modules() if isinstance(m, (GCLinear, GCLoRALinear))]
+
+
+def _random_windows(x, win_len, align_to=128, g=None):
+    """Random aligned windows of length win_len (data_selection.py:302-315)."""
+    N, T = x.size()
+    if T <= win_len:
+        idx = torch.arange(min(T, win_len), device=x.device).expand(N, -1)
+        return x[:, :win_len], idx
+    max_start = T - win_len
+    starts = torch.randint(0, max_start + 1, (N,), device=x.device, generator=g)
+    if align_to is not None and align_to > 1:
+        starts = torch.clamp((starts // align_to) * align_to, 0, max_start)
+    idx = starts[:, None] + torch.arange(win_len, device=x.device)[None, :]
+    return x.gather(1, idx), idx
+
+
+# ----------------------------------------------------------------- scoring core
+class _Pair:
+    __slots__ = ("p", "g_t", "a_t", "g_v", "a_v")
+
+    def __init__(self, p, g_t, a_t, g_v, a_v):
+        self.p, self.g_t, self.a_t, self.g_v, self.a_v = p, g_t, a_t, g_v, a_v
+
+
+def capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len=512):
+    """Stage 1: (dL/dZ, A) of every captured layer for candidates and proxies.
+
+    One forward over the candidates and the round's proxy batch with dropout
+    off, per-sample mean next-token cross-entropy (labels -100 ignored),
+    dL/dZ by autograd to each layer's stored pre-activation, then each
+    layer's factorisation split into candidate / proxy halves
+    (data_selection.py:345-445).  Returns (pairs, n_candidates, n_proxies).
+    """
+    batch_val = _sample_proxy_batch_for_step(validation_loader)
+    val_bs = batch_val["input_ids"].shape[0]
+    train_bs = batch_train["input_ids"].shape[0]
+
+    L = min(batch_train["input_ids"].shape[1], batch_val["input_ids"].shape[1])
+    if score_len is not None:
+        L = min(L, score_len)
+    for bd in (batch_train, batch_val):
+        for key in ("input_ids", "attention_mask", "labels"):
+            bd[key] = bd[key][:, :L]
+
+    labels = torch.cat([batch_train["labels"], batch_val["labels"]], dim=0)
+    inputs = {k: torch.cat([batch_train[k], batch_val[k]], dim=0) for k in batch_train.keys() if k != "labels"}
+    del batch_train, batch_val
+    was_training = model.training
+    model.eval()
+    logits = model(input_seq=inputs["input_ids"], target_seq=None, sliding_window_num_blocks=None)
+    if was_training:
+        model.train()
+
+    shift_logits = logits[..., :-1, :].contiguous()
+    shift_labels = labels[..., 1:].contiguous()
+    tok_loss = torch.nn.functional.cross_entropy(shift_logits.view(-1, shift_logits.size(-1)), shift_labels.view(-1),
+                                                 reduction="none", ignore_index=-100).view(shift_labels.size())
+    mask = (shift_labels != -100).float()
+    loss = (tok_loss * mask).sum(dim=-1) / mask.sum(dim=-1)
+
+    raw = [layer.pre_activation for layer in trainable_layers]
+    keep = [i for i, z in enumerate(raw) if isinstance(z, torch.Tensor) and z.requires_grad and z.grad_fn is not None]
+    if not keep:
+        raise RuntimeError("No usable pre_activations captured. Check GC hooks / forward path.")
+    layers_kept = [trainable_layers[i] for i in keep]
+    z_grads = torch.autograd.grad(loss.mean(), [raw[i] for i in keep], retain_graph=False, allow_unused=True)
+    del logits, shift_logits, tok_loss
+
+    pairs: list[_Pair] = []
+    for layer, zg in zip(layers_kept, z_grads):
+        if zg is None:
+            continue
+        parts = layer.pe_grad_gradcomp(zg, per_sample=True)
+        if isinstance(parts, tuple) and len(parts) == 2 and all(isinstance(x, torch.Tensor) for x in parts):
+            parts = [parts]
+        else:
+            parts = list(parts)
+        lparams = [getattr(layer, n) for n in ("lora_A", "lora_B") if hasattr(layer, n)]
+        for i, (g, a) in enumerate(parts):
+            p = lparams[i] if i < len(lparams) else getattr(layer, "weight", None)
+            g, a = g.detach(), a.detach()
+            pairs.append(_Pair(p, g[:train_bs], a[:train_bs], g[train_bs:], a[train_bs:]))
+    return pairs, train_bs, val_bs
+
+
+class LayerPlan:
+    """Stage-4 inputs of one (dL/dZ, A) pair: what the kernels apply.
+
+    g_t is the candidate dL/dZ after the Muon transform (if any); c is the
+    float32 product C_t * layer_scale; exp_avg_sq / eps give the AdamW
+    diagonal folded into the candidate sketch table.
+    """
+    __slots__ = ("pid", "kind", "g_t", "a_t", "g_v", "a_v", "c", "exp_avg_sq", "eps")
+
+    def __init__(self, pid, kind, g_t, a_t, g_v, a_v, c, exp_avg_sq, eps):
+        self.pid, self.kind, self.g_t, self.a_t, self.g_v, self.a_v = pid, kind, g_t, a_t, g_v, a_v
+        self.c, self.exp_avg_sq, self.eps = c, exp_avg_sq, eps
+
+
+def plan_layers(pairs, optimizer, preconditioner, device):
+    """Preconditioner per pair, as data_selection.py:447-506 and :545-569 resolve it.
+
+    'auto' picks per param group (betas -> adamw, momentum -> muon); Muon's S
+    transforms the candidate dL/dZ (the proxy side stays untransformed);
+    AdamW contributes C_t and its diagonal 1/(sqrt(v)+eps); a preconditioned
+    matrix parameter also gets layer_scale = 1/sqrt(d_out d_in).
+    """
+    param2opt = _build_param2opt_map(_as_opt_list(optimizer))
+    auto_mode = preconditioner == "auto"
+    S_map, muon_scale, adamw = {}, {}, {}
+    for p in {pr.p for pr in pairs if pr.p is not None}:
+        opt_p = param2opt.get(p, None)
+        if opt_p is None:
+            continue
+        group = _find_group_for_param(opt_p, p)
+        kind = _group_kind(group) if auto_mode else preconditioner
+        if kind == "muon":
+            if p in opt_p.state:
+                S_map[p] = _get_muon_S_matrix(p, opt_p)
+            muon_scale[p] = global_C_t_muon(opt_p, p).to(dtype=torch.float32)
+        elif kind == "adamw":
+            adamw[p] = (global_C_t(opt_p, p).to(dtype=torch.float32), group, opt_p.state.get(p, {}))
+
+    plans = []
+    for pid, pr in enumerate(pairs):
+        p, g_t = pr.p, pr.g_t
+        scale = torch.tensor(1.0)
+        layer_scale = 1.0
+        v_sq, eps = None, 1e-8
+        eff = "sgd"
+        if p is not None:
+            opt_p = param2opt.get(p, None)
+            if opt_p is not None:
+                eff = _group_kind(_find_group_for_param(opt_p, p)) if auto_mode else preconditioner
+                if eff == "muon" and p in S_map:
+                    g_t = (g_t.float() @ S_map[p].to(g_t.device).float()).to(g_t.dtype)
+                    scale = muon_scale[p]
+                elif eff == "adamw" and p in adamw:
+                    scale, group_p, state_p = adamw[p]
+                    if state_p.get("exp_avg_sq", None) is not None:
+                        v_sq, eps = state_p["exp_avg_sq"], group_p.get("eps", 1e-8)
+                if eff != "sgd" and p.ndim >= 2:
+                    layer_scale = 1.0 / float((p.shape[-1] * p.shape[-2]) ** 0.5)
+        c = float((scale.detach().cpu().to(torch.float32) * layer_scale).item())
+        if v_sq is not None:
+            v_sq = v_sq.detach().to(device=device, dtype=torch.float32)
+        plans.append(LayerPlan(pid, eff, g_t, pr.a_t, pr.g_v, pr.a_v, c, v_sq, eps))
+    return plans
+
+
+def _score_and_similarity(model, device, batch_train, validation_loader, optimizer, trainable_layers,
+                          preconditioner="adamw", score_len=512, per_val=False, with_similarity=True):
+    """Device tensors (score [B] or [B, n], sim [B, B] or None) for one window."""
+    pairs, train_bs, val_bs = capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len)
+    plans = plan_layers(pairs, optimizer, preconditioner, device)
+    del pairs
+    projector = get_projector()
+    use_projection = projector is not None and projector.enabled
+    score = torch.zeros((train_bs, val_bs) if per_val else (train_bs,), device=device, dtype=torch.float32)
+    sim = torch.zeros((train_bs, train_bs), device=device, dtype=torch.float32) if with_similarity else None
+
+    for pl in plans:
+        if pl.g_t.dim() == 2:
+            g_t, a_t, g_v, a_v = pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1), pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)
+        else:
+            g_t, a_t, g_v, a_v = pl.g_t, pl.a_t, pl.g_v, pl.a_v
+        c = pl.c
+        if use_projection:
+            # stage 3 + 4: one fused sketch pass for the candidates (AdamW
+            # diagonal in the table), one for the proxy batch summed to a row
+            phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
+            if per_val:
+                phi_v = projector.sketch(g_v, a_v, pl.pid)
+                ops.sketch_gram(phi_t, phi_v, alpha=c, out=score, accumulate=True)
+            elif val_bs > 0:
+                tau = projector.sketch(g_v, a_v, pl.pid, rows_div=val_bs)
+                ops.sketch_dot(phi_t, tau[0], alpha=c / val_bs, out=score, accumulate=True)
+            if sim is not None:
+                ops.sketch_gram(phi_t, alpha=c * c, out=sim, accumulate=True)
+            del phi_t
+        else:
+            _score_dense(g_t, a_t, g_v, a_v, pl.exp_avg_sq, pl.eps, c, per_val, score)
+            if sim is not None:
+                d_out, d_in = g_t.shape[2], a_t.shape[2]
+                diag = None if pl.exp_avg_sq is None else ops_inv_rms(pl.exp_avg_sq, pl.eps).reshape(d_out, d_in)
+                ops.sketch_gram(_materialize(g_t, a_t, diag), alpha=c * c, out=sim, accumulate=True)
+    return score, sim
+
+
+def ops_inv_rms(v: torch.Tensor, eps: float) -> torch.Tensor:
+    """1/(sqrt(v)+eps) in float32 (the AdamW diagonal, data_selection.py:208-214)."""
+    return (v.float().sqrt() + eps).reciprocal()
+
+
+def _score_dense(g_t, a_t, g_v, a_v, v_sq, eps, c, per_val, score):
+    """Projection-off scores via the ghost kernel against the dense proxy target.
+
+    score_b += c * <D o G_b, mean_j G_vj> (per_val: one column per proxy j);
+    the proxy gradient sum G_v^T A_v over all proxy tokens is a plain GEMM.
+    """
+    d_out, d_in = g_t.shape[2], a_t.shape[2]
+    n = g_v.shape[0]
+    if n == 0:
+        return
+    diag = None if v_sq is None else ops_inv_rms(v_sq, eps).reshape(d_out, d_in)
+    gt_p, at_p = _pad8(g_t), _pad8(a_t)
+    do_p, di_p = gt_p.shape[2], at_p.shape[2]
+
+    def target(gv, av):
+        w = gv.float().reshape(-1, d_out).T @ av.float().reshape(-1, d_in)
+        if diag is not None:
+            w = w * diag
+        if (do_p, di_p) != (d_out, d_in):
+            w = torch.nn.functional.pad(w, (0, di_p - d_in, 0, do_p - d_out))
+        return ops.dense_target_pair(w)
+
+    if per_val:
+        for j in range(n):
+            col = ops.ghost_score(at_p, gt_p, target(g_v[j:j + 1], a_v[j:j + 1]), alpha=c)
+            score[:, j] += col
+    else:
+        ops.ghost_score(at_p, gt_p, target(g_v, a_v), alpha=c / n, out=score, accumulate=True)
+
+
+def _pad8(x):
+    d = x.shape[-1]
+    p = (d + 7) // 8 * 8
+    return x if p == d else torch.nn.functional.pad(x, (0, p - d))
+
+
+def compute_GradProd_GC_per_iter(model, device, batch_train, validation_loader, optimizer, trainable_layers,
+                                 preconditioner="adamw", score_len=512, per_val=False,
+                                 return_tracin_and_similarity=True):
+    """OPUS step-wise scores and candidate similarity (data_selection.py:318-594).
+
+    Returns NumPy float32 (scores [B] or [B, n], similarity [B, B] or None),
+    as the reference does.
+    """
+    score, sim = _score_and_similarity(model, device, batch_train, validation_loader, optimizer, trainable_layers,
+                                       preconditioner=preconditioner, score_len=score_len, per_val=per_val,
+                                       with_similarity=return_tracin_and_similarity)
+    score_np = score.detach().cpu().numpy()
+    if return_tracin_and_similarity:
+        return score_np, sim.detach().cpu().numpy()
+    return score_np, None
+
+
+def grad_dotprod(A1, B1, A2, B2) -> torch.Tensor:
+    """<G1_i, G2_j> for all pairs (data_selection.py:597-604)."""
+    if A1.dim() == 2 and B1.dim() == 2:
+        return grad_dotprod_non_sequential(A1, B1, A2, B2)
+    if A1.dim() == 3 and B1.dim() == 3:
+        return grad_dotprod_sequential(A1, B1, A2, B2)
+    raise ValueError(f"Unexpected input shape: {A1.size()}, grad_output shape: {B1.size()}")
+
+
+def grad_dotprod_non_sequential(A1, B1, A2, B2):
+    """(A1 A2^T) * (B1 B2^T) for single-token samples (data_selection.py:607-611)."""
+    return torch.matmul(A1, A2.T) * torch.matmul(B1, B2.T)
+
+
+def grad_dotprod_sequential(A1, B1, A2, B2, chunk_size=1024):
+    """Flattened per-sample gradient Gram (data_selection.py:614-619), argument order as the reference."""
+    lhs = _materialize(A1, B1)
+    rhs = _materialize(A2, B2)
+    return ops.sketch_gram(lhs, rhs)
+
+
+# ----------------------------------------------------------------- selection
+def _to_device_pair(scores, interaction_matrix):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    s = torch.as_tensor(np.asarray(scores, dtype=np.float32) if not torch.is_tensor(scores) else scores)
+    m = torch.as_tensor(np.asarray(interaction_matrix, dtype=np.float32)
+                        if not torch.is_tensor(interaction_matrix) else interaction_matrix)
+    return s.to(dev, torch.float32), m.to(dev, torch.float32)
+
+
+def greedy_selection(scores, interaction_matrix, K):
+    """Greedy pick with interaction penalty (data_selection.py:622-638), on the device.
+
+    Returns a list of K np.int64 indices like the reference.
+    """
+    s, m = _to_device_pair(scores, interaction_matrix)
+    idx = ops.greedy_select(s, m, int(K))
+    return [np.int64(i) for i in idx.cpu().numpy()]
+
+
+def stochastic_greedy_selection(scores, interaction_matrix, K, temperature=1.0):
+    """Boltzmann sampling of K with interaction penalty (data_selection.py:641-675), on the device.
+
+    Draws one double per pick from NumPy's global RNG, the stream
+    np.random.choice consumes in the reference, so a seeded NumPy state gives
+    the reference's indices.
+    """
+    s, m = _to_device_pair(scores, interaction_matrix)
+    K = int(K)
+    if K > s.numel():
+        raise ValueError("zero-size array to reduction operation maximum which has no identity")
+    u = torch.from_numpy(np.random.random_sample(K).astype(np.float64))
+    idx = ops.boltzmann_select(s, m, K, float(temperature), u)
+    ops.check_device_error("stochastic_greedy_selection")
+    return [np.int64(i) for i in idx.cpu().numpy()]
+
+
+def _select_on_device(scores, sim, K, method, temperature):
+    if method == "greedy":
+        return ops.greedy_select(scores, sim, K)
+    if method == "stochastic":
+        if K > scores.numel():
+            raise ValueError("zero-size array to reduction operation maximum which has no identity")
+        u = torch.from_numpy(np.random.random_sample(K).astype(np.float64))
+        idx = ops.boltzmann_select(scores, sim, K, float(temperature), u)
+        ops.check_device_error("stochastic_greedy_selection")
+        return idx
+    raise ValueError(f"Unknown selection method: {method}")
+
+
+def get_batch_opus(model, buffer_seq, buffer_labels, proxy_seq, proxy_labels, optimizer, trainable_layers,
+                   validation_loader, selection_ratio, seq_len, selection_strategy="opus", selection_method="greedy",
+                   temperature=1.5, score_len=512, preconditioner="adamw", return_scores_only: bool = False,
+                   n_windows: int = 1):
+    """OPUS batch selection (data_selection.py:678-836).
+
+    Returns the selected indices (LongTensor on buffer_seq.device), or
+    (scores [N], interaction [N, N]) float32 tensors if return_scores_only.
+    """
+    device = buffer_seq.device
+    score_len = min(score_len, seq_len)
+    assert score_len % 128 == 0, "score_len must be multiple of 128 (FlexAttention BLOCK_SIZE)"
+
+    def to_batches(x, L):
+        if x.dim() == 1:
+            n = x.size(0) // L
+            if n == 0:
+                raise ValueError(f"Length insufficient: {x.size(0)} < {L}")
+            return x[: n * L].view(n, L)
+        if x.dim() == 2 and x.size(1) == L:
+            return x
+        raise ValueError(f"Expected [N,{L}] or [T], got {tuple(x.shape)}")
+
+    buffer_seq = to_batches(buffer_seq, seq_len)
+    buffer_labels = to_batches(buffer_labels, seq_len)
+    if proxy_seq is not None:
+        proxy_seq = to_batches(proxy_seq, seq_len)
+        proxy_labels = to_batches(proxy_labels, seq_len)
+    num_buf = buffer_seq.size(0)
+    num_to_select = max(1, int(num_buf * selection_ratio))
+
+    def model_loss_one(seq_1d, lab_1d, use_score_len=False):
+        L = score_len if use_score_len else seq_len
+        win_blocks = torch.tensor(L // 128, dtype=torch.int32, device=seq_1d.device)
+        return model(seq_1d[:L], lab_1d[:L], win_blocks)
+
+    if selection_strategy == "random":
+        return torch.randperm(num_buf, device=device)[:num_to_select]
+
+    if selection_strategy == "ppl":
+        mode = (selection_method or "high").lower()
+        with torch.no_grad():
+            losses = torch.stack([model_loss_one(buffer_seq[i], buffer_labels[i], use_score_len=True).detach()
+                                  for i in range(num_buf)])
+        if mode == "low":
+            return torch.topk(-losses, k=num_to_select, largest=True)[1]
+        if mode == "mid":
+            ql = torch.quantile(losses, torch.tensor(0.2, device=losses.device))
+            qh = torch.quantile(losses, torch.tensor(0.8, device=losses.device))
+            mask = (losses >= ql) & (losses <= qh)
+            mid_idx = torch.nonzero(mask, as_tuple=False).squeeze(-1)
+            if mid_idx.numel() >= num_to_select:
+                median = torch.quantile(losses, torch.tensor(0.5, device=losses.device))
+                order = torch.topk(-torch.abs(losses[mid_idx] - median), k=num_to_select, largest=True)[1]
+                return mid_idx[order]
+            remaining = num_to_select - mid_idx.numel()
+            fill_mask = ~mask
+            dist_all = torch.full_like(losses, float("inf"))
+            below, above = losses < ql, losses > qh
+            dist_all[below] = ql - losses[below]
+            dist_all[above] = losses[above] - qh
+            dist_all[~fill_mask] = float("inf")
+            fill_k = min(remaining, int(fill_mask.sum().item()))
+            fill_order = torch.topk(-dist_all, k=fill_k, largest=True)[1]
+            return torch.cat([mid_idx, fill_order.to(mid_idx.device)], dim=0)
+        return torch.topk(losses, k=num_to_select, largest=True)[1]
+
+    if selection_strategy == "opus":
+        global _GBG_CALL_ID
+        n_windows = max(1, int(n_windows))
+        scores = sim = None
+        pinned_here = False
+        if getattr(validation_loader, "_fixed_batch", None) is None:
+            validation_loader._fixed_batch = _sample_proxy_batch_for_step(validation_loader)
+            pinned_here = True
+        try:
+            for _ in range(n_windows):
+                gen = make_window_generator(step=_GBG_CALL_ID, rank=_get_rank_safe(), device=buffer_seq.device.type)
+                _GBG_CALL_ID += 1
+                win_inputs, idx = _random_windows(buffer_seq, score_len, align_to=128, g=gen)
+                batch_train = {"input_ids": win_inputs, "attention_mask": torch.ones_like(win_inputs),
+                               "labels": buffer_labels.gather(1, idx)}
+                w_scores, w_sim = _score_and_similarity(model, buffer_seq.device, batch_train, validation_loader,
+                                                        optimizer, trainable_layers, preconditioner=preconditioner,
+                                                        score_len=score_len, per_val=False, with_similarity=True)
+                if scores is None:
+                    scores, sim = w_scores, w_sim
+                else:
+                    scores += w_scores
+                    sim += w_sim
+        finally:
+            if pinned_here:
+                validation_loader._fixed_batch = None
+        scores /= n_windows
+        sim /= n_windows
+        if return_scores_only:
+            return scores.to(torch.float32), sim.to(torch.float32)
+        return _select_on_device(scores, sim, num_to_select, selection_method, temperature).to(buffer_seq.device)
+
+    raise ValueError(f"Unknown selection strategy: {selection_strategy}")

@@ -1,0 +1,201 @@
+"""Parity of the sm_100a kernels with the oracle (GPU)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import opus_oracle as orc
+from opus_b200 import ops
+from opus_b200.train.random_projection import GradientProjector
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def cuda_tables(numel, pid, k, seed=42):
+    """The reference's table recipe on the CUDA generator, plus the packed table."""
+    h, s = orc.hash_sign_tables(numel, pid, k, seed=seed, device=DEV)
+    packed = ops.pack_hash_sign(torch.from_numpy(h).to(DEV), torch.from_numpy(s).to(DEV), k)
+    return h, s, packed
+
+
+def rel_close(got, want, rtol, what=""):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    scale = max(np.abs(want).max(), 1e-30)
+    err = np.abs(got - want).max() / scale
+    assert err <= rtol, f"{what}: max |err| / max |ref| = {err:.3e} > {rtol}"
+
+
+def test_pack_bit_exact():
+    h, s, packed = cuda_tables(100_003, 7, 16384)
+    np.testing.assert_array_equal(packed.cpu().numpy().view(np.uint32), orc.pack_tables(h, s))
+
+
+def test_pack_rejects_out_of_range_bucket():
+    h = torch.tensor([0, 5, 16], dtype=torch.int64, device=DEV)
+    s = torch.tensor([1.0, -1.0, 1.0], device=DEV)
+    with pytest.raises(RuntimeError, match="0x201"):
+        ops.pack_hash_sign(h, s, 16)
+    # the device error word was cleared: a valid call succeeds afterwards
+    ops.pack_hash_sign(h, s, 17)
+
+
+def decode_table(table, d_out, d_in):
+    """Host decode of the tiled epilogue table back to [d_out, d_in] buckets and weights."""
+    n_ob, n_cb = -(-d_out // 128), -(-d_in // 256)
+    t = table.cpu().numpy().view(np.uint32).reshape(n_ob, n_cb, 8, 16, 128, 4)
+    bucket = np.zeros((n_ob * 128, n_cb * 256), np.uint32)
+    weight = np.zeros((n_ob * 128, n_cb * 256), np.float32)
+    for ob in range(n_ob):
+        for cb in range(n_cb):
+            blk = t[ob, cb]  # [j, p, r, 4]
+            for e in range(2):
+                cols = (np.arange(8)[:, None] * 32 + np.arange(16)[None, :] * 2 + e)  # [j, p]
+                b = blk[..., e].transpose(2, 0, 1)  # [r, j, p]
+                w = blk[..., 2 + e].transpose(2, 0, 1).view(np.float32)
+                bucket[ob * 128:(ob + 1) * 128, cb * 256 + cols] = b
+                weight[ob * 128:(ob + 1) * 128, cb * 256 + cols] = w
+    return bucket, weight
+
+
+@pytest.mark.parametrize("d_out,d_in", [(128, 256), (72, 48), (200, 520)])
+def test_table_layout_and_adam_diag(d_out, d_in):
+    k = 4096
+    h, s, packed = cuda_tables(d_out * d_in, 1, k)
+    v = np.random.default_rng(0).uniform(1e-9, 1e-3, (d_out, d_in)).astype(np.float32)
+    table = ops.build_sketch_table(packed, d_out, d_in, exp_avg_sq=torch.from_numpy(v).to(DEV), eps=1e-8)
+    bucket, weight = decode_table(table, d_out, d_in)
+    np.testing.assert_array_equal(bucket[:d_out, :d_in], h.reshape(d_out, d_in))
+    want = s.reshape(d_out, d_in) * orc.inv_rms(v, 1e-8)
+    np.testing.assert_array_equal(weight[:d_out, :d_in], want)  # bit-exact AdamW diagonal
+    assert not weight[d_out:, :].any() and not weight[:, d_in:].any()
+    diag = torch.rand(d_out, d_in, device=DEV)
+    _, weight2 = decode_table(ops.build_sketch_table(packed, d_out, d_in, diag=diag), d_out, d_in)
+    np.testing.assert_array_equal(weight2[:d_out, :d_in], s.reshape(d_out, d_in) * diag.cpu().numpy())
+
+
+SKETCH_SHAPES = [
+    # B, T, d_out, d_in, k
+    (1, 64, 128, 256, 512),
+    (2, 100, 72, 48, 512),
+    (3, 1, 8, 8, 64),
+    (2, 130, 200, 264, 1000),
+    (4, 64, 384, 768, 16384),
+    (2, 70, 128, 256, 32768),
+    (2, 64, 136, 264, 65536),
+    (5, 33, 136, 520, 8192),
+]
+
+
+@pytest.mark.parametrize("B,T,d_out,d_in,k", SKETCH_SHAPES)
+def test_sketch_gemm_matches_oracle(B, T, d_out, d_in, k):
+    torch.manual_seed(B * 1000 + T)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 3, k)
+    diag = torch.rand(d_out, d_in, device=DEV) * 1e-3 + 1e-6
+    table = ops.build_sketch_table(packed, d_out, d_in, diag=diag)
+    phi = ops.sketch_gemm(g, a, table, k)
+    ops.check_device_error("sketch_gemm")
+    want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k,
+                                     diag=diag.cpu().numpy())
+    rel_close(phi.cpu().numpy(), want, 1e-4, "phi")
+
+
+def test_sketch_gemm_rows_div_and_accumulate():
+    B, T, d_out, d_in, k = 6, 48, 64, 128, 2048
+    g = torch.randn(B, T, d_out, device=DEV).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 0, k)
+    table = ops.build_sketch_table(packed, d_out, d_in)
+    per = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
+    grouped = ops.sketch_gemm(g, a, table, k, rows_div=4)  # rows {0..3}, {4, 5}
+    rel_close(grouped.cpu().numpy(), np.stack([per[:4].sum(0), per[4:].sum(0)]), 1e-4, "rows_div")
+    out = ops.sketch_gemm(g, a, table, k)
+    ops.sketch_gemm(g, a, table, k, out=out, accumulate=True)
+    rel_close(out.cpu().numpy(), 2 * per, 1e-4, "accumulate")
+
+
+def test_sketch_gemm_f32_inputs_split():
+    B, T, d_out, d_in, k = 3, 50, 96, 64, 1024
+    g = torch.randn(B, T, d_out, device=DEV)
+    a = torch.randn(B, T, d_in, device=DEV)
+    h, s, packed = cuda_tables(d_out * d_in, 2, k)
+    phi = ops.sketch_gemm(g, a, ops.build_sketch_table(packed, d_out, d_in), k)
+    want = orc.project_full_gradient(g.cpu().numpy(), a.cpu().numpy(), h, s, k)
+    rel_close(phi.cpu().numpy(), want, 2e-5, "f32 split")
+
+
+def test_project_full_gradient_golden():
+    gd = load_golden("project")
+    for i in range(int(gd["n"])):
+        k, pid, _two_d = (int(x) for x in gd[f"meta{i}"])
+        proj = GradientProjector(sketch_dim=k, seed=42, device="cpu")
+        S = gd.get(f"S{i}")
+        diag = gd.get(f"diag{i}")
+        phi = proj.project_full_gradient(torch.from_numpy(gd[f"g{i}"]).to(DEV), torch.from_numpy(gd[f"a{i}"]).to(DEV),
+                                         param_id=pid, preconditioner_S=None if S is None else torch.from_numpy(S).to(DEV),
+                                         diagonal_preconditioner=None if diag is None else torch.from_numpy(diag).to(DEV))
+        rel_close(phi.cpu().numpy(), gd[f"phi{i}"], 1e-4, f"golden project case {i}")
+
+
+@pytest.mark.parametrize("transposed", [False, True])
+@pytest.mark.parametrize("d_out,d_in,k", [(64, 96, 256), (3072, 768, 16384), (100, 36, 100000)])
+def test_sketch_dense(transposed, d_out, d_in, k):
+    h, s, packed = cuda_tables(d_out * d_in, 5, k)
+    W = torch.randn(d_out, d_in, device=DEV)
+    diag = torch.rand(d_out, d_in, device=DEV)
+    src = W.T.contiguous() if transposed else W
+    out = ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, diag=diag)
+    want = orc.dense_sketch(W.cpu().numpy(), h, s, k, diag=diag.cpu().numpy())
+    rel_close(out.cpu().numpy(), want, 1e-5, "dense sketch")
+
+
+def test_sketch_dot_and_gram():
+    rng = np.random.default_rng(1)
+    A = rng.standard_normal((70, 3000)).astype(np.float32)
+    Bm = rng.standard_normal((9, 3000)).astype(np.float32)
+    tau = rng.standard_normal(3000).astype(np.float32)
+    tA, tB, tt = (torch.from_numpy(x).to(DEV) for x in (A, Bm, tau))
+    rel_close(ops.sketch_dot(tA, tt, alpha=0.5).cpu().numpy(), 0.5 * A.astype(np.float64) @ tau, 1e-5, "dot")
+    rel_close(ops.sketch_gram(tA, alpha=2.0).cpu().numpy(), 2.0 * A.astype(np.float64) @ A.T, 1e-5, "gram")
+    out = ops.sketch_gram(tA, tB)
+    ops.sketch_gram(tA, tB, out=out, accumulate=True)
+    rel_close(out.cpu().numpy(), 2.0 * A.astype(np.float64) @ Bm.T, 1e-5, "gram ab")
+
+
+def test_split_bf16():
+    x = torch.randn(10001, device=DEV) * 100
+    hi, lo = ops.split_bf16(x)
+    assert torch.equal(hi, x.bfloat16())
+    err = (hi.float() + lo.float() - x).abs() / x.abs()
+    assert float(err.max()) < 2 ** -15
+
+
+@pytest.mark.parametrize("B,T,d_in,d_out", [(2, 128, 64, 256), (3, 100, 48, 72), (2, 300, 264, 520),
+                                            (4, 256, 768, 3072)])
+def test_ghost_score_matches_oracle(B, T, d_in, d_out):
+    torch.manual_seed(T)
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    V = torch.randn(d_out, d_in, device=DEV) / d_in ** 0.5
+    got = ops.ghost_score(a, g, ops.dense_target_pair(V), alpha=1.5)
+    ops.check_device_error("ghost_score")
+    want = 1.5 * orc.ghost_score(a.float().cpu().numpy(), g.float().cpu().numpy(), V.cpu().numpy())
+    rel_close(got.cpu().numpy(), want, 1e-4, "ghost")
+
+
+def test_ghost_equals_sketch_dot_through_desketch():
+    """<G_b, D s tau[h]> by the ghost kernel == CS(D o G_b) . tau by the sketch kernels."""
+    B, T, d_out, d_in, k = 4, 256, 384, 256, 4096
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-2).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 9, k)
+    v = torch.rand(d_out, d_in, device=DEV) * 1e-3
+    tau = torch.randn(k, device=DEV)
+    phi = ops.sketch_gemm(g, a, ops.build_sketch_table(packed, d_out, d_in, exp_avg_sq=v), k)
+    via_sketch = ops.sketch_dot(phi, tau, alpha=0.25)
+    vt = ops.desketch(tau, packed, d_out, d_in, scale=0.25, exp_avg_sq=v)
+    via_ghost = ops.ghost_score(a, g, vt)
+    rel_close(via_ghost.cpu().numpy(), via_sketch.cpu().numpy(), 1e-4, "ghost vs sketch")
