@@ -51,7 +51,10 @@ def parse_args():
     ap.add_argument("--impl", default="opus_b200", choices=["opus_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    return ap.parse_args()
+    ap.add_argument("--batch", type=int, default=B,
+                    help="candidates per GPU (default 256; smaller only for profiling captures)")
+    args = ap.parse_args()
+    return args
 
 
 def measured_peaks():
@@ -115,13 +118,13 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_inputs(device, rank):
+def make_inputs(device, rank, nb=B):
     """Seeded synthetic inputs of the workload shapes, generated on the device."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(1234 + rank)
-    a = torch.randn(B, T, D_IN, generator=g, device=device).to(torch.bfloat16)
-    dz = (torch.randn(B, T, D_OUT, generator=g, device=device) * 1e-3).to(torch.bfloat16)
+    a = torch.randn(nb, T, D_IN, generator=g, device=device).to(torch.bfloat16)
+    dz = (torch.randn(nb, T, D_OUT, generator=g, device=device) * 1e-3).to(torch.bfloat16)
     V = torch.randn(D_IN, D_OUT, generator=g, device=device) * (1.0 / D_IN) ** 0.5
     diag = torch.rand(D_OUT, D_IN, generator=g, device=device) * (1e-3 - 1e-6) + 1e-6
     return a, dz, V, diag
@@ -138,15 +141,18 @@ def run_gpu(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    a, dz, V, diag = make_inputs(dev, rank)
+    nb = args.batch
+    n_sel = max(1, nb // 4)
+    a, dz, V, diag = make_inputs(dev, rank, nb)
     proj = GradientProjector(sketch_dim=K_SKETCH, seed=SEED, device="cuda")
     pid = 0
     packed = proj.packed_table(D_OUT * D_IN, pid, dev)
-    uni = torch.from_numpy(np.random.default_rng(99 + rank).random(N_SELECT)).to(dev)
-    phi = torch.empty(B, K_SKETCH, device=dev)
+    load = proj.max_bucket_load(D_OUT * D_IN, pid, dev)
+    uni = torch.from_numpy(np.random.default_rng(99 + rank).random(n_sel)).to(dev)
+    phi = torch.empty(nb, K_SKETCH, device=dev)
     tau = torch.empty(K_SKETCH, device=dev)
-    score = torch.empty(B, device=dev)
-    sim = torch.empty(B, B, device=dev)
+    score = torch.empty(nb, device=dev)
+    sim = torch.empty(nb, nb, device=dev)
     ev = {}
 
     def step(time_kernel=False):
@@ -157,12 +163,12 @@ def run_gpu(args, rank, world, local_rank):
             ev["s"].append(torch.cuda.Event(enable_timing=True))
             ev["e"].append(torch.cuda.Event(enable_timing=True))
             ev["s"][-1].record()
-        ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi, accumulate=True)
+        ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi, accumulate=True, max_bucket_load=load)
         if time_kernel:
             ev["e"][-1].record()
         ops.sketch_dot(phi, tau, out=score)
         ops.sketch_gram(phi, out=sim)
-        return ops.boltzmann_select(score, sim, N_SELECT, TEMPERATURE, uni)
+        return ops.boltzmann_select(score, sim, n_sel, TEMPERATURE, uni)
 
     for _ in range(args.warmup):
         step()
@@ -201,13 +207,13 @@ def run_gpu(args, rank, world, local_rank):
             evs[1].record()
             ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau)
             evs[2].record()
-            ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi)
+            ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi, max_bucket_load=load)
             evs[3].record()
             ops.sketch_dot(phi, tau, out=score)
             evs[4].record()
             ops.sketch_gram(phi, out=sim)
             evs[5].record()
-            ops.boltzmann_select(score, sim, N_SELECT, TEMPERATURE, uni)
+            ops.boltzmann_select(score, sim, n_sel, TEMPERATURE, uni)
             evs[6].record()
             torch.cuda.synchronize()
             for i in range(len(names)):
@@ -232,7 +238,7 @@ def run_gpu(args, rank, world, local_rank):
             tau_e = proj.project_vector(V_d.T, pid)
             sc = ops.sketch_dot(phi_e, tau_e)
             sm = ops.sketch_gram(phi_e)
-            return ds.stochastic_greedy_selection(sc, sm, N_SELECT, temperature=TEMPERATURE)
+            return ds.stochastic_greedy_selection(sc, sm, n_sel, temperature=TEMPERATURE)
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):
@@ -252,8 +258,8 @@ def run_gpu(args, rank, world, local_rank):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t[0])
         h2d = sum(x.numel() * x.element_size() for x in (a_h, dz_h, V_h, diag_h))
-        e2e = {"value": round(B * world / (e_ms / e2e_steps / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": N_SELECT * 8, "api": "GradientProjector.project_full_gradient + "
+        e2e = {"value": round(nb * world / (e_ms / e2e_steps / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": n_sel * 8, "api": "GradientProjector.project_full_gradient + "
                "project_vector + stochastic_greedy_selection", "steps": e2e_steps}
     return ms_per_step, kern_ms, stages, e2e, clk.summary()
 
@@ -357,7 +363,8 @@ def main():
             dist.barrier()
     if rank == 0:
         burst, sustained, hbm, src = measured_peaks()
-        flops = 2.0 * B * T * D_OUT * D_IN
+        nb = args.batch
+        flops = 2.0 * nb * T * D_OUT * D_IN
         achieved = flops / (kern_ms * 1e-3) / 1e12
         roofline = {"bound": "tensor", "kernel": "sketch_gemm", "achieved": round(achieved, 2),
                     "peak": sustained, "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
@@ -370,12 +377,13 @@ def main():
             cpu = {"value": round(v, 4), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
                    "sample": f"{done} of 256 candidates ({per_cand:.3f} s each, f32 GEMM + AdamW diag + CountSketch "
                              f"+ dots) + one 64-of-256 draw ({t_sel:.3f} s), extrapolated to 256"}
-        value = B * world / (ms_per_step / 1e3)
+        value = nb * world / (ms_per_step / 1e3)
         line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": T, "k": K_SKETCH,
-                           "select": f"{N_SELECT} of {B} per GPU, Boltzmann T={TEMPERATURE}",
+                "config": {"workload": WORKLOAD if nb == B else WORKLOAD.replace("256 seqs", f"{nb} seqs"),
+                           "global_batch": nb * world, "seq_len": T, "k": K_SKETCH,
+                           "select": f"{max(1, nb // 4)} of {nb} per GPU, Boltzmann T={TEMPERATURE}",
                            "parallelism": f"dp{world} (candidates sharded, local selection)",
                            "l2": "inputs 2.0 GB per GPU > 126 MB L2, no flush"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,

@@ -97,13 +97,21 @@ OPUS_API int opus_build_sketch_table(const uint32_t* packed, const float* diag, 
  *         being linear).  d_out and d_in must be multiples of 8.
  *   phi:  [ceil(n_rows/rows_div), k] f32; row b/rows_div receives candidate b
  *         (rows_div = n_rows sums the proxy batch into one row).
+ *   max_bucket_load: the largest number of weight elements sharing one bucket
+ *         (max of the bucket histogram).  It bounds the CTA's 32-bit
+ *         fixed-point shared-memory sketch so no bucket can overflow; <= 0
+ *         sends every update to f32 global atomics instead (exact, slower).
  *   accumulate = 0 zeroes phi first.
+ * Accuracy: each update is rounded to a power-of-two quantum of at most
+ * 2^-(log2(2^31/max_bucket_load) - 3) times the largest |w G| of the
+ * candidate's first tile in the CTA (~1e-6 relative for GPT-2 layers);
+ * larger, NaN or Inf updates are added exactly in f32.
  * Replaces GradientProjector.project_full_gradient
  * (OPUS/train/random_projection.py:134-193) on 3-D inputs.
  */
 OPUS_API int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
-                     int d_in, const void* table, int64_t table_entries, int64_t k, int rows_div,
-                     float* phi, int accumulate, void* stream);
+                     int d_in, const void* table, int64_t table_entries, int64_t k, int max_bucket_load,
+                     int rows_div, float* phi, int accumulate, void* stream);
 
 /*
  * K1 — dense CountSketch of one [d_out,d_in] f32 matrix (the proxy target

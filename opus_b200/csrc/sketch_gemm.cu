@@ -7,16 +7,28 @@
 // w(o,c) = s(o,c) * D(o,c) from the precomputed table and adds it into bucket
 // h(o,c) of candidate b's sketch.  G_b is never written to HBM.
 //
-// Warp roles (192 threads, persistent, one CTA per SM):
+// Warp roles (320 threads, persistent, one CTA per SM):
 //   warp 0      TMA producer: 3-D tile loads of dLdZ and a into a ring of
 //               shared-memory stages (128-byte swizzle, MN-major operands);
 //   warp 1      TMEM allocation + single-thread UMMA issue into one of two
 //               256-column accumulators (double-buffered against the epilogue);
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator, table lookup,
-//               shared-memory atomic scatter into the CTA's private sketch,
-//               flushed to HBM with vector reductions when the candidate row
-//               changes (or scattered straight to HBM when k is too large for
-//               shared memory).
+//   warps 2..9  epilogue: two warps per TMEM lane quarter, each taking half
+//               of the tile's 32-column chunks.
+//
+// Shared-memory sketch in 32-bit fixed point.  Float atomics on shared memory
+// are compare-and-swap loops on this hardware, integer adds are native, so
+// the CTA-private sketch of the current candidate holds int32 buckets at a
+// power-of-two scale S chosen from the candidate's first tile in this CTA
+// (max |w G| maps to cap/16).  cap = 2^31 / (largest bucket load of the
+// layer) bounds every admitted update, so no bucket can overflow whatever the
+// data; an update above cap (or NaN/Inf, or any update before a scale could
+// be chosen) goes straight to the f32 output row with a global atomic add.
+// The sketch is converted back to f32 and added to the output row (vector
+// reductions) whenever the candidate changes.  Quantisation error per update
+// is at most (max |w G| of the first tile) * 2^-(log2(cap) - 4 + 1), i.e.
+// ~1e-6 of the tile maximum for the GPT-2 layer shapes.  When k is too large
+// for shared memory every update is an f32 global atomic add.
+//
 // Work units (b, ob, cb) are numbered candidate-major and split into equal
 // contiguous ranges, one per CTA.
 #include <cstdio>
@@ -27,8 +39,11 @@
 namespace opus {
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int kChunksPerWarp = kChunksPerTile / (kEpiWarps / 4);  // 4
+constexpr int kHeadroomLog2 = 4;                     // first-tile max maps to cap / 16
 constexpr int kBoxMN = 64;                           // bf16 elements per 128-byte swizzle row
 constexpr int kBK = 64;                              // tokens per pipeline stage
 constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
@@ -49,7 +64,7 @@ constexpr int kTmemCols = 2 * kTileN;  // two accumulators
 
 struct SmemPlan {
   int stages;
-  int smem_sketch;   // 1: CTA-private sketch in shared memory
+  int smem_sketch;   // 1: CTA-private fixed-point sketch in shared memory
   size_t bytes;      // dynamic shared memory to request
 };
 
@@ -61,8 +76,8 @@ __device__ __forceinline__ uint4 ld_nc_na(const uint4* p) {
   return v;
 }
 
-// Bounded barrier over the 128 epilogue threads (an mbarrier, so that a
-// thread that gave up cannot leave the others blocked forever).
+// Bounded barrier over the epilogue threads (an mbarrier, so that a thread
+// that gave up cannot leave the others blocked forever).
 __device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatile int* abort_flag, int* err) {
   mbar_arrive(bar);
   const bool ok = mbar_wait(bar, phase, abort_flag, err, kDevTimeoutGroup);
@@ -70,24 +85,26 @@ __device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatil
   return ok;
 }
 
-__device__ bool flush_sketch(float* sk, float* dst, int64_t k, int et, uint64_t* bar, uint32_t& phase,
-                             volatile int* abort_flag, int* err) {
+// Add the fixed-point sketch (scaled by 2^-scale_exp) into dst and clear it.
+__device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int et, uint64_t* bar,
+                             uint32_t& phase, volatile int* abort_flag, int* err) {
   if (!epi_sync(bar, phase, abort_flag, err)) return false;
+  const float inv = ldexpf(1.0f, -scale_exp);
   if ((k & 3) == 0) {
-    float4* s4 = reinterpret_cast<float4*>(sk);
+    int4* s4 = reinterpret_cast<int4*>(sk);
     for (int64_t i = et; i < k / 4; i += kEpiThreads) {
-      const float4 x = s4[i];
-      if (x.x != 0.0f || x.y != 0.0f || x.z != 0.0f || x.w != 0.0f) {
-        red_add_v4(dst + 4 * i, x.x, x.y, x.z, x.w);
-        s4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const int4 q = s4[i];
+      if (q.x | q.y | q.z | q.w) {
+        red_add_v4(dst + 4 * i, (float)q.x * inv, (float)q.y * inv, (float)q.z * inv, (float)q.w * inv);
+        s4[i] = make_int4(0, 0, 0, 0);
       }
     }
   } else {
     for (int64_t i = et; i < k; i += kEpiThreads) {
-      const float x = sk[i];
-      if (x != 0.0f) {
-        atomicAdd(dst + i, x);
-        sk[i] = 0.0f;
+      const int q = sk[i];
+      if (q != 0) {
+        atomicAdd(dst + i, (float)q * inv);
+        sk[i] = 0;
       }
     }
   }
@@ -97,12 +114,13 @@ __device__ bool flush_sketch(float* sk, float* dst, int64_t k, int et, uint64_t*
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
-                       int n_cb, int64_t k, int rows_div, int stages, int smem_sketch, int* err) {
+                       int n_cb, int64_t k, int rows_div, int stages, int smem_sketch, float cap, int cap_log2,
+                       int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* stage_mem = smem;
-  float* sk = reinterpret_cast<float*>(smem + (size_t)stages * kStageBytes);
+  int* sk = reinterpret_cast<int*>(smem + (size_t)stages * kStageBytes);
   uint8_t* tail = smem + (size_t)stages * kStageBytes + (smem_sketch ? (size_t)k * 4 : 0);
   tail = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tail) + 15) & ~uintptr_t(15));
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
@@ -113,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain_bar = epi_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* tile_max_bits = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tiles_per_row = (int64_t)n_ob * n_cb;
@@ -133,6 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(epi_bar, kEpiThreads);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
+    *tile_max_bits = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -144,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   if (smem_sketch) {
-    for (int64_t i = threadIdx.x; i < k; i += kThreads) sk[i] = 0.0f;
+    for (int64_t i = threadIdx.x; i < k; i += kThreads) sk[i] = 0;
   }
   tc_fence_before();
   __syncthreads();
@@ -227,57 +247,119 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int et = threadIdx.x - 64;          // 0..127
+    const int et = threadIdx.x - 64;          // 0..255
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;         // which 4 of the 8 column chunks
     const int r = q * 32 + lane;              // tile row owned by this thread
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t kk32 = static_cast<uint32_t>(k);
     int acc = 0;
     uint32_t aph = 0;
     uint32_t epi_phase = 0;
-    int64_t cur_row = -1;
+    int64_t cur_b = -1;
+    int scale_exp = 0;      // fixed-point scale S = 2^scale_exp of the current candidate
+    bool scaled = false;    // a scale has been chosen for the current candidate
     bool bad = false;
     bool ok = true;
     for (int64_t u = u_begin; u < u_end; ++u) {
       const int b = static_cast<int>(u / tiles_per_row);
       const int64_t tile = u % tiles_per_row;
-      const int64_t row = b / rows_div;
-      if (smem_sketch && row != cur_row) {
-        if (cur_row >= 0 && !flush_sketch(sk, phi + cur_row * k, k, et, epi_bar, epi_phase, abort_flag, err)) {
+      float* out_row = phi + (int64_t)(b / rows_div) * k;
+      if (smem_sketch && b != cur_b) {
+        if (cur_b >= 0 && !flush_sketch(sk, phi + (cur_b / rows_div) * k, k, scale_exp, et, epi_bar, epi_phase,
+                                        abort_flag, err)) {
           ok = false;
           break;
         }
-        cur_row = row;
+        cur_b = b;
+        scaled = false;
       }
       if (!mbar_wait(&tfull[acc], aph, abort_flag, err, kDevTimeoutEpilogue)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float* dst = smem_sketch ? sk : phi + row * k;
       const uint4* tp = table + tile * kEntriesPerTile + r;
-      const uint32_t kk32 = static_cast<uint32_t>(k);
+      const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
+      if (smem_sketch && !scaled) {
+        // First tile of this candidate in this CTA: scale from max |w G| over the tile.
+        float m = 0.0f;
+        for (int jj = 0; jj < kChunksPerWarp; ++jj) {
+          const int j = half * kChunksPerWarp + jj;
+          uint32_t v[32];
+          tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int p = 0; p < kPairsPerChunk; ++p) {
+            const uint4 e = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
+            const float x0 = fabsf(__uint_as_float(v[2 * p]) * __uint_as_float(e.z));
+            const float x1 = fabsf(__uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w));
+            if (x0 <= 3.0e38f) m = fmaxf(m, x0);   // finite values only
+            if (x1 <= 3.0e38f) m = fmaxf(m, x1);
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        if (lane == 0) atomicMax(tile_max_bits, __float_as_int(m));
+        if (!epi_sync(epi_bar, epi_phase, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        const float tmax = __int_as_float(*const_cast<volatile int*>(tile_max_bits));
+        if (tmax > 0.0f) {
+          int e2;
+          frexpf(tmax, &e2);                       // tmax < 2^e2
+          int se = cap_log2 - kHeadroomLog2 - e2;  // tmax * 2^se < cap / 16
+          se = max(-120, min(120, se));
+          scale_exp = se;
+          scaled = true;
+        }
+        if (!epi_sync(epi_bar, epi_phase, abort_flag, err)) {  // everyone has read the maximum
+          ok = false;
+          break;
+        }
+        if (et == 0) *tile_max_bits = 0;
+      }
+      const float S = ldexpf(1.0f, scale_exp);
+      const bool use_int = smem_sketch && scaled;
 #pragma unroll 1
-      for (int j = 0; j < kChunksPerTile; ++j) {
+      for (int jj = 0; jj < kChunksPerWarp; ++jj) {
+        const int j = half * kChunksPerWarp + jj;
         uint32_t v[32];
-        tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTileN + j * kChunkCols), v);
+        tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
         tmem_ld_wait();
+        if (jj == kChunksPerWarp - 1) {
+          // all of this thread's accumulator reads are done: release the buffer
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
 #pragma unroll
         for (int p = 0; p < kPairsPerChunk; ++p) {
           const uint4 e = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
-          const float x0 = __uint_as_float(v[2 * p]) * __uint_as_float(e.z);
-          const float x1 = __uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w);
-          if (e.x < kk32) atomicAdd(dst + e.x, x0); else bad = true;
-          if (e.y < kk32) atomicAdd(dst + e.y, x1); else bad = true;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t bucket = h ? e.y : e.x;
+            const float x = __uint_as_float(v[2 * p + h]) * __uint_as_float(h ? e.w : e.z);
+            if (bucket >= kk32) {
+              bad = true;
+              continue;
+            }
+            const float y = x * S;
+            if (use_int && fabsf(y) < cap) {
+              atomicAdd(sk + bucket, __float2int_rn(y));
+            } else if (x != 0.0f) {
+              atomicAdd(out_row + bucket, x);   // outlier, non-finite, unscaled or no shared sketch
+            }
+          }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         aph ^= 1;
       }
     }
-    if (ok && smem_sketch && cur_row >= 0) flush_sketch(sk, phi + cur_row * k, k, et, epi_bar, epi_phase, abort_flag, err);
+    if (ok && smem_sketch && cur_b >= 0)
+      flush_sketch(sk, phi + (cur_b / rows_div) * k, k, scale_exp, et, epi_bar, epi_phase, abort_flag, err);
     if (bad) record_device_error(err, kDevBadBucket);
   }
 
@@ -289,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 SmemPlan plan_smem(int64_t k) {
   const size_t limit = static_cast<size_t>(max_smem_optin());
-  const size_t fixed = 1024 /*alignment slack*/ + 16 + 8 * (2 * 8 + 6) + 16;
+  const size_t fixed = 1024 /*alignment slack*/ + 16 + 8 * (2 * 8 + 6) + 32;
   SmemPlan p{0, 0, 0};
   for (int st = 6; st >= 2; --st) {
     const size_t need = fixed + (size_t)st * kStageBytes + (size_t)k * 4;
@@ -312,8 +394,8 @@ SmemPlan plan_smem(int64_t k) {
 using namespace opus;
 
 extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
-                                int d_in, const void* table, int64_t table_entries_given, int64_t k, int rows_div,
-                                float* phi, int accumulate, void* stream) {
+                                int d_in, const void* table, int64_t table_entries_given, int64_t k,
+                                int max_bucket_load, int rows_div, float* phi, int accumulate, void* stream) {
   if (dtype != OPUS_DTYPE_BF16)
     return set_error(OPUS_ERR_UNSUPPORTED,
                      "sketch_gemm: operands must be bf16 (split f32 operands into bf16 hi/lo with opus_split_bf16)");
@@ -349,8 +431,28 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  const SmemPlan plan = plan_smem(k);
+  SmemPlan plan = plan_smem(k);
   if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small");
+  // Fixed-point cap: max_bucket_load admitted updates of magnitude <= cap sum to < 2^31.
+  float cap = 0.0f;
+  int cap_log2 = 0;
+  if (max_bucket_load > 0) {
+    const int64_t cap_int = 0x7FFFFFFFll / max_bucket_load;
+    cap = static_cast<float>(cap_int);
+    if (static_cast<double>(cap) > static_cast<double>(cap_int)) cap = nextafterf(cap, 0.0f);
+    while ((int64_t(1) << (cap_log2 + 1)) <= cap_int) ++cap_log2;
+    if (cap_log2 < 2 * kHeadroomLog2) max_bucket_load = 0;  // too little range left for fixed point
+  }
+  if (max_bucket_load <= 0 && plan.smem_sketch) {
+    // No usable bound: every update goes to global f32 atomics; use the smem for stages.
+    for (int stg = 4; stg >= 2; --stg) {
+      const size_t need = plan.bytes - (size_t)plan.stages * kStageBytes - (size_t)k * 4 + (size_t)stg * kStageBytes;
+      if (need <= static_cast<size_t>(max_smem_optin())) {
+        plan = {stg, 0, need};
+        break;
+      }
+    }
+  }
   OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
@@ -359,7 +461,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   int* err = device_error_word();
   sketch_gemm_kernel<<<grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows,
                                                         seq_len, n_ob, n_cb, k, rows_div, plan.stages, plan.smem_sketch,
-                                                        err);
+                                                        cap, cap_log2, err);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -62,6 +62,13 @@ def pack_hash_sign(hash_: torch.Tensor, sign: torch.Tensor, k: int, validate: bo
     return out
 
 
+def bucket_max_load(packed: torch.Tensor, k: int) -> int:
+    """Largest number of elements sharing one bucket (bounds the fixed-point sketch)."""
+    _cuda(packed, "packed")
+    buckets = (packed.reshape(-1) & 0x7FFFFFFF).to(torch.int64)
+    return int(torch.bincount(buckets, minlength=int(k)).max().item()) if buckets.numel() else 0
+
+
 def sketch_table_entries(d_out: int, d_in: int) -> int:
     return int(_lib.load().opus_sketch_table_entries(int(d_out), int(d_in)))
 
@@ -108,11 +115,14 @@ def _as3d(t: torch.Tensor, name: str) -> torch.Tensor:
 
 
 def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int, rows_div: int = 1,
-                out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+                out: torch.Tensor | None = None, accumulate: bool = False,
+                max_bucket_load: int = 0) -> torch.Tensor:
     """phi[b // rows_div] (+)= CountSketch(w o (dLdZ_b^T a_b)) for every candidate b.
 
     dLdZ [B, T, d_out] and a [B, T, d_in] in bf16 (tensor cores directly) or
     f32 (split into bf16 hi/lo; hi*hi + hi*lo + lo*hi accumulated).
+    max_bucket_load (see bucket_max_load) enables the fixed-point
+    shared-memory sketch; 0 adds every update with f32 global atomics.
     """
     _cuda(dLdZ, "dLdZ")
     _cuda(a, "a")
@@ -131,7 +141,8 @@ def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int
 
     def launch(g: torch.Tensor, x: torch.Tensor, acc: bool) -> None:
         _lib.check(lib.opus_sketch_gemm(_ptr(g), _ptr(x), _lib.DTYPE_BF16, B, T, d_out, d_in, _ptr(table), n_entries,
-                                        int(k), int(rows_div), _ptr(out), int(acc), _stream(g)),
+                                        int(k), int(max_bucket_load), int(rows_div), _ptr(out), int(acc),
+                                        _stream(g)),
                    "opus_sketch_gemm")
 
     if dLdZ.dtype == torch.bfloat16 and a.dtype == torch.bfloat16:

@@ -34,6 +34,8 @@ class GradientProjector:
         self.sign_functions: dict = {}
         # (numel, param_id, compute device) -> packed uint32 table (int32 storage)
         self._packed: dict = {}
+        # (numel, param_id) -> largest bucket load (bounds the fixed-point sketch)
+        self._max_load: dict = {}
         # (numel, param_id, d_out, d_in, compute device) -> sign-only epilogue table
         self._sign_tables: dict = {}
 
@@ -62,7 +64,14 @@ class GradientProjector:
             h, s = self._get_hash_and_sign(param_numel, param_id) if cached else self._generate(param_numel, param_id)
             t = ops.pack_hash_sign(h.to(device), s.to(device), self.sketch_dim)
             self._packed[key] = t
+            if (param_numel, param_id) not in self._max_load:
+                self._max_load[(param_numel, param_id)] = ops.bucket_max_load(t, self.sketch_dim)
         return t
+
+    def max_bucket_load(self, param_numel: int, param_id: int, device) -> int:
+        """Largest number of a parameter's elements hashed to one bucket."""
+        self.packed_table(param_numel, param_id, device)
+        return self._max_load[(param_numel, param_id)]
 
     def layer_table(self, d_out: int, d_in: int, param_id: int, device, diag: torch.Tensor | None = None,
                     exp_avg_sq: torch.Tensor | None = None, eps: float = 1e-8) -> tuple[torch.Tensor, int, int]:
@@ -152,7 +161,10 @@ class GradientProjector:
             dLdZ = torch.nn.functional.pad(dLdZ, (0, do_p - d_out))
         if di_p != d_in:
             a = torch.nn.functional.pad(a, (0, di_p - d_in))
-        return ops.sketch_gemm(dLdZ, a, table, self.sketch_dim, rows_div=rows_div, out=out, accumulate=accumulate)
+        # padded elements (bucket 0, weight 0) add exact zeros: they do not count toward the load
+        load = self.max_bucket_load(d_out * d_in, param_id, dLdZ.device)
+        return ops.sketch_gemm(dLdZ, a, table, self.sketch_dim, rows_div=rows_div, out=out, accumulate=accumulate,
+                               max_bucket_load=load)
 
     def clear_cache(self):
         """Drop every cached table (random_projection.py:195-198)."""
@@ -160,3 +172,4 @@ class GradientProjector:
         self.sign_functions.clear()
         self._packed.clear()
         self._sign_tables.clear()
+        self._max_load.clear()

@@ -44,9 +44,11 @@ def _null():
 def test_argument_validation_without_device():
     """Entry points reject bad arguments before touching the device (status codes, message set)."""
     lib = _lib.load()
-    rc = lib.opus_sketch_gemm(_null(), _null(), _lib.DTYPE_F32, 1, 1, 8, 8, _null(), 0, 16, 1, _null(), 0, _null())
+    rc = lib.opus_sketch_gemm(_null(), _null(), _lib.DTYPE_F32, 1, 1, 8, 8, _null(), 0, 16, 4, 1, _null(), 0,
+                              _null())
     assert rc == _lib.OPUS_ERR_UNSUPPORTED and "bf16" in _lib.last_error()
-    rc = lib.opus_sketch_gemm(_null(), _null(), _lib.DTYPE_BF16, -1, 1, 8, 8, _null(), 0, 16, 1, _null(), 0, _null())
+    rc = lib.opus_sketch_gemm(_null(), _null(), _lib.DTYPE_BF16, -1, 1, 8, 8, _null(), 0, 16, 4, 1, _null(), 0,
+                              _null())
     assert rc == _lib.OPUS_ERR_INVALID
     with pytest.raises(ValueError):
         _lib.check(rc, "opus_sketch_gemm")

@@ -88,19 +88,45 @@ SKETCH_SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("fixed_point", [True, False])
 @pytest.mark.parametrize("B,T,d_out,d_in,k", SKETCH_SHAPES)
-def test_sketch_gemm_matches_oracle(B, T, d_out, d_in, k):
+def test_sketch_gemm_matches_oracle(B, T, d_out, d_in, k, fixed_point):
     torch.manual_seed(B * 1000 + T)
     g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
     a = torch.randn(B, T, d_in, device=DEV).bfloat16()
     h, s, packed = cuda_tables(d_out * d_in, 3, k)
     diag = torch.rand(d_out, d_in, device=DEV) * 1e-3 + 1e-6
     table = ops.build_sketch_table(packed, d_out, d_in, diag=diag)
-    phi = ops.sketch_gemm(g, a, table, k)
+    load = ops.bucket_max_load(packed, k) if fixed_point else 0
+    assert load == int(np.bincount(h, minlength=k).max()) or not fixed_point
+    phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=load)
     ops.check_device_error("sketch_gemm")
     want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k,
                                      diag=diag.cpu().numpy())
     rel_close(phi.cpu().numpy(), want, 1e-4, "phi")
+
+
+def test_sketch_gemm_outliers_and_nonfinite():
+    """Updates far above the first tile's scale, and NaN, take the exact f32 path.
+
+    300 work units over at most 148 CTAs: each CTA sees two or more
+    consecutive tiles of a candidate, and every odd o-block of candidate 0 is
+    1e6 times larger than the even ones, so a CTA that scaled on an even tile
+    meets outliers on the next one.
+    """
+    B, T, d_out, d_in, k = 4, 64, 9600, 256, 4096
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3)
+    g[0].view(T, 75, 128)[:, 1::2, :] *= 1e6
+    g[1, 5, 200] = float("nan")   # candidate 1: NaN reaches a set of buckets
+    g = g.bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 4, k)
+    table = ops.build_sketch_table(packed, d_out, d_in)
+    phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=ops.bucket_max_load(packed, k)).cpu().numpy()
+    want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
+    rel_close(phi[0], want[0], 1e-4, "outlier candidate")
+    np.testing.assert_array_equal(np.isnan(phi[1]), np.isnan(want[1]))
+    assert np.isnan(phi[1]).any()
 
 
 def test_sketch_gemm_rows_div_and_accumulate():
@@ -109,11 +135,12 @@ def test_sketch_gemm_rows_div_and_accumulate():
     a = torch.randn(B, T, d_in, device=DEV).bfloat16()
     h, s, packed = cuda_tables(d_out * d_in, 0, k)
     table = ops.build_sketch_table(packed, d_out, d_in)
+    load = ops.bucket_max_load(packed, k)
     per = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
-    grouped = ops.sketch_gemm(g, a, table, k, rows_div=4)  # rows {0..3}, {4, 5}
+    grouped = ops.sketch_gemm(g, a, table, k, rows_div=4, max_bucket_load=load)  # rows {0..3}, {4, 5}
     rel_close(grouped.cpu().numpy(), np.stack([per[:4].sum(0), per[4:].sum(0)]), 1e-4, "rows_div")
-    out = ops.sketch_gemm(g, a, table, k)
-    ops.sketch_gemm(g, a, table, k, out=out, accumulate=True)
+    out = ops.sketch_gemm(g, a, table, k, max_bucket_load=load)
+    ops.sketch_gemm(g, a, table, k, out=out, accumulate=True, max_bucket_load=load)
     rel_close(out.cpu().numpy(), 2 * per, 1e-4, "accumulate")
 
 
@@ -122,7 +149,8 @@ def test_sketch_gemm_f32_inputs_split():
     g = torch.randn(B, T, d_out, device=DEV)
     a = torch.randn(B, T, d_in, device=DEV)
     h, s, packed = cuda_tables(d_out * d_in, 2, k)
-    phi = ops.sketch_gemm(g, a, ops.build_sketch_table(packed, d_out, d_in), k)
+    phi = ops.sketch_gemm(g, a, ops.build_sketch_table(packed, d_out, d_in), k,
+                          max_bucket_load=ops.bucket_max_load(packed, k))
     want = orc.project_full_gradient(g.cpu().numpy(), a.cpu().numpy(), h, s, k)
     rel_close(phi.cpu().numpy(), want, 2e-5, "f32 split")
 
@@ -194,7 +222,8 @@ def test_ghost_equals_sketch_dot_through_desketch():
     h, s, packed = cuda_tables(d_out * d_in, 9, k)
     v = torch.rand(d_out, d_in, device=DEV) * 1e-3
     tau = torch.randn(k, device=DEV)
-    phi = ops.sketch_gemm(g, a, ops.build_sketch_table(packed, d_out, d_in, exp_avg_sq=v), k)
+    phi = ops.sketch_gemm(g, a, ops.build_sketch_table(packed, d_out, d_in, exp_avg_sq=v), k,
+                          max_bucket_load=ops.bucket_max_load(packed, k))
     via_sketch = ops.sketch_dot(phi, tau, alpha=0.25)
     vt = ops.desketch(tau, packed, d_out, d_in, scale=0.25, exp_avg_sq=v)
     via_ghost = ops.ghost_score(a, g, vt)
