@@ -29,8 +29,10 @@
 // ~1e-6 of the tile maximum for the GPT-2 layer shapes.  When k is too large
 // for shared memory every update is an f32 global atomic add.
 //
-// Work units (b, ob, cb) are numbered candidate-major and split into equal
-// contiguous ranges, one per CTA.
+// Work: a job is one candidate's tiles for a contiguous range of o-blocks
+// (every column block); jobs are numbered candidate-major and dealt to CTAs
+// round-robin, so at any time the CTAs work on neighbouring candidates whose
+// operands stay resident in L2, and each job ends with one sketch flush.
 #include <cstdio>
 
 #include "opus_common.cuh"
@@ -68,12 +70,23 @@ struct SmemPlan {
   size_t bytes;      // dynamic shared memory to request
 };
 
+// Read-only table load that bypasses L1 (each entry is read once per tile).
+// Not volatile: independent loads may be hoisted and kept in flight together.
 __device__ __forceinline__ uint4 ld_nc_na(const uint4* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
   return v;
+}
+
+// O-block range [begin, end) of job j: each candidate's o-blocks are split
+// into `groups` contiguous ranges.
+__device__ __forceinline__ int job_ob_begin(int64_t job, int groups, int n_ob) {
+  return static_cast<int>((job % groups) * n_ob / groups);
+}
+__device__ __forceinline__ int job_ob_end(int64_t job, int groups, int n_ob) {
+  return static_cast<int>((job % groups + 1) * n_ob / groups);
 }
 
 // Bounded barrier over the epilogue threads (an mbarrier, so that a thread
@@ -114,8 +127,8 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
-                       int n_cb, int64_t k, int rows_div, int stages, int smem_sketch, float cap, int cap_log2,
-                       int* err) {
+                       int n_cb, int groups, int64_t k, int rows_div, int stages, int smem_sketch, float cap,
+                       int cap_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -134,10 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* tile_max_bits = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tiles_per_row = (int64_t)n_ob * n_cb;
-  const int64_t units = (int64_t)n_rows * tiles_per_row;
-  const int64_t u_begin = units * blockIdx.x / gridDim.x;
-  const int64_t u_end = units * (blockIdx.x + 1) / gridDim.x;
+  // Job j = (candidate j / groups, o-block group j % groups) covers that
+  // group's o-blocks x all column blocks; CTA i takes jobs i, i + grid, ...,
+  // so the CTAs work on neighbouring candidates at any time and each
+  // candidate's operands stay L2-resident while they are read.
+  const int64_t n_jobs = (int64_t)n_rows * groups;
   const int n_kb = (seq_len + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -176,11 +190,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      for (int64_t u = u_begin; u < u_end; ++u) {
-        const int b = static_cast<int>(u / tiles_per_row);
-        const int rem = static_cast<int>(u % tiles_per_row);
-        const int ob = rem / n_cb, cb = rem % n_cb;
-        bool ok = true;
+      bool ok = true;
+      for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+      for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
+      for (int cb = 0; cb < n_cb && ok; ++cb) {
+        const int b = static_cast<int>(job / groups);
         for (int kb = 0; kb < n_kb; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err, kDevTimeoutProducer)) {
             ok = false;
@@ -199,7 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             ph ^= 1;
           }
         }
-        if (!ok) break;
       }
     }
   } else if (warp == 1) {
@@ -210,7 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int64_t u = u_begin; u < u_end && ok; ++u) {
+      for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+      for (int64_t u = 0; u < (int64_t)(job_ob_end(job, groups, n_ob) - job_ob_begin(job, groups, n_ob)) * n_cb && ok;
+           ++u) {
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, err, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
@@ -256,22 +271,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t aph = 0;
     uint32_t epi_phase = 0;
-    int64_t cur_b = -1;
+    int64_t cur_job = -1;
     int scale_exp = 0;      // fixed-point scale S = 2^scale_exp of the current candidate
     bool scaled = false;    // a scale has been chosen for the current candidate
     bool bad = false;
     bool ok = true;
-    for (int64_t u = u_begin; u < u_end; ++u) {
-      const int b = static_cast<int>(u / tiles_per_row);
-      const int64_t tile = u % tiles_per_row;
+    for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+    for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
+    for (int cb = 0; cb < n_cb && ok; ++cb) {
+      const int b = static_cast<int>(job / groups);
+      const int64_t tile = (int64_t)ob * n_cb + cb;
       float* out_row = phi + (int64_t)(b / rows_div) * k;
-      if (smem_sketch && b != cur_b) {
-        if (cur_b >= 0 && !flush_sketch(sk, phi + (cur_b / rows_div) * k, k, scale_exp, et, epi_bar, epi_phase,
-                                        abort_flag, err)) {
+      if (smem_sketch && job != cur_job) {
+        if (cur_job >= 0 && !flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k, scale_exp, et, epi_bar,
+                                          epi_phase, abort_flag, err)) {
           ok = false;
           break;
         }
-        cur_b = b;
+        cur_job = job;
         scaled = false;
       }
       if (!mbar_wait(&tfull[acc], aph, abort_flag, err, kDevTimeoutEpilogue)) {
@@ -286,12 +303,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m = 0.0f;
         for (int jj = 0; jj < kChunksPerWarp; ++jj) {
           const int j = half * kChunksPerWarp + jj;
+          uint4 ent[kPairsPerChunk];
+#pragma unroll
+          for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
           uint32_t v[32];
           tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
           tmem_ld_wait();
 #pragma unroll
           for (int p = 0; p < kPairsPerChunk; ++p) {
-            const uint4 e = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
+            const uint4 e = ent[p];
             const float x0 = fabsf(__uint_as_float(v[2 * p]) * __uint_as_float(e.z));
             const float x1 = fabsf(__uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w));
             if (x0 <= 3.0e38f) m = fmaxf(m, x0);   // finite values only
@@ -325,6 +345,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int jj = 0; jj < kChunksPerWarp; ++jj) {
         const int j = half * kChunksPerWarp + jj;
+        // all 16 table entries of the chunk in flight before the accumulator wait
+        uint4 ent[kPairsPerChunk];
+#pragma unroll
+        for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
         uint32_t v[32];
         tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
         tmem_ld_wait();
@@ -335,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int p = 0; p < kPairsPerChunk; ++p) {
-          const uint4 e = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
+          const uint4 e = ent[p];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t bucket = h ? e.y : e.x;
@@ -358,8 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         aph ^= 1;
       }
     }
-    if (ok && smem_sketch && cur_b >= 0)
-      flush_sketch(sk, phi + (cur_b / rows_div) * k, k, scale_exp, et, epi_bar, epi_phase, abort_flag, err);
+    if (ok && smem_sketch && cur_job >= 0)
+      flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k, scale_exp, et, epi_bar, epi_phase, abort_flag,
+                   err);
     if (bad) record_device_error(err, kDevBadBucket);
   }
 
@@ -456,12 +481,26 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
-  const int64_t units = (int64_t)n_rows * n_ob * n_cb;
-  const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
+  // Split each candidate's o-blocks into `groups` jobs so that the rounds of
+  // jobs over the SMs waste the least time: minimise ceil(jobs / SMs) x
+  // (o-blocks per job), preferring larger jobs on ties.
+  const int sms = sm_count();
+  int groups = 1;
+  int64_t best = -1;
+  for (int q = 1; q <= n_ob; ++q) {
+    const int64_t jobs = (int64_t)n_rows * q;
+    const int64_t cost = ((jobs + sms - 1) / sms) * ((n_ob + q - 1) / q);
+    if (best < 0 || cost < best) {
+      best = cost;
+      groups = q;
+    }
+  }
+  const int64_t n_jobs = (int64_t)n_rows * groups;
+  const int grid = static_cast<int>(n_jobs < sms ? n_jobs : sms);
   int* err = device_error_word();
   sketch_gemm_kernel<<<grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows,
-                                                        seq_len, n_ob, n_cb, k, rows_div, plan.stages, plan.smem_sketch,
-                                                        cap, cap_log2, err);
+                                                        seq_len, n_ob, n_cb, groups, k, rows_div, plan.stages,
+                                                        plan.smem_sketch, cap, cap_log2, err);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
