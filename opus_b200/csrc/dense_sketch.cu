@@ -12,60 +12,40 @@ constexpr int kDenseTile = 32;  // 32 x 32 (o, c) tiles
 
 // Grid-stride over 32x32 tiles of the [d_out, d_in] grid.  The weight tile is
 // read in its stored orientation (coalesced either way) and staged through
-// shared memory; the packed table is read row-major.  Scatter goes to a
-// CTA-private shared sketch (flushed with vector reductions) when it fits,
-// otherwise straight to global memory.
+// shared memory; the packed table is read row-major; every element is added
+// to its bucket with an f32 reduction in L2 (shared-memory float atomics are
+// compare-and-swap loops, and one matrix gives each bucket only ~numel/k
+// updates).
 __global__ void __launch_bounds__(kDenseThreads) dense_sketch_kernel(const float* __restrict__ w, int transposed,
                                                                      const uint32_t* __restrict__ packed,
                                                                      const float* __restrict__ diag, int d_out,
-                                                                     int d_in, int64_t k, float* __restrict__ out,
-                                                                     int smem_sketch) {
-  extern __shared__ float sk[];
+                                                                     int d_in, int64_t k, float* __restrict__ out) {
   __shared__ float tile_w[kDenseTile][kDenseTile + 1];
-  if (smem_sketch)
-    for (int64_t i = threadIdx.x; i < k; i += kDenseThreads) sk[i] = 0.0f;
-  __syncthreads();
-  float* dst = smem_sketch ? sk : out;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
   const int n_to = (d_out + kDenseTile - 1) / kDenseTile, n_tc = (d_in + kDenseTile - 1) / kDenseTile;
   const int64_t n_tiles = (int64_t)n_to * n_tc;
   for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
     const int o0 = static_cast<int>(t / n_tc) * kDenseTile, c0 = static_cast<int>(t % n_tc) * kDenseTile;
-    for (int rr = ty; rr < kDenseTile; rr += 8) {
-      if (!transposed) {
-        const int o = o0 + rr, c = c0 + tx;
-        tile_w[rr][tx] = (o < d_out && c < d_in) ? w[(int64_t)o * d_in + c] : 0.0f;
-      } else {
+    if (transposed) {
+      for (int rr = ty; rr < kDenseTile; rr += 8) {
         const int c = c0 + rr, o = o0 + tx;
         tile_w[tx][rr] = (o < d_out && c < d_in) ? w[(int64_t)c * d_out + o] : 0.0f;
       }
+      __syncthreads();
     }
-    __syncthreads();
     for (int rr = ty; rr < kDenseTile; rr += 8) {
       const int o = o0 + rr, c = c0 + tx;
       if (o < d_out && c < d_in) {
         const int64_t idx = (int64_t)o * d_in + c;
         const uint32_t hv = packed[idx];
-        float x = tile_w[rr][tx];
+        float x = transposed ? tile_w[rr][tx] : w[idx];
         if (diag != nullptr) x = x * diag[idx];
         if (hv & 0x80000000u) x = -x;
         const uint32_t bucket = hv & 0x7FFFFFFFu;
-        if (bucket < static_cast<uint64_t>(k)) atomicAdd(dst + bucket, x);
+        if (bucket < static_cast<uint64_t>(k)) atomicAdd(out + bucket, x);
       }
     }
-    __syncthreads();
-  }
-  if (smem_sketch) {
-    if ((k & 3) == 0) {
-      const float4* s4 = reinterpret_cast<const float4*>(sk);
-      for (int64_t i = threadIdx.x; i < k / 4; i += kDenseThreads) {
-        const float4 x = s4[i];
-        if (x.x != 0.0f || x.y != 0.0f || x.z != 0.0f || x.w != 0.0f) red_add_v4(out + 4 * i, x.x, x.y, x.z, x.w);
-      }
-    } else {
-      for (int64_t i = threadIdx.x; i < k; i += kDenseThreads)
-        if (sk[i] != 0.0f) atomicAdd(out + i, sk[i]);
-    }
+    if (transposed) __syncthreads();
   }
 }
 
@@ -124,19 +104,10 @@ int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, co
   if (!w || !packed || !sketch) return set_error(OPUS_ERR_INVALID, "sketch_dense: NULL pointer");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (!accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(sketch, 0, (size_t)k * sizeof(float), st));
-  const int64_t numel = (int64_t)d_out * d_in;
-  const size_t sk_bytes = (size_t)k * sizeof(float);
-  const int smem_sketch = sk_bytes <= 96 * 1024 ? 1 : 0;
   const int64_t n_tiles = (int64_t)((d_out + kDenseTile - 1) / kDenseTile) * ((d_in + kDenseTile - 1) / kDenseTile);
-  int64_t grid = smem_sketch ? numel / (2 * k) : (int64_t)sm_count() * 4;
-  if (grid < 1) grid = 1;
-  if (grid > 2 * sm_count()) grid = 2 * sm_count();
+  int64_t grid = (int64_t)sm_count() * 8;
   if (grid > n_tiles) grid = n_tiles;
-  const size_t dyn = smem_sketch ? sk_bytes : 0;
-  if (dyn > 48 * 1024)
-    OPUS_CUDA_TRY(cudaFuncSetAttribute(dense_sketch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
-  dense_sketch_kernel<<<(int)grid, kDenseThreads, dyn, st>>>(w, transposed, packed, diag, d_out, d_in, k, sketch,
-                                                              smem_sketch);
+  dense_sketch_kernel<<<(int)grid, kDenseThreads, 0, st>>>(w, transposed, packed, diag, d_out, d_in, k, sketch);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -1,6 +1,6 @@
 // Stage 5: Boltzmann (softmax-temperature) and greedy selection with the
-// interaction penalty, each on one 1024-thread CTA with the scores held in
-// shared memory.  The float32 / float64 operation order follows numpy so the
+// interaction penalty on one CTA with the scores held in shared memory (one
+// warp for up to 4096 candidates, 1024 threads above).  The float32 / float64 operation order follows numpy so the
 // same uniforms give the same indices as the host implementation:
 //   - scaled = score / T in float32, shifted by its max only if max > 700;
 //   - p = exp(scaled) rounded to float32 (computed in double);
@@ -30,10 +30,10 @@ struct SelShared {
   int leaf_start[kMaxLeaves];
   int leaf_len[kMaxLeaves];
   float leaf_sum[kMaxLeaves];
-  long long scan_ll[kSelThreads / 32];
-  double red_d[kSelThreads / 32];
-  int red_i[kSelThreads / 32];
-  float red_f[kSelThreads / 32];
+  long long scan_ll[32];
+  double red_d[32];
+  int red_i[32];
+  float red_f[32];
   int n_leaves;
   int m;
   float smax;
@@ -87,8 +87,10 @@ __device__ float pw_combine(int n, const SelShared& s, int& leaf) {
   return __fadd_rn(l, r);
 }
 
-// ---- block helpers (1024 threads = 32 warps)
+// ---- block helpers (NT threads = NT/32 warps, NT a power of two in [64, 1024])
+template <int NT>
 __device__ long long block_excl_scan_ll(long long v, SelShared& s, long long* total) {
+  constexpr int W = NT / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   long long x = v;
 #pragma unroll
@@ -99,48 +101,51 @@ __device__ long long block_excl_scan_ll(long long v, SelShared& s, long long* to
   if (lane == 31) s.scan_ll[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    long long w = s.scan_ll[lane];
+    long long w = lane < W ? s.scan_ll[lane] : 0;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const long long y = __shfl_up_sync(0xffffffffu, w, off);
       if (lane >= off) w += y;
     }
-    s.scan_ll[lane] = w;  // inclusive per-warp totals
+    if (lane < W) s.scan_ll[lane] = w;  // inclusive per-warp totals
   }
   __syncthreads();
   const long long before = (warp > 0 ? s.scan_ll[warp - 1] : 0) + (x - v);
-  if (total) *total = s.scan_ll[31];
+  if (total) *total = s.scan_ll[W - 1];
   __syncthreads();
   return before;
 }
 
-__device__ int block_sum_i(int v, SelShared& s) {
+// Sum of an int and a double over the block in one barrier pair.
+template <int NT>
+__device__ void block_sum_id(int& vi, double& vd, SelShared& s) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  if (lane == 0) s.red_i[warp] = v;
+  for (int off = 16; off > 0; off >>= 1) {
+    vi += __shfl_xor_sync(0xffffffffu, vi, off);
+    vd += __shfl_xor_sync(0xffffffffu, vd, off);
+  }
+  if (lane == 0) {
+    s.red_i[warp] = vi;
+    s.red_d[warp] = vd;
+  }
   __syncthreads();
-  int t = 0;
-  for (int i = 0; i < 32; ++i) t += s.red_i[i];
+  int ti = 0;
+  double td = 0.0;
+  for (int i = 0; i < NT / 32; ++i) {
+    ti += s.red_i[i];
+    td += s.red_d[i];
+  }
   __syncthreads();
-  return t;
+  vi = ti;
+  vd = td;
 }
 
-__device__ double block_sum_d(double v, SelShared& s) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  if (lane == 0) s.red_d[warp] = v;
-  __syncthreads();
-  double t = 0.0;
-  for (int i = 0; i < 32; ++i) t += s.red_d[i];
-  __syncthreads();
-  return t;
-}
-
-__global__ void __launch_bounds__(kSelThreads, 1)
+template <int NT>
+__global__ void __launch_bounds__(NT, 1)
     boltzmann_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
                      float temp, const double* __restrict__ uniforms, int64_t* __restrict__ out_idx, int* err) {
+  constexpr int kSelThreads = NT;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   SelShared& s = *reinterpret_cast<SelShared*>(sel_smem);
   const int tid = threadIdx.x;
@@ -153,27 +158,30 @@ __global__ void __launch_bounds__(kSelThreads, 1)
   const int lo = min(n, tid * per), hi = min(n, lo + per);
 
   for (int r = 0; r < n_select; ++r) {
-    // (1) compact available scores, scaled by 1/T in float32
+    const double u = uniforms[r];
+    // (1) compact available scores scaled by 1/T (float32) and take their exp
+    //     (no shift: the max only matters above 700, handled below)
     int cnt = 0;
     for (int i = lo; i < hi; ++i) cnt += s.avail[i];
     long long m_ll = 0;
-    int pos = static_cast<int>(block_excl_scan_ll(cnt, s, &m_ll));
+    const int base = static_cast<int>(block_excl_scan_ll<NT>(cnt, s, &m_ll));
     const int m = static_cast<int>(m_ll);
-    for (int i = lo; i < hi; ++i) {
-      if (s.avail[i]) {
-        s.pc[pos] = __fdiv_rn(s.scores[i], temp);
-        s.pidx[pos] = i;
-        ++pos;
-      }
-    }
-    __syncthreads();
-    // (2) max over scaled values (NaN anywhere -> np.max is NaN -> no shift)
     float lmax = -INFINITY;
     int lnan = 0;
-    for (int i = tid; i < m; i += kSelThreads) {
-      const float x = s.pc[i];
-      if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
+    {
+      int pos = base;
+      for (int i = lo; i < hi; ++i) {
+        if (s.avail[i]) {
+          const float x = __fdiv_rn(s.scores[i], temp);
+          s.cdf[pos] = x;   // scaled score, kept for the rare shifted recomputation
+          s.pc[pos] = static_cast<float>(exp(static_cast<double>(x)));
+          s.pidx[pos] = i;
+          ++pos;
+          if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
+        }
+      }
     }
+    // (2) max over scaled values (NaN anywhere -> np.max is NaN -> no shift)
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
@@ -187,7 +195,7 @@ __global__ void __launch_bounds__(kSelThreads, 1)
     if (tid == 0) {
       float mx = -INFINITY;
       int nn = 0;
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < NT / 32; ++i) {
         mx = fmaxf(mx, s.red_f[i]);
         nn |= s.red_i[i];
       }
@@ -197,17 +205,37 @@ __global__ void __launch_bounds__(kSelThreads, 1)
       pw_enumerate(0, m, s);
     }
     __syncthreads();
-    const bool shift = !s.any_nan && s.smax > 700.0f;
-    const float smax = s.smax;
-    // (3) p = exp(scaled) in float32
-    for (int i = tid; i < m; i += kSelThreads) {
-      float x = s.pc[i];
-      if (shift) x = __fsub_rn(x, smax);
-      s.pc[i] = static_cast<float>(exp(static_cast<double>(x)));
+    if (!s.any_nan && s.smax > 700.0f) {
+      // (3') x - max in float32 before the exp, as the reference does above 700
+      const float smax = s.smax;
+      for (int i = base; i < base + cnt; ++i)
+        s.pc[i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(static_cast<float>(s.cdf[i]), smax))));
+      __syncthreads();
     }
-    __syncthreads();
-    // (4) numpy pairwise sum: leaves in parallel, tree combine on one thread
-    if (tid < s.n_leaves) s.leaf_sum[tid] = pw_leaf(s.pc + s.leaf_start[tid], s.leaf_len[tid]);
+    // (4) numpy pairwise sum: leaves of <= 128 with 8 lanes each (lane j holds
+    //     accumulator r[j]; ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail;
+    //     shorter leaves are a plain running sum), tree combine on one thread
+    const int n_leaves = s.n_leaves;
+    for (int l0 = 0; l0 < n_leaves; l0 += NT / 8) {
+      const int leaf = l0 + (tid >> 3), j = tid & 7;
+      const bool active = leaf < n_leaves;
+      const int a0 = active ? s.leaf_start[leaf] : 0;
+      const int ln = active ? s.leaf_len[leaf] : 0;
+      const int full = ln >= 8 ? ln - (ln % 8) : 0;
+      float acc = 0.0f;
+      if (full >= 8) {
+        acc = s.pc[a0 + j];
+        for (int i = 8; i < full; i += 8) acc = __fadd_rn(acc, s.pc[a0 + i + j]);
+      }
+      const float p01 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+      const float p03 = __fadd_rn(p01, __shfl_xor_sync(0xffffffffu, p01, 2));
+      const float p07 = __fadd_rn(p03, __shfl_xor_sync(0xffffffffu, p03, 4));
+      if (active && j == 0) {
+        float res = full >= 8 ? p07 : 0.0f;
+        for (int i = full; i < ln; ++i) res = __fadd_rn(res, s.pc[a0 + i]);
+        s.leaf_sum[leaf] = res;
+      }
+    }
     __syncthreads();
     if (tid == 0) {
       int leaf = 0;
@@ -217,9 +245,8 @@ __global__ void __launch_bounds__(kSelThreads, 1)
     const float total = s.total;
     const bool uniform = (total == 0.0f) || !isfinite(total);
     const float inv_m = __fdiv_rn(1.0f, static_cast<float>(m));
-    // (5) normalise (contiguous ownership of compacted positions from here on)
-    const int pm = (m + kSelThreads - 1) / kSelThreads;
-    const int plo = min(m, tid * pm), phi_ = min(m, plo + pm);
+    // (5) normalise (each thread its own compacted range [base, base + cnt))
+    const int plo = base, phi_ = base + cnt;
     int not_exact = 0;
     long long fixed_sum = 0;
     double dsum = 0.0;
@@ -231,15 +258,14 @@ __global__ void __launch_bounds__(kSelThreads, 1)
       fixed_sum += static_cast<long long>(x);
       dsum += static_cast<double>(p);
     }
-    not_exact = block_sum_i(not_exact, s);
-    const double psum = block_sum_d(dsum, s);
+    block_sum_id<NT>(not_exact, dsum, s);
+    const double psum = dsum;
     // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32).
     if (tid == 0 && fabs(psum - 1.0) > 3.4526698300124393e-04) record_device_error(err, 0x301);
-    const double u = uniforms[r];
     int below = 0;
     if (!not_exact) {
       long long tot = 0;
-      long long run = block_excl_scan_ll(fixed_sum, s, &tot);
+      long long run = block_excl_scan_ll<NT>(fixed_sum, s, &tot);
       const double cdf_last = static_cast<double>(tot) * 0x1p-52;
       for (int i = plo; i < phi_; ++i) {
         run += static_cast<long long>(static_cast<double>(s.pc[i]) * 0x1p52);
@@ -259,13 +285,14 @@ __global__ void __launch_bounds__(kSelThreads, 1)
       const double cdf_last = s.cdf_total;
       for (int i = plo; i < phi_; ++i) below += (__ddiv_rn(s.cdf[i], cdf_last) <= u) ? 1 : 0;
     }
-    const int idx = block_sum_i(below, s);
+    double unused = 0.0;
+    block_sum_id<NT>(below, unused, s);
+    const int idx = below;
     const int sel = s.pidx[idx < m ? idx : m - 1];
     if (tid == 0) out_idx[r] = sel;
     // (6) interaction penalty on every score (float32), retire the pick
     const float* row = sim + (int64_t)sel * n;
     for (int i = tid; i < n; i += kSelThreads) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
-    __syncthreads();
     if (tid == 0) s.avail[sel] = 0;
     __syncthreads();
   }
@@ -347,9 +374,23 @@ int opus_boltzmann_select(const float* scores, const float* sim, int n, int n_se
   if (n_select == 0) return OPUS_OK;
   if (!scores || !sim || !uniforms || !out_idx) return set_error(OPUS_ERR_INVALID, "boltzmann: NULL pointer");
   const size_t smem = sizeof(SelShared);
-  OPUS_CUDA_TRY(cudaFuncSetAttribute(boltzmann_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  boltzmann_kernel<<<1, kSelThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      scores, sim, n, n_select, static_cast<float>(temperature), uniforms, out_idx, device_error_word());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float tf = static_cast<float>(temperature);
+  int* err = device_error_word();
+  // one candidate per thread up to 1024 candidates, then 1024 threads
+#define OPUS_LAUNCH_BOLTZMANN(NT)                                                                              \
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(boltzmann_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+  boltzmann_kernel<NT><<<1, NT, smem, st>>>(scores, sim, n, n_select, tf, uniforms, out_idx, err)
+  if (n <= 128) {
+    OPUS_LAUNCH_BOLTZMANN(128);
+  } else if (n <= 256) {
+    OPUS_LAUNCH_BOLTZMANN(256);
+  } else if (n <= 512) {
+    OPUS_LAUNCH_BOLTZMANN(512);
+  } else {
+    OPUS_LAUNCH_BOLTZMANN(1024);
+  }
+#undef OPUS_LAUNCH_BOLTZMANN
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -50,19 +50,24 @@ __global__ void __launch_bounds__(256) build_table_kernel(const uint32_t* __rest
   const int ob = tile / n_cb, cb = tile % n_cb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = cb * kTileN + j * kChunkCols + lane;
-  for (int r = warp; r < kTileM; r += 8) {
-    const int o = ob * kTileM + r;
-    uint32_t hv = 0;
-    float wv = 0.0f;
-    if (o < d_out && c < d_in) {
-      const int64_t idx = (int64_t)o * d_in + c;
-      hv = packed[idx];
-      const float d = element_weight(diag, v, eps, idx);
-      wv = (hv & 0x80000000u) ? -d : d;
-      hv &= 0x7FFFFFFFu;
-    }
-    sh[r][lane] = hv;
-    sw[r][lane] = wv;
+  // 16 rows per warp, all loads issued before any use
+  uint32_t hv[kTileM / 8];
+  float src[kTileM / 8];
+#pragma unroll
+  for (int i = 0; i < kTileM / 8; ++i) {
+    const int o = ob * kTileM + warp + 8 * i;
+    const bool in = o < d_out && c < d_in;
+    const int64_t idx = (int64_t)o * d_in + c;
+    hv[i] = in ? packed[idx] : 0u;
+    src[i] = in ? (diag != nullptr ? diag[idx] : (v != nullptr ? v[idx] : 1.0f)) : 0.0f;
+  }
+#pragma unroll
+  for (int i = 0; i < kTileM / 8; ++i) {
+    const int r = warp + 8 * i;
+    const float d = (diag == nullptr && v != nullptr) ? adam_diag(src[i], eps) : src[i];
+    const float wv = (hv[i] & 0x80000000u) ? -d : d;
+    sh[r][lane] = hv[i] & 0x7FFFFFFFu;
+    sw[r][lane] = (ob * kTileM + r < d_out && c < d_in) ? wv : 0.0f;
   }
   __syncthreads();
   uint4* out = table + ((int64_t)tile * kChunksPerTile + j) * (kPairsPerChunk * kTileM);
