@@ -1,7 +1,8 @@
 // Stage 5: Boltzmann (softmax-temperature) and greedy selection with the
-// interaction penalty on one CTA with the scores held in shared memory (one
-// warp for up to 4096 candidates, 1024 threads above).  The float32 / float64 operation order follows numpy so the
-// same uniforms give the same indices as the host implementation:
+// interaction penalty on one CTA with the scores held in shared memory (128
+// to 1024 threads, chosen by the candidate count).  The float32 / float64
+// operation order follows numpy so the same uniforms give the same indices as
+// the host implementation:
 //   - scaled = score / T in float32, shifted by its max only if max > 700;
 //   - p = exp(scaled) rounded to float32 (computed in double);
 //   - sum = numpy's pairwise float32 sum (0 + blocks of <=128 with 8
@@ -87,134 +88,92 @@ __device__ float pw_combine(int n, const SelShared& s, int& leaf) {
   return __fadd_rn(l, r);
 }
 
-// ---- block helpers (NT threads = NT/32 warps, NT a power of two in [64, 1024])
-template <int NT>
-__device__ long long block_excl_scan_ll(long long v, SelShared& s, long long* total) {
-  constexpr int W = NT / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  long long x = v;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const long long y = __shfl_up_sync(0xffffffffu, x, off);
-    if (lane >= off) x += y;
-  }
-  if (lane == 31) s.scan_ll[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    long long w = lane < W ? s.scan_ll[lane] : 0;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const long long y = __shfl_up_sync(0xffffffffu, w, off);
-      if (lane >= off) w += y;
-    }
-    if (lane < W) s.scan_ll[lane] = w;  // inclusive per-warp totals
-  }
-  __syncthreads();
-  const long long before = (warp > 0 ? s.scan_ll[warp - 1] : 0) + (x - v);
-  if (total) *total = s.scan_ll[W - 1];
-  __syncthreads();
-  return before;
-}
-
-// Sum of an int and a double over the block in one barrier pair.
-template <int NT>
-__device__ void block_sum_id(int& vi, double& vd, SelShared& s) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    vi += __shfl_xor_sync(0xffffffffu, vi, off);
-    vd += __shfl_xor_sync(0xffffffffu, vd, off);
-  }
-  if (lane == 0) {
-    s.red_i[warp] = vi;
-    s.red_d[warp] = vd;
-  }
-  __syncthreads();
-  int ti = 0;
-  double td = 0.0;
-  for (int i = 0; i < NT / 32; ++i) {
-    ti += s.red_i[i];
-    td += s.red_d[i];
-  }
-  __syncthreads();
-  vi = ti;
-  vd = td;
-}
-
+// Thread t owns the contiguous original indices [t*per, (t+1)*per), so the
+// compacted (available-only) order is thread order and then index order
+// inside a thread.  Each owned element keeps its compacted position, which
+// only moves down by one when an earlier element is picked.
 template <int NT>
 __global__ void __launch_bounds__(NT, 1)
     boltzmann_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
                      float temp, const double* __restrict__ uniforms, int64_t* __restrict__ out_idx, int* err) {
-  constexpr int kSelThreads = NT;
+  constexpr int W = NT / 32;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   SelShared& s = *reinterpret_cast<SelShared*>(sel_smem);
-  const int tid = threadIdx.x;
-  for (int i = tid; i < n; i += kSelThreads) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (n + NT - 1) / NT;
+  const int lo = min(n, tid * per), hi = min(n, lo + per);
+  for (int i = tid; i < n; i += NT) {
     s.scores[i] = scores_in[i];
     s.avail[i] = 1;
+    s.pidx[i] = i;         // compacted position -> original index (rewritten as picks retire)
   }
   __syncthreads();
-  const int per = (n + kSelThreads - 1) / kSelThreads;
-  const int lo = min(n, tid * per), hi = min(n, lo + per);
+  int m = n;               // available candidates
 
   for (int r = 0; r < n_select; ++r) {
     const double u = uniforms[r];
-    // (1) compact available scores scaled by 1/T (float32) and take their exp
-    //     (no shift: the max only matters above 700, handled below)
+    // (1) scaled scores of this thread's available elements, their max and
+    //     count; the exp lands at the compacted positions after barrier 2
     int cnt = 0;
     for (int i = lo; i < hi; ++i) cnt += s.avail[i];
-    long long m_ll = 0;
-    const int base = static_cast<int>(block_excl_scan_ll<NT>(cnt, s, &m_ll));
-    const int m = static_cast<int>(m_ll);
     float lmax = -INFINITY;
     int lnan = 0;
-    {
-      int pos = base;
-      for (int i = lo; i < hi; ++i) {
-        if (s.avail[i]) {
-          const float x = __fdiv_rn(s.scores[i], temp);
-          s.cdf[pos] = x;   // scaled score, kept for the rare shifted recomputation
-          s.pc[pos] = static_cast<float>(exp(static_cast<double>(x)));
-          s.pidx[pos] = i;
-          ++pos;
-          if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
-        }
-      }
+    for (int i = lo; i < hi; ++i) {
+      if (!s.avail[i]) continue;
+      const float x = __fdiv_rn(s.scores[i], temp);
+      s.cdf[i] = x;  // exp is taken after the max is known (shift above 700)
+      if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
     }
-    // (2) max over scaled values (NaN anywhere -> np.max is NaN -> no shift)
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
       lnan |= __shfl_xor_sync(0xffffffffu, lnan, off);
     }
-    if ((tid & 31) == 0) {
-      s.red_f[tid >> 5] = lmax;
-      s.red_i[tid >> 5] = lnan;
+    // compacted base of this thread = exclusive prefix of the per-thread counts
+    int wx = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wx, off);
+      if (lane >= off) wx += y;
     }
-    __syncthreads();
+    if (lane == 31) s.red_i[warp] = wx;
+    if (lane == 0) {
+      s.red_f[warp] = lmax;
+      s.scan_ll[warp] = lnan;
+    }
+    __syncthreads();                                                   // barrier 1
+    int base = wx - cnt;
+    for (int w = 0; w < warp; ++w) base += s.red_i[w];
     if (tid == 0) {
       float mx = -INFINITY;
       int nn = 0;
-      for (int i = 0; i < NT / 32; ++i) {
-        mx = fmaxf(mx, s.red_f[i]);
-        nn |= s.red_i[i];
+      for (int w = 0; w < W; ++w) {
+        mx = fmaxf(mx, s.red_f[w]);
+        nn |= static_cast<int>(s.scan_ll[w]);
       }
       s.smax = mx;
       s.any_nan = nn;
       s.n_leaves = 0;
       pw_enumerate(0, m, s);
     }
-    __syncthreads();
-    if (!s.any_nan && s.smax > 700.0f) {
-      // (3') x - max in float32 before the exp, as the reference does above 700
-      const float smax = s.smax;
-      for (int i = base; i < base + cnt; ++i)
-        s.pc[i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(static_cast<float>(s.cdf[i]), smax))));
-      __syncthreads();
+    __syncthreads();                                                   // barrier 2
+    const bool do_shift = !s.any_nan && s.smax > 700.0f;
+    const float smax = s.smax;
+    {
+      int pos = base;
+      for (int i = lo; i < hi; ++i) {
+        if (!s.avail[i]) continue;
+        float x = static_cast<float>(s.cdf[i]);
+        if (do_shift) x = __fsub_rn(x, smax);
+        s.pc[pos] = static_cast<float>(exp(static_cast<double>(x)));
+        s.pidx[pos] = i;
+        ++pos;
+      }
     }
-    // (4) numpy pairwise sum: leaves of <= 128 with 8 lanes each (lane j holds
-    //     accumulator r[j]; ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail;
-    //     shorter leaves are a plain running sum), tree combine on one thread
+    __syncthreads();                                                   // barrier 3
+    // (2) numpy pairwise sum: leaves of <= 128, 8 lanes each (lane j holds
+    //     accumulator r[j]; ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the
+    //     tail; shorter leaves are a running sum), tree combine on thread 0
     const int n_leaves = s.n_leaves;
     for (int l0 = 0; l0 < n_leaves; l0 += NT / 8) {
       const int leaf = l0 + (tid >> 3), j = tid & 7;
@@ -236,65 +195,94 @@ __global__ void __launch_bounds__(NT, 1)
         s.leaf_sum[leaf] = res;
       }
     }
-    __syncthreads();
+    __syncthreads();                                                   // barrier 4
     if (tid == 0) {
       int leaf = 0;
-      s.total = __fadd_rn(0.0f, pw_combine(m, s, leaf));
+      s.total = __fadd_rn(0.0f, n_leaves == 1 ? s.leaf_sum[0] : pw_combine(m, s, leaf));
+      s.pick = 0;
     }
-    __syncthreads();
+    __syncthreads();                                                   // barrier 5
     const float total = s.total;
     const bool uniform = (total == 0.0f) || !isfinite(total);
     const float inv_m = __fdiv_rn(1.0f, static_cast<float>(m));
-    // (5) normalise (each thread its own compacted range [base, base + cnt))
-    const int plo = base, phi_ = base + cnt;
+    // (3) normalise this thread's compacted range [base, base + cnt); exact
+    //     int64 running sum when every p is a multiple of 2^-52
     int not_exact = 0;
-    long long fixed_sum = 0;
+    long long fsum = 0;
     double dsum = 0.0;
-    for (int i = plo; i < phi_; ++i) {
+    for (int i = base; i < base + cnt; ++i) {
       const float p = uniform ? inv_m : __fdiv_rn(s.pc[i], total);
       s.pc[i] = p;
       const double x = static_cast<double>(p) * 0x1p52;
       if (x != trunc(x)) not_exact = 1;
-      fixed_sum += static_cast<long long>(x);
+      fsum += static_cast<long long>(x);
       dsum += static_cast<double>(p);
     }
-    block_sum_id<NT>(not_exact, dsum, s);
-    const double psum = dsum;
+    long long fx = fsum;
+    double dx = dsum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, fx, off);
+      if (lane >= off) fx += y;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      dx += __shfl_xor_sync(0xffffffffu, dx, off);
+      not_exact |= __shfl_xor_sync(0xffffffffu, not_exact, off);
+    }
+    if (lane == 31) s.scan_ll[warp] = fx;
+    if (lane == 0) {
+      s.red_d[warp] = dx;
+      s.red_i[warp] = not_exact;
+    }
+    __syncthreads();                                                   // barrier 6
+    long long fbase = fx - fsum;
+    long long ftot = 0;
+    double psum = 0.0;
+    int ne = 0;
+    for (int w = 0; w < W; ++w) {
+      if (w < warp) fbase += s.scan_ll[w];
+      ftot += s.scan_ll[w];
+      psum += s.red_d[w];
+      ne |= s.red_i[w];
+    }
     // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32).
     if (tid == 0 && fabs(psum - 1.0) > 3.4526698300124393e-04) record_device_error(err, 0x301);
     int below = 0;
-    if (!not_exact) {
-      long long tot = 0;
-      long long run = block_excl_scan_ll<NT>(fixed_sum, s, &tot);
-      const double cdf_last = static_cast<double>(tot) * 0x1p-52;
-      for (int i = plo; i < phi_; ++i) {
+    if (!ne) {
+      const double cdf_last = static_cast<double>(ftot) * 0x1p-52;
+      long long run = fbase;
+      for (int i = base; i < base + cnt; ++i) {
         run += static_cast<long long>(static_cast<double>(s.pc[i]) * 0x1p52);
-        const double c = __ddiv_rn(static_cast<double>(run) * 0x1p-52, cdf_last);
-        below += (c <= u) ? 1 : 0;
+        below += (__ddiv_rn(static_cast<double>(run) * 0x1p-52, cdf_last) <= u) ? 1 : 0;
       }
     } else {
       if (tid == 0) {
         double acc = 0.0;
         for (int i = 0; i < m; ++i) {
           acc = __dadd_rn(acc, static_cast<double>(s.pc[i]));
-          s.cdf[i] = acc;
+          s.cdf[i] = acc;   // scaled scores are no longer needed in this draw
         }
         s.cdf_total = acc;
       }
       __syncthreads();
       const double cdf_last = s.cdf_total;
-      for (int i = plo; i < phi_; ++i) below += (__ddiv_rn(s.cdf[i], cdf_last) <= u) ? 1 : 0;
+      for (int i = base; i < base + cnt; ++i) below += (__ddiv_rn(s.cdf[i], cdf_last) <= u) ? 1 : 0;
     }
-    double unused = 0.0;
-    block_sum_id<NT>(below, unused, s);
-    const int idx = below;
-    const int sel = s.pidx[idx < m ? idx : m - 1];
+    // (4) searchsorted(side='right') = number of cdf entries <= u
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) below += __shfl_xor_sync(0xffffffffu, below, off);
+    if (lane == 0 && below) atomicAdd(&s.pick, below);
+    __syncthreads();                                                   // barrier 7
+    const int idx = min(s.pick, m - 1);
+    const int sel = s.pidx[idx];
     if (tid == 0) out_idx[r] = sel;
-    // (6) interaction penalty on every score (float32), retire the pick
+    // (5) interaction penalty on every score (float32), retire the pick
     const float* row = sim + (int64_t)sel * n;
-    for (int i = tid; i < n; i += kSelThreads) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
+    for (int i = tid; i < n; i += NT) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
     if (tid == 0) s.avail[sel] = 0;
-    __syncthreads();
+    --m;
+    __syncthreads();                                                   // barrier 8
   }
 }
 
