@@ -10,8 +10,10 @@
 //   - p /= sum in float32, or 1/m when the sum is 0 or not finite;
 //   - cdf = float64 running sum, cdf /= cdf[-1], idx = #{cdf <= u}.
 // The float64 running sum is evaluated exactly with an int64 scan whenever
-// every p is a multiple of 2^-52 (then no partial sum rounds); otherwise one
-// thread runs the sequential float64 recurrence.
+// every p is a multiple of 2^-52 (then no partial sum rounds), and the
+// division by cdf[-1] with the comparison against u becomes one integer
+// threshold per draw; otherwise one thread runs the sequential float64
+// recurrence and every element is divided.
 #include "opus_common.cuh"
 
 namespace opus {
@@ -20,7 +22,11 @@ namespace {
 constexpr int kSelThreads = 1024;
 constexpr int kSelMax = 8192;
 constexpr int kPwBlock = 128;
-constexpr int kMaxLeaves = 256;
+// numpy splits a length-m sum at m/2 rounded down to a multiple of 8 until a
+// piece is <= 128 long; for m <= 8192 the pieces at depth 7 are <= 79 long,
+// so the split tree has at most 8 levels of at most 128 nodes.
+constexpr int kLevels = 8;
+constexpr int kLevelSlots = 128;
 
 struct SelShared {
   double cdf[kSelMax];
@@ -28,70 +34,117 @@ struct SelShared {
   float pc[kSelMax];
   int pidx[kSelMax];
   unsigned char avail[kSelMax];
-  int leaf_start[kMaxLeaves];
-  int leaf_len[kMaxLeaves];
-  float leaf_sum[kMaxLeaves];
+  int lvl_start[kLevels][kLevelSlots];
+  int lvl_len[kLevels][kLevelSlots];   // 0 = no node in this slot
+  float lvl_sum[kLevels][kLevelSlots];
+  int leaf_slot[kLevels * kLevelSlots];  // (level << 7) | slot of every leaf
+  int n_leaves;
+  int tree_depth;
   long long scan_ll[32];
   double red_d[32];
   int red_i[32];
+  int red_ne[32];
+  int red_cnt[32];
   float red_f[32];
-  int n_leaves;
-  int m;
-  float smax;
-  int any_nan;
+  int red_nan[32];
   float total;
-  int not_exact;
   double cdf_total;
-  int pick;
 };
 
-// ---- numpy pairwise float32 sum
-__device__ float pw_leaf(const float* a, int n) {
-  if (n < 8) {
-    float res = 0.0f;
-    for (int i = 0; i < n; ++i) res = __fadd_rn(res, a[i]);
-    return res;
+// ---- numpy pairwise float32 sum, as a split tree built level by level
+// One warp: the node in slot j of level d has children in slots 2j, 2j+1 of
+// level d+1 (left piece first, as numpy adds left + right).
+__device__ void pw_tree_build(int m, SelShared& s, int lane) {
+  if (lane == 0) {
+    s.lvl_start[0][0] = 0;
+    s.lvl_len[0][0] = m;
   }
-  float r[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = a[j];
-  int i = 8;
-  for (; i < n - (n % 8); i += 8) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], a[i + j]);
+  int nl = 0, depth = kLevels - 1;
+  for (int d = 0; d < kLevels; ++d) {
+    __syncwarp();
+    const int width = 1 << d;
+    bool more = false;
+    for (int j0 = 0; j0 < width; j0 += 32) {
+      const int j = j0 + lane;
+      const int len = j < width ? s.lvl_len[d][j] : 0;
+      const bool leaf = len > 0 && len <= kPwBlock;
+      if (d + 1 < kLevels && j < width) {
+        const int start = s.lvl_start[d][j];
+        int n2 = 0;
+        if (len > kPwBlock) {
+          n2 = len / 2;
+          n2 -= n2 % 8;
+        }
+        s.lvl_start[d + 1][2 * j] = start;
+        s.lvl_len[d + 1][2 * j] = n2;
+        s.lvl_start[d + 1][2 * j + 1] = start + n2;
+        s.lvl_len[d + 1][2 * j + 1] = len > kPwBlock ? len - n2 : 0;
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, leaf);
+      if (leaf) s.leaf_slot[nl + __popc(bal & ((1u << lane) - 1u))] = (d << 7) | j;
+      nl += __popc(bal);
+      more |= __any_sync(0xffffffffu, len > kPwBlock);
+    }
+    if (!more) {
+      depth = d;  // deepest level holding a node
+      break;
+    }
   }
-  float res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
-                        __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
-  for (; i < n; ++i) res = __fadd_rn(res, a[i]);
-  return res;
+  if (lane == 0) {
+    s.n_leaves = nl;
+    s.tree_depth = depth;
+  }
 }
 
-__device__ void pw_enumerate(int a, int n, SelShared& s) {
-  if (n <= kPwBlock) {
-    s.leaf_start[s.n_leaves] = a;
-    s.leaf_len[s.n_leaves] = n;
-    s.n_leaves++;
-    return;
+// One warp, after every leaf sum is in lvl_sum: internal nodes bottom-up.
+__device__ float pw_tree_sum(SelShared& s, int lane) {
+  for (int d = s.tree_depth - 1; d >= 0; --d) {
+    __syncwarp();
+    const int width = 1 << d;
+    for (int j = lane; j < width; j += 32)
+      if (s.lvl_len[d][j] > kPwBlock) s.lvl_sum[d][j] = __fadd_rn(s.lvl_sum[d + 1][2 * j], s.lvl_sum[d + 1][2 * j + 1]);
   }
-  int n2 = n / 2;
-  n2 -= n2 % 8;
-  pw_enumerate(a, n2, s);
-  pw_enumerate(a + n2, n - n2, s);
+  __syncwarp();
+  return s.lvl_sum[0][0];
 }
 
-__device__ float pw_combine(int n, const SelShared& s, int& leaf) {
-  if (n <= kPwBlock) return s.leaf_sum[leaf++];
-  int n2 = n / 2;
-  n2 -= n2 % 8;
-  const float l = pw_combine(n2, s, leaf);
-  const float r = pw_combine(n - n2, s, leaf);
-  return __fadd_rn(l, r);
+__device__ __forceinline__ unsigned long long shr128(unsigned long long h, unsigned long long l, int k) {
+  if (k >= 128) return 0ull;
+  if (k >= 64) return h >> (k - 64);
+  if (k == 0) return l;
+  return (l >> k) | (h << (64 - k));
 }
 
-// Thread t owns the contiguous original indices [t*per, (t+1)*per), so the
-// compacted (available-only) order is thread order and then index order
-// inside a thread.  Each owned element keeps its compacted position, which
-// only moves down by one when an earlier element is picked.
+// For integers 0 <= X < 2^53 and 0 < L < 2^54: the largest X with
+// RN(X / L) <= u in float64 (-1 if none).  RN(q) <= u holds exactly when q is
+// below the midpoint (2U+1) * 2^(e-1) between u = U * 2^e and its successor,
+// or equal to it with U even (ties to even); with R = (2U+1) * L that is
+// X * 2^(1-e) < R (or == R), evaluated in 128-bit integers.
+__device__ long long cdf_threshold(double u, long long L) {
+  if (isnan(u) || u < 0.0) return -1;
+  if (u >= 1.0) return 0x7fffffffffffffffll;
+  if (u == 0.0) return 0;
+  const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(u));
+  const int ex = static_cast<int>((bits >> 52) & 0x7ff);
+  if (ex == 0) return 0;  // subnormal u: X / L >= 2^-54 for every X >= 1
+  const unsigned long long U = (bits & 0xFFFFFFFFFFFFFull) | (1ull << 52);
+  const int sh = 1076 - ex;
+  const unsigned long long a = 2 * U + 1;
+  const unsigned long long lo = a * static_cast<unsigned long long>(L);
+  const unsigned long long hi = __umul64hi(a, static_cast<unsigned long long>(L));
+  unsigned long long t = shr128(hi - (lo == 0 ? 1ull : 0ull), lo - 1ull, sh);
+  if ((U & 1ull) == 0 && sh < 128) {
+    const bool tie = sh >= 64 ? (lo == 0 && (hi & ((1ull << (sh - 64)) - 1ull)) == 0)
+                              : (lo & ((1ull << sh) - 1ull)) == 0;
+    if (tie) t = shr128(hi, lo, sh);
+  }
+  return static_cast<long long>(t);
+}
+
+// Thread t owns the contiguous original indices [t*per, (t+1)*per): their
+// scores, availability and interaction penalties, so no barrier separates one
+// draw from the next.  The compacted (available-only) order is thread order,
+// then index order inside a thread.
 template <int NT>
 __global__ void __launch_bounds__(NT, 1)
     boltzmann_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
@@ -102,26 +155,24 @@ __global__ void __launch_bounds__(NT, 1)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = (n + NT - 1) / NT;
   const int lo = min(n, tid * per), hi = min(n, lo + per);
-  for (int i = tid; i < n; i += NT) {
+  for (int i = lo; i < hi; ++i) {
     s.scores[i] = scores_in[i];
     s.avail[i] = 1;
-    s.pidx[i] = i;         // compacted position -> original index (rewritten as picks retire)
   }
-  __syncthreads();
-  int m = n;               // available candidates
 
   for (int r = 0; r < n_select; ++r) {
+    const int m = n - r;  // available candidates
     const double u = uniforms[r];
-    // (1) scaled scores of this thread's available elements, their max and
-    //     count; the exp lands at the compacted positions after barrier 2
+    // (1) scaled scores of the owned available elements, their max and count;
+    //     warp 0 also lays out the pairwise-sum tree for m elements
     int cnt = 0;
-    for (int i = lo; i < hi; ++i) cnt += s.avail[i];
     float lmax = -INFINITY;
     int lnan = 0;
     for (int i = lo; i < hi; ++i) {
       if (!s.avail[i]) continue;
+      ++cnt;
       const float x = __fdiv_rn(s.scores[i], temp);
-      s.cdf[i] = x;  // exp is taken after the max is known (shift above 700)
+      s.cdf[i] = x;
       if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
     }
 #pragma unroll
@@ -129,7 +180,6 @@ __global__ void __launch_bounds__(NT, 1)
       lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
       lnan |= __shfl_xor_sync(0xffffffffu, lnan, off);
     }
-    // compacted base of this thread = exclusive prefix of the per-thread counts
     int wx = cnt;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -139,26 +189,36 @@ __global__ void __launch_bounds__(NT, 1)
     if (lane == 31) s.red_i[warp] = wx;
     if (lane == 0) {
       s.red_f[warp] = lmax;
-      s.scan_ll[warp] = lnan;
+      s.red_nan[warp] = lnan;
     }
+    if (warp == 0) pw_tree_build(m, s, lane);
     __syncthreads();                                                   // barrier 1
-    int base = wx - cnt;
-    for (int w = 0; w < warp; ++w) base += s.red_i[w];
-    if (tid == 0) {
-      float mx = -INFINITY;
-      int nn = 0;
-      for (int w = 0; w < W; ++w) {
-        mx = fmaxf(mx, s.red_f[w]);
-        nn |= static_cast<int>(s.scan_ll[w]);
+    // (2) every warp combines the per-warp partials itself: compacted base,
+    //     max, NaN flag; then exp at the compacted positions (shifted by the
+    //     max only above 700, as the reference does)
+    int base;
+    float smax;
+    bool any_nan;
+    {
+      const int ci = lane < W ? s.red_i[lane] : 0;
+      int incl = ci;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
       }
-      s.smax = mx;
-      s.any_nan = nn;
-      s.n_leaves = 0;
-      pw_enumerate(0, m, s);
+      base = __shfl_sync(0xffffffffu, incl - ci, warp) + (wx - cnt);
+      float mx = lane < W ? s.red_f[lane] : -INFINITY;
+      int nn = lane < W ? s.red_nan[lane] : 0;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        nn |= __shfl_xor_sync(0xffffffffu, nn, off);
+      }
+      smax = mx;
+      any_nan = nn != 0;
     }
-    __syncthreads();                                                   // barrier 2
-    const bool do_shift = !s.any_nan && s.smax > 700.0f;
-    const float smax = s.smax;
+    const bool do_shift = !any_nan && smax > 700.0f;
     {
       int pos = base;
       for (int i = lo; i < hi; ++i) {
@@ -170,16 +230,18 @@ __global__ void __launch_bounds__(NT, 1)
         ++pos;
       }
     }
-    __syncthreads();                                                   // barrier 3
-    // (2) numpy pairwise sum: leaves of <= 128, 8 lanes each (lane j holds
-    //     accumulator r[j]; ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the
-    //     tail; shorter leaves are a running sum), tree combine on thread 0
+    __syncthreads();                                                   // barrier 2
+    // (3) leaf sums, 8 lanes per leaf: lane j holds numpy's accumulator r[j],
+    //     combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail;
+    //     leaves shorter than 8 are a running sum from 0
     const int n_leaves = s.n_leaves;
     for (int l0 = 0; l0 < n_leaves; l0 += NT / 8) {
       const int leaf = l0 + (tid >> 3), j = tid & 7;
       const bool active = leaf < n_leaves;
-      const int a0 = active ? s.leaf_start[leaf] : 0;
-      const int ln = active ? s.leaf_len[leaf] : 0;
+      const int slot = active ? s.leaf_slot[leaf] : 0;
+      const int d = slot >> 7, sj = slot & (kLevelSlots - 1);
+      const int a0 = active ? s.lvl_start[d][sj] : 0;
+      const int ln = active ? s.lvl_len[d][sj] : 0;
       const int full = ln >= 8 ? ln - (ln % 8) : 0;
       float acc = 0.0f;
       if (full >= 8) {
@@ -192,21 +254,21 @@ __global__ void __launch_bounds__(NT, 1)
       if (active && j == 0) {
         float res = full >= 8 ? p07 : 0.0f;
         for (int i = full; i < ln; ++i) res = __fadd_rn(res, s.pc[a0 + i]);
-        s.leaf_sum[leaf] = res;
+        s.lvl_sum[d][sj] = res;
       }
     }
-    __syncthreads();                                                   // barrier 4
-    if (tid == 0) {
-      int leaf = 0;
-      s.total = __fadd_rn(0.0f, n_leaves == 1 ? s.leaf_sum[0] : pw_combine(m, s, leaf));
-      s.pick = 0;
+    __syncthreads();                                                   // barrier 3
+    if (warp == 0) {
+      const float root = pw_tree_sum(s, lane);
+      if (lane == 0) s.total = __fadd_rn(0.0f, root);
     }
-    __syncthreads();                                                   // barrier 5
+    __syncthreads();                                                   // barrier 4
     const float total = s.total;
     const bool uniform = (total == 0.0f) || !isfinite(total);
     const float inv_m = __fdiv_rn(1.0f, static_cast<float>(m));
-    // (3) normalise this thread's compacted range [base, base + cnt); exact
-    //     int64 running sum when every p is a multiple of 2^-52
+    // (4) normalise the owned compacted range [base, base + cnt); p * 2^52
+    //     is an integer for every p >= 2^-29, and then the float64 running
+    //     sum is exact and equals an int64 scan
     int not_exact = 0;
     long long fsum = 0;
     double dsum = 0.0;
@@ -219,7 +281,6 @@ __global__ void __launch_bounds__(NT, 1)
       dsum += static_cast<double>(p);
     }
     long long fx = fsum;
-    double dx = dsum;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const long long y = __shfl_up_sync(0xffffffffu, fx, off);
@@ -227,41 +288,53 @@ __global__ void __launch_bounds__(NT, 1)
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
-      dx += __shfl_xor_sync(0xffffffffu, dx, off);
+      dsum += __shfl_xor_sync(0xffffffffu, dsum, off);
       not_exact |= __shfl_xor_sync(0xffffffffu, not_exact, off);
     }
     if (lane == 31) s.scan_ll[warp] = fx;
     if (lane == 0) {
-      s.red_d[warp] = dx;
-      s.red_i[warp] = not_exact;
+      s.red_d[warp] = dsum;
+      s.red_ne[warp] = not_exact;
     }
-    __syncthreads();                                                   // barrier 6
-    long long fbase = fx - fsum;
-    long long ftot = 0;
-    double psum = 0.0;
-    int ne = 0;
-    for (int w = 0; w < W; ++w) {
-      if (w < warp) fbase += s.scan_ll[w];
-      ftot += s.scan_ll[w];
-      psum += s.red_d[w];
-      ne |= s.red_i[w];
+    __syncthreads();                                                   // barrier 5
+    long long fbase, ftot;
+    bool exact;
+    {
+      const long long wt = lane < W ? s.scan_ll[lane] : 0;
+      long long incl = wt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const long long y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      fbase = __shfl_sync(0xffffffffu, incl - wt, warp) + (fx - fsum);
+      ftot = __shfl_sync(0xffffffffu, incl, 31);
+      double pd = lane < W ? s.red_d[lane] : 0.0;
+      int ne = lane < W ? s.red_ne[lane] : 0;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        pd += __shfl_xor_sync(0xffffffffu, pd, off);
+        ne |= __shfl_xor_sync(0xffffffffu, ne, off);
+      }
+      exact = ne == 0;
+      // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32).
+      if (tid == 0 && fabs(pd - 1.0) > 3.4526698300124393e-04) record_device_error(err, 0x301);
     }
-    // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32).
-    if (tid == 0 && fabs(psum - 1.0) > 3.4526698300124393e-04) record_device_error(err, 0x301);
+    // (5) searchsorted(cdf / cdf[-1], u, 'right') = #{cdf entries <= u}
     int below = 0;
-    if (!ne) {
-      const double cdf_last = static_cast<double>(ftot) * 0x1p-52;
+    if (exact) {
+      const long long thr = cdf_threshold(u, ftot);
       long long run = fbase;
       for (int i = base; i < base + cnt; ++i) {
         run += static_cast<long long>(static_cast<double>(s.pc[i]) * 0x1p52);
-        below += (__ddiv_rn(static_cast<double>(run) * 0x1p-52, cdf_last) <= u) ? 1 : 0;
+        below += run <= thr ? 1 : 0;
       }
     } else {
       if (tid == 0) {
         double acc = 0.0;
         for (int i = 0; i < m; ++i) {
           acc = __dadd_rn(acc, static_cast<double>(s.pc[i]));
-          s.cdf[i] = acc;   // scaled scores are no longer needed in this draw
+          s.cdf[i] = acc;  // the scaled scores of this draw are consumed
         }
         s.cdf_total = acc;
       }
@@ -269,20 +342,20 @@ __global__ void __launch_bounds__(NT, 1)
       const double cdf_last = s.cdf_total;
       for (int i = base; i < base + cnt; ++i) below += (__ddiv_rn(s.cdf[i], cdf_last) <= u) ? 1 : 0;
     }
-    // (4) searchsorted(side='right') = number of cdf entries <= u
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) below += __shfl_xor_sync(0xffffffffu, below, off);
-    if (lane == 0 && below) atomicAdd(&s.pick, below);
-    __syncthreads();                                                   // barrier 7
-    const int idx = min(s.pick, m - 1);
-    const int sel = s.pidx[idx];
+    if (lane == 0) s.red_cnt[warp] = below;
+    __syncthreads();                                                   // barrier 6
+    int pick = lane < W ? s.red_cnt[lane] : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) pick += __shfl_xor_sync(0xffffffffu, pick, off);
+    const int sel = s.pidx[min(pick, m - 1)];
     if (tid == 0) out_idx[r] = sel;
-    // (5) interaction penalty on every score (float32), retire the pick
+    // (6) interaction penalty on every owned score (float32); the owner of
+    //     the pick retires it
     const float* row = sim + (int64_t)sel * n;
-    for (int i = tid; i < n; i += NT) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
-    if (tid == 0) s.avail[sel] = 0;
-    --m;
-    __syncthreads();                                                   // barrier 8
+    for (int i = lo; i < hi; ++i) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
+    if (sel >= lo && sel < hi) s.avail[sel] = 0;
   }
 }
 

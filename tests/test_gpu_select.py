@@ -56,6 +56,39 @@ def test_boltzmann_matches_oracle_random(n, K, temp, spread):
     assert got == want
 
 
+@pytest.mark.parametrize("n,temp,spread", [(200, 1.0, 1.0), (1000, 0.5, 4.0), (3000, 1.0, 0.1)])
+def test_boltzmann_uniform_on_cdf_boundaries(n, temp, spread):
+    """u exactly on, just below and just above normalised cdf entries (searchsorted 'right').
+
+    numpy's SIMD float32 exp is not correctly rounded (on AVX-512 hosts about
+    a third of inputs come out one ulp away), while the kernel's is; u placed
+    on a cdf entry sees every such ulp, so the scores here are drawn where the
+    two agree and the test isolates the cdf search.
+    """
+    rng = np.random.default_rng(7 * n)
+    sc = (rng.standard_normal(4 * n) * spread).astype(np.float32)
+    xs = sc / np.float32(temp)
+    sc = sc[np.exp(xs) == np.exp(xs.astype(np.float64)).astype(np.float32)][:n]
+    assert sc.size == n
+    sim = np.zeros((n, n), np.float32)
+    x = sc / np.float32(temp)
+    p = np.exp(x)
+    p /= p.sum()
+    cdf = p.astype(np.float64).cumsum()
+    cdf /= cdf[-1]
+    us = [0.0, np.nextafter(1.0, 0.0), float(cdf[0]), float(cdf[-2])]
+    for j in rng.integers(0, n - 1, 12):
+        c = float(cdf[j])
+        us += [c, float(np.nextafter(c, 0.0)), float(np.nextafter(c, 1.0))]
+    uni = torch.tensor(us, dtype=torch.float64, device=DEV)
+    s_d, sim_d = dev(sc), dev(sim)
+    for i, u in enumerate(us):
+        want = orc.stochastic_greedy_selection(sc, sim, 1, temperature=temp, uniforms=[u])
+        got = ops.boltzmann_select(s_d, sim_d, 1, temp, uni[i:i + 1]).cpu().tolist()
+        assert got == want, (i, u)
+    ops.check_device_error("boltzmann")
+
+
 def test_public_stochastic_selection_uses_numpy_stream():
     g = load_golden("select")
     np.random.seed(1000)
