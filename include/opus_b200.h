@@ -69,6 +69,18 @@ OPUS_API int opus_device_error(int* code);
 OPUS_API int opus_pack_hash_sign(const int64_t* hash, const float* sign, int64_t numel, int64_t k,
                         uint32_t* packed, void* stream);
 
+/*
+ * H1 — per-bucket element counts of a packed table and their maximum.
+ * opus_sketch_gemm sizes its int32 fixed-point shared-memory sketch by the
+ * largest bucket load.  The reference has no such step: its scatter_add_
+ * (OPUS/train/random_projection.py:317) accumulates in f32 and needs no bound.
+ *   counts: caller-owned scratch of counts_len >= k int32, zeroed here and
+ *           left holding the histogram; out_max: one int64 on the device.
+ * A bucket outside [0,k) is skipped and reported through opus_device_error.
+ */
+OPUS_API int opus_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int* counts,
+                                  int64_t counts_len, int64_t* out_max, void* stream);
+
 /* Number of 16-byte entries of the tiled epilogue table for a [d_out,d_in] layer. */
 OPUS_API int64_t opus_sketch_table_entries(int d_out, int d_in);
 

@@ -3,6 +3,7 @@
 //   opus_pack_hash_sign     int64 bucket + f32 sign  ->  uint32 (bucket | neg<<31)
 //   opus_build_sketch_table packed + AdamW diag      ->  tiled epilogue table
 //   opus_desketch           tau + packed + diag      ->  dense bf16 hi/lo target
+//   opus_bucket_max_load    packed                   ->  per-bucket counts, their max
 #include "opus_common.cuh"
 #include "sketch_layout.cuh"
 
@@ -105,6 +106,99 @@ int grid_for(int64_t n, int threads) {
   return static_cast<int>(g);
 }
 
+// Per-bucket element counts of a packed table.  Up to kHistSmemBuckets
+// buckets each CTA counts into shared memory (native int32 shared atomics) and
+// adds its nonzero bins to the global counts once; larger sketches count
+// straight into the global array (L2 atomics).  An entry whose bucket is not
+// below k is skipped and recorded as kDevBadBucket.
+constexpr int kHistThreads = 512;
+constexpr int kHistSmemBuckets = 32768;  // 128 KB of shared counts
+
+template <bool kShared>
+__global__ void __launch_bounds__(kHistThreads) bucket_hist_kernel(const uint32_t* __restrict__ packed, int64_t numel,
+                                                                  uint32_t k, int* __restrict__ counts, int* err) {
+  extern __shared__ int sh_counts[];
+  if (kShared) {
+    for (uint32_t i = threadIdx.x; i < k; i += blockDim.x) sh_counts[i] = 0;
+    __syncthreads();
+  }
+  int* dst = kShared ? sh_counts : counts;
+  bool bad = false;
+  auto count = [&](uint32_t v) {
+    const uint32_t b = v & 0x7FFFFFFFu;
+    if (b < k) atomicAdd(dst + b, 1); else bad = true;
+  };
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // 16-byte loads over the aligned body, scalar loads over the rest
+  const int64_t mis = static_cast<int64_t>(reinterpret_cast<uintptr_t>(packed) & 15);
+  int64_t head = mis == 0 ? 0 : (16 - mis) / 4;
+  if (head > numel) head = numel;
+  const int64_t n4 = (numel - head) / 4;
+  const uint4* p4 = reinterpret_cast<const uint4*>(packed + head);
+  for (int64_t i = tid; i < n4; i += stride) {
+    const uint4 v = __ldg(p4 + i);
+    count(v.x);
+    count(v.y);
+    count(v.z);
+    count(v.w);
+  }
+  for (int64_t i = tid; i < head; i += stride) count(packed[i]);
+  for (int64_t i = head + n4 * 4 + tid; i < numel; i += stride) count(packed[i]);
+  if (bad) record_device_error(err, kDevBadBucket);
+  if (kShared) {
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < k; i += blockDim.x) {
+      const int c = sh_counts[i];
+      if (c) atomicAdd(counts + i, c);
+    }
+  }
+}
+
+// One CTA: max over the k counts.
+__global__ void __launch_bounds__(1024) bucket_max_kernel(const int* __restrict__ counts, int64_t k,
+                                                          int64_t* __restrict__ out) {
+  int mx = 0;
+  for (int64_t i = threadIdx.x; i < k; i += 1024) mx = max(mx, counts[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  __shared__ int part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    mx = part[threadIdx.x];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (threadIdx.x == 0) *out = mx;
+  }
+}
+
+// Counts (zeroed here) then their max; counts holds the histogram afterwards.
+int launch_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int* counts, int64_t* out_max,
+                           cudaStream_t st) {
+  OPUS_CUDA_TRY(cudaMemsetAsync(counts, 0, (size_t)k * sizeof(int), st));
+  if (numel > 0) {
+    int* err = device_error_word();
+    if (k <= kHistSmemBuckets) {
+      // enough CTAs to stream the table, few enough that the k-bin flushes stay
+      // well below the element count
+      int64_t grid = numel / (8 * k);
+      grid = grid < 1 ? 1 : (grid > sm_count() ? sm_count() : grid);
+      const size_t smem = (size_t)k * sizeof(int);
+      OPUS_CUDA_TRY(cudaFuncSetAttribute(bucket_hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+      bucket_hist_kernel<true><<<(int)grid, kHistThreads, smem, st>>>(packed, numel, (uint32_t)k, counts, err);
+    } else {
+      bucket_hist_kernel<false><<<grid_for(numel / 4 + 1, kHistThreads), kHistThreads, 0, st>>>(
+          packed, numel, (uint32_t)k, counts, err);
+    }
+    OPUS_CUDA_TRY(cudaGetLastError());
+  }
+  bucket_max_kernel<<<1, 1024, 0, st>>>(counts, k, out_max);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
 }  // namespace
 }  // namespace opus
 
@@ -154,6 +248,16 @@ int opus_desketch(const float* tau, const uint32_t* packed, const float* diag, c
                                                                           scale, hi, hi + numel);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
+}
+
+int opus_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int* counts, int64_t counts_len,
+                         int64_t* out_max, void* stream) {
+  if (numel < 0 || k <= 0 || k > 0x7FFFFFFF) return set_error(OPUS_ERR_INVALID, "bucket_max_load: bad numel/k");
+  if (counts_len < k)
+    return set_error(OPUS_ERR_INVALID, "bucket_max_load: counts holds %lld entries, need %lld", (long long)counts_len,
+                     (long long)k);
+  if ((numel > 0 && !packed) || !counts || !out_max) return set_error(OPUS_ERR_INVALID, "bucket_max_load: NULL pointer");
+  return launch_bucket_max_load(packed, numel, k, counts, out_max, (cudaStream_t)stream);
 }
 
 }  // extern "C"

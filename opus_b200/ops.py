@@ -62,11 +62,22 @@ def pack_hash_sign(hash_: torch.Tensor, sign: torch.Tensor, k: int, validate: bo
     return out
 
 
+def bucket_counts(packed: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-bucket element counts [k] int32 and their max [1] int64, on the device."""
+    _cuda(packed, "packed")
+    packed = _contig(packed.reshape(-1))
+    if packed.dtype not in (torch.int32, torch.uint32):
+        raise ValueError("packed table must be 32-bit")
+    counts = torch.empty(int(k), dtype=torch.int32, device=packed.device)
+    out = torch.empty(1, dtype=torch.int64, device=packed.device)
+    _lib.check(_lib.load().opus_bucket_max_load(_ptr(packed), packed.numel(), int(k), _ptr(counts), counts.numel(),
+                                               _ptr(out), _stream(packed)), "opus_bucket_max_load")
+    return counts, out
+
+
 def bucket_max_load(packed: torch.Tensor, k: int) -> int:
     """Largest number of elements sharing one bucket (bounds the fixed-point sketch)."""
-    _cuda(packed, "packed")
-    buckets = (packed.reshape(-1) & 0x7FFFFFFF).to(torch.int64)
-    return int(torch.bincount(buckets, minlength=int(k)).max().item()) if buckets.numel() else 0
+    return int(bucket_counts(packed, k)[1].item())
 
 
 def sketch_table_entries(d_out: int, d_in: int) -> int:

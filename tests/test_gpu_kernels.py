@@ -59,6 +59,36 @@ def decode_table(table, d_out, d_in):
     return bucket, weight
 
 
+@pytest.mark.parametrize("numel,k,offset", [(3072 * 768, 16384, 0), (1_000_003, 65536, 1), (37, 8, 3),
+                                            (100_000, 32768, 2), (5, 131072, 0)])
+def test_bucket_counts_match_bincount(numel, k, offset):
+    """Shared-memory (k <= 32768) and global-atomic histograms, misaligned starts."""
+    rng = np.random.default_rng(numel)
+    buckets = rng.integers(0, k, numel + offset).astype(np.uint32)
+    signs = rng.integers(0, 2, numel + offset).astype(np.uint32) << np.uint32(31)
+    packed = torch.from_numpy((buckets | signs).view(np.int32)).to(DEV)[offset:]
+    counts, mx = ops.bucket_counts(packed, k)
+    ops.check_device_error("bucket_counts")
+    want = np.bincount(buckets[offset:].astype(np.int64), minlength=k)
+    np.testing.assert_array_equal(counts.cpu().numpy(), want)
+    assert int(mx.item()) == int(want.max())
+
+
+def test_bucket_counts_empty_and_bad_bucket():
+    counts, mx = ops.bucket_counts(torch.empty(0, dtype=torch.int32, device=DEV), 16)
+    assert int(mx.item()) == 0 and int(counts.sum().item()) == 0
+    bad = torch.tensor([1, 2, 40, 3], dtype=torch.int32, device=DEV)
+    counts, _ = ops.bucket_counts(bad, 16)
+    with pytest.raises(RuntimeError, match="0x201"):
+        ops.check_device_error("bucket_counts")
+    assert counts.cpu().tolist()[:4] == [0, 1, 1, 1]
+
+
+def test_bucket_max_load_of_reference_tables():
+    h, s, packed = cuda_tables(3072 * 768, 0, 16384)
+    assert ops.bucket_max_load(packed, 16384) == int(np.bincount(h, minlength=16384).max())
+
+
 @pytest.mark.parametrize("d_out,d_in", [(128, 256), (72, 48), (200, 520)])
 def test_table_layout_and_adam_diag(d_out, d_in):
     k = 4096
