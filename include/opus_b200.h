@@ -81,6 +81,26 @@ OPUS_API int opus_pack_hash_sign(const int64_t* hash, const float* sign, int64_t
 OPUS_API int opus_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int* counts,
                                   int64_t counts_len, int64_t* out_max, void* stream);
 
+/*
+ * The same maximum as opus_bucket_max_load, computed without allocating any
+ * device memory: no reference counterpart (the reference has no bucket-load
+ * step at all).  Some hosts cannot hand the library a k-entry workspace: a
+ * process that reserves its device memory up front and treats any later
+ * allocation as a failure, or an out-of-memory path that needs the bound
+ * while the allocator has nothing left to give.  This entry point counts in a
+ * static device array of the library instead.
+ *   - k <= 262144 (1 MB of counts); larger k is rejected with OPUS_ERR_INVALID.
+ *   - The first call on each device looks up the array's address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - Every call zeroes the array on its stream before counting.  Calls that
+ *     overlap on one device share the array and race: serialise them.
+ *   - *out_max (one int64 on the device) is -1 when a bucket lies outside
+ *     [0,k); the library's device error word is not touched.
+ */
+OPUS_API int opus_bucket_max_load_noalloc(const uint32_t* packed, int64_t numel, int64_t k, int64_t* out_max,
+                                          void* stream);
+
 /* Number of 16-byte entries of the tiled epilogue table for a [d_out,d_in] layer. */
 OPUS_API int64_t opus_sketch_table_entries(int d_out, int d_in);
 

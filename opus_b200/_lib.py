@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "opus_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
     "opus_pack_hash_sign": (_c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p]),
     "opus_bucket_max_load": (_c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_p]),
+    "opus_bucket_max_load_noalloc": (_c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_p]),
     "opus_sketch_table_entries": (_c_i64, [_c_int, _c_int]),
     "opus_build_sketch_table": (_c_int, [_c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "opus_sketch_gemm": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_i64, _c_int,

@@ -4,6 +4,9 @@
 //   opus_build_sketch_table packed + AdamW diag      ->  tiled epilogue table
 //   opus_desketch           tau + packed + diag      ->  dense bf16 hi/lo target
 //   opus_bucket_max_load    packed                   ->  per-bucket counts, their max
+//   opus_bucket_max_load_noalloc                     ->  the max, counting in static device memory
+#include <mutex>
+
 #include "opus_common.cuh"
 #include "sketch_layout.cuh"
 
@@ -199,6 +202,88 @@ int launch_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int
   return OPUS_OK;
 }
 
+// ---- the max bucket load without any allocation
+// Counting needs k int32 of scratch.  This variant keeps it in a static
+// device array of the module (one copy per device, reserved when the module
+// loads) instead of a caller's buffer: slot 0 is the bad-bucket flag and the
+// counts start 64 ints (256 B) in.  Both are zeroed on the stream by every
+// call; calls that overlap on one device share the array and race.
+constexpr int64_t kNoAllocMaxBuckets = 262144;  // 1 MB of counts
+constexpr int kNoAllocCountsOffset = 64;
+constexpr int kNoAllocMaxDevices = 64;
+
+std::mutex g_noalloc_mu;
+int* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+}  // namespace
+
+static __device__ __align__(256) int g_noalloc_scratch[kNoAllocCountsOffset + kNoAllocMaxBuckets];
+
+namespace {
+
+// Device address of the static scratch for the current device, looked up by
+// the first call on that device and cached.
+int noalloc_scratch(int** out) {
+  int dev = 0;
+  OPUS_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(OPUS_ERR_UNSUPPORTED, "bucket_max_load_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    OPUS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = static_cast<int*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return OPUS_OK;
+}
+
+// One CTA: max over the k counts, or -1 when the flag records a bucket >= k.
+__global__ void __launch_bounds__(1024) bucket_max_flagged_kernel(const int* __restrict__ counts, int64_t k,
+                                                                  const int* __restrict__ bad,
+                                                                  int64_t* __restrict__ out) {
+  int mx = 0;
+  for (int64_t i = threadIdx.x; i < k; i += 1024) mx = max(mx, counts[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  __shared__ int part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    mx = part[threadIdx.x];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (threadIdx.x == 0) *out = *bad ? -1 : mx;
+  }
+}
+
+int launch_bucket_max_load_noalloc(const uint32_t* packed, int64_t numel, int64_t k, int64_t* out_max,
+                                   cudaStream_t st) {
+  int* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != OPUS_OK) return rc;
+  int* bad = scratch;
+  int* counts = scratch + kNoAllocCountsOffset;
+  OPUS_CUDA_TRY(cudaMemsetAsync(scratch, 0, (size_t)(kNoAllocCountsOffset + k) * sizeof(int), st));
+  if (numel > 0) {
+    if (k <= kHistSmemBuckets) {
+      int64_t grid = numel / (8 * k);
+      grid = grid < 1 ? 1 : (grid > sm_count() ? sm_count() : grid);
+      const size_t smem = (size_t)k * sizeof(int);
+      OPUS_CUDA_TRY(cudaFuncSetAttribute(bucket_hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+      bucket_hist_kernel<true><<<(int)grid, kHistThreads, smem, st>>>(packed, numel, (uint32_t)k, counts, bad);
+    } else {
+      bucket_hist_kernel<false><<<grid_for(numel / 4 + 1, kHistThreads), kHistThreads, 0, st>>>(
+          packed, numel, (uint32_t)k, counts, bad);
+    }
+    OPUS_CUDA_TRY(cudaGetLastError());
+  }
+  bucket_max_flagged_kernel<<<1, 1024, 0, st>>>(counts, k, bad, out_max);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
 }  // namespace
 }  // namespace opus
 
@@ -258,6 +343,15 @@ int opus_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int* 
                      (long long)k);
   if ((numel > 0 && !packed) || !counts || !out_max) return set_error(OPUS_ERR_INVALID, "bucket_max_load: NULL pointer");
   return launch_bucket_max_load(packed, numel, k, counts, out_max, (cudaStream_t)stream);
+}
+
+int opus_bucket_max_load_noalloc(const uint32_t* packed, int64_t numel, int64_t k, int64_t* out_max, void* stream) {
+  if (numel < 0 || k <= 0) return set_error(OPUS_ERR_INVALID, "bucket_max_load_noalloc: bad numel/k");
+  if (k > kNoAllocMaxBuckets)
+    return set_error(OPUS_ERR_INVALID, "bucket_max_load_noalloc: k=%lld exceeds the static scratch of %lld buckets",
+                     (long long)k, (long long)kNoAllocMaxBuckets);
+  if ((numel > 0 && !packed) || !out_max) return set_error(OPUS_ERR_INVALID, "bucket_max_load_noalloc: NULL pointer");
+  return launch_bucket_max_load_noalloc(packed, numel, k, out_max, (cudaStream_t)stream);
 }
 
 }  // extern "C"
