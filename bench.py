@@ -14,10 +14,13 @@ L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Multi-GPU (torchrun, one rank per GPU): every rank scores its own 256
-candidates and draws its own picks (the reference's default local selection
-mode), so the work per GPU is fixed (weak scaling) and no data crosses GPUs
-in the timed region.  Rank 0 prints one JSON line.
+Multi-GPU (torchrun, one rank per GPU): every rank holds its own 256
+candidates (weak scaling) and sketches its share of the target's rows; one
+NCCL all-reduce of the target sketch, scoring and the local similarity block
+on each rank, one all-gather of scores and similarity blocks, then every rank
+runs the same global Boltzmann draw of 64 x N of the 256 x N candidates with
+the block-diagonal interaction matrix.  Device time is the max over ranks.
+Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
@@ -137,27 +140,37 @@ def run_gpu(args, rank, world, local_rank):
 
     from opus_b200 import ops
     from opus_b200.train import data_selection as ds
+    from opus_b200.train import distributed as sd
     from opus_b200.train.random_projection import GradientProjector
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     nb = args.batch
-    n_sel = max(1, nb // 4)
+    n_sel_local = max(1, nb // 4)
+    n_sel = n_sel_local * world  # one global draw over all ranks' candidates
     a, dz, V, diag = make_inputs(dev, rank, nb)
     proj = GradientProjector(sketch_dim=K_SKETCH, seed=SEED, device="cuda")
     pid = 0
     packed = proj.packed_table(D_OUT * D_IN, pid, dev)
     load = proj.max_bucket_load(D_OUT * D_IN, pid, dev)
-    uni = torch.from_numpy(np.random.default_rng(99 + rank).random(n_sel)).to(dev)
+    rows = sd.shard_range(D_OUT, rank, world)  # this rank's share of the target
+    uni = torch.from_numpy(np.random.default_rng(99).random(n_sel)).to(dev)  # the same on every rank
     phi = torch.empty(nb, K_SKETCH, device=dev)
     tau = torch.empty(K_SKETCH, device=dev)
     score = torch.empty(nb, device=dev)
     sim = torch.empty(nb, nb, device=dev)
     ev = {}
 
+    def select(score_, sim_):
+        if world == 1:
+            return ops.boltzmann_select(score_, sim_, n_sel, TEMPERATURE, uni)
+        scores_all, blocks = sd.gather_scores_and_blocks(score_, sim_)
+        return ops.boltzmann_select(scores_all, blocks, n_sel, TEMPERATURE, uni)
+
     def step(time_kernel=False):
         table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
-        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau)
+        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau, rows=rows)
+        sd.allreduce_target_sketches(tau)
         phi.zero_()
         if time_kernel:
             ev["s"].append(torch.cuda.Event(enable_timing=True))
@@ -168,7 +181,7 @@ def run_gpu(args, rank, world, local_rank):
             ev["e"][-1].record()
         ops.sketch_dot(phi, tau, out=score)
         ops.sketch_gram(phi, out=sim)
-        return ops.boltzmann_select(score, sim, n_sel, TEMPERATURE, uni)
+        return select(score, sim)
 
     for _ in range(args.warmup):
         step()
@@ -194,31 +207,34 @@ def run_gpu(args, rank, world, local_rank):
         dist.barrier()
     ms_per_step = ms / args.steps
 
-    # per-stage breakdown (untimed for the headline; events around each stage)
-    stages = {}
-    if rank == 0:
-        names = ["table", "target_sketch", "sketch_gemm", "score", "gram", "select"]
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
-        reps = 5
-        acc = [0.0] * len(names)
-        for _ in range(reps):
-            evs[0].record()
-            table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
-            evs[1].record()
-            ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau)
-            evs[2].record()
-            ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi, max_bucket_load=load)
-            evs[3].record()
-            ops.sketch_dot(phi, tau, out=score)
-            evs[4].record()
-            ops.sketch_gram(phi, out=sim)
-            evs[5].record()
-            ops.boltzmann_select(score, sim, n_sel, TEMPERATURE, uni)
-            evs[6].record()
-            torch.cuda.synchronize()
-            for i in range(len(names)):
-                acc[i] += evs[i].elapsed_time(evs[i + 1]) / reps
-        stages = {n: round(x, 4) for n, x in zip(names, acc)}
+    # per-stage breakdown (untimed for the headline; events around each stage;
+    # every rank runs it so the collectives stay matched, rank 0 reports)
+    names = ["table", "target_sketch", "allreduce", "sketch_gemm", "score", "gram", "gather", "select"]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+    reps = 5
+    acc = [0.0] * len(names)
+    for _ in range(reps):
+        evs[0].record()
+        table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
+        evs[1].record()
+        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau, rows=rows)
+        evs[2].record()
+        sd.allreduce_target_sketches(tau)
+        evs[3].record()
+        ops.sketch_gemm(dz, a, table, K_SKETCH, out=phi, max_bucket_load=load)
+        evs[4].record()
+        ops.sketch_dot(phi, tau, out=score)
+        evs[5].record()
+        ops.sketch_gram(phi, out=sim)
+        evs[6].record()
+        scores_all, blocks = sd.gather_scores_and_blocks(score, sim) if world > 1 else (score, sim)
+        evs[7].record()
+        ops.boltzmann_select(scores_all, blocks, n_sel, TEMPERATURE, uni)
+        evs[8].record()
+        torch.cuda.synchronize()
+        for i in range(len(names)):
+            acc[i] += evs[i].elapsed_time(evs[i + 1]) / reps
+    stages = {n: round(x, 4) for n, x in zip(names, acc) if world > 1 or n not in ("allreduce", "gather")}
 
     # end to end through the public API with host buffers
     e2e = None
@@ -238,7 +254,10 @@ def run_gpu(args, rank, world, local_rank):
             tau_e = proj.project_vector(V_d.T, pid)
             sc = ops.sketch_dot(phi_e, tau_e)
             sm = ops.sketch_gram(phi_e)
-            return ds.stochastic_greedy_selection(sc, sm, n_sel, temperature=TEMPERATURE)
+            if world == 1:
+                return ds.stochastic_greedy_selection(sc, sm, n_sel, temperature=TEMPERATURE)
+            gidx, _ = sd.select_global(sc, sm, n_sel, method="stochastic", temperature=TEMPERATURE)
+            return gidx.cpu()
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):
@@ -260,7 +279,8 @@ def run_gpu(args, rank, world, local_rank):
         h2d = sum(x.numel() * x.element_size() for x in (a_h, dz_h, V_h, diag_h))
         e2e = {"value": round(nb * world / (e_ms / e2e_steps / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": n_sel * 8, "api": "GradientProjector.project_full_gradient + "
-               "project_vector + stochastic_greedy_selection", "steps": e2e_steps}
+               "project_vector + " + ("stochastic_greedy_selection" if world == 1 else "distributed.select_global"),
+               "steps": e2e_steps}
     return ms_per_step, kern_ms, stages, e2e, clk.summary()
 
 
@@ -383,8 +403,11 @@ def main():
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": WORKLOAD if nb == B else WORKLOAD.replace("256 seqs", f"{nb} seqs"),
                            "global_batch": nb * world, "seq_len": T, "k": K_SKETCH,
-                           "select": f"{max(1, nb // 4)} of {nb} per GPU, Boltzmann T={TEMPERATURE}",
-                           "parallelism": f"dp{world} (candidates sharded, local selection)",
+                           "select": f"{max(1, nb // 4) * world} of {nb * world} in one global Boltzmann draw, "
+                                     f"T={TEMPERATURE}",
+                           "parallelism": (f"dp{world}: candidates sharded, target sketch rows sharded + NCCL "
+                                           "all-reduce, scores and similarity blocks all-gathered, global draw "
+                                           "with the block-diagonal interaction matrix") if world > 1 else "dp1",
                            "l2": "inputs 2.0 GB per GPU > 126 MB L2, no flush"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
                 "gpu_launches": 6 * args.steps, "stage_ms": stages}

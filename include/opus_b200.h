@@ -149,11 +149,14 @@ OPUS_API int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_
  * K1 — dense CountSketch of one [d_out,d_in] f32 matrix (the proxy target
  * direction): sketch[h(o,c)] += s(o,c) * diag(o,c) * w(o,c), with w read as
  * w[o*d_in+c] (transposed = 0) or w[c*d_out+o] (transposed = 1); diag may be
- * NULL.  Replaces GradientProjector.project_vector
+ * NULL.  Only rows row_begin <= o < row_end are added (0, d_out for the whole
+ * matrix): ranks that share the target each sketch their rows and sum the
+ * partial sketches.  Replaces GradientProjector.project_vector
  * (OPUS/train/random_projection.py:72-99).
  */
 OPUS_API int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, const float* diag,
-                      int d_out, int d_in, int64_t k, float* sketch, int accumulate, void* stream);
+                      int d_out, int d_in, int row_begin, int row_end, int64_t k, float* sketch, int accumulate,
+                      void* stream);
 
 /*
  * K2 — de-sketched target for the ghost contraction:
@@ -208,6 +211,21 @@ OPUS_API int opus_boltzmann_select(const float* scores, const float* sim, int n,
  * wins as in np.argmax), scores -= sim[idx], scores[idx] = -inf. */
 OPUS_API int opus_greedy_select(const float* scores, const float* sim, int n, int n_select, int64_t* out_idx,
                        void* stream);
+
+/*
+ * Global selection over candidates sharded across ranks (the choreography of
+ * the reference's global mode, train.py:1100-1178, with the candidates scored
+ * where they live): the same samplers with a block-diagonal interaction
+ * matrix, sim_blocks [n/block, block, block] holding each rank's local
+ * similarity; entries outside the blocks are zero, so a pick penalises only
+ * its own block (x - 0 == x exactly).  Results equal opus_boltzmann_select /
+ * opus_greedy_select on the dense block-diagonal matrix.  block must divide n.
+ */
+OPUS_API int opus_boltzmann_select_blocks(const float* scores, const float* sim_blocks, int n, int block,
+                                          int n_select, double temperature, const double* uniforms,
+                                          int64_t* out_idx, void* stream);
+OPUS_API int opus_greedy_select_blocks(const float* scores, const float* sim_blocks, int n, int block, int n_select,
+                                       int64_t* out_idx, void* stream);
 
 /* f32 -> bf16 pair: hi = bf16_rn(x), lo = bf16_rn(x - hi), n elements.
  * Used to feed f32 activations/gradients to the bf16 tensor-core kernels. */

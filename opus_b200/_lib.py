@@ -36,7 +36,8 @@ SIGNATURES: dict[str, tuple] = {
     "opus_build_sketch_table": (_c_int, [_c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "opus_sketch_gemm": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_i64, _c_int,
                                   _c_int, _c_p, _c_int, _c_p]),
-    "opus_sketch_dense": (_c_int, [_c_p, _c_int, _c_p, _c_p, _c_int, _c_int, _c_i64, _c_p, _c_int, _c_p]),
+    "opus_sketch_dense": (_c_int, [_c_p, _c_int, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_p, _c_int,
+                                   _c_p]),
     "opus_desketch": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_i64, _c_f32, _c_p, _c_p]),
     "opus_ghost_score": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_f32, _c_p, _c_int,
                                   _c_p]),
@@ -44,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
     "opus_sketch_gram": (_c_int, [_c_p, _c_int, _c_p, _c_int, _c_i64, _c_f32, _c_p, _c_int, _c_p]),
     "opus_boltzmann_select": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_f64, _c_p, _c_p, _c_p]),
     "opus_greedy_select": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_p, _c_p]),
+    "opus_boltzmann_select_blocks": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_f64, _c_p, _c_p, _c_p]),
+    "opus_greedy_select_blocks": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_p, _c_p]),
     "opus_split_bf16": (_c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p]),
 }
 

@@ -10,7 +10,8 @@ namespace {
 constexpr int kDenseThreads = 256;
 constexpr int kDenseTile = 32;  // 32 x 32 (o, c) tiles
 
-// Grid-stride over 32x32 tiles of the [d_out, d_in] grid.  The weight tile is
+// Grid-stride over 32x32 tiles of rows [row_begin, row_end) of the
+// [d_out, d_in] grid (a rank's share of the target in sharded selection).  The weight tile is
 // read in its stored orientation (coalesced either way) and staged through
 // shared memory; the packed table is read row-major; every element is added
 // to its bucket with an f32 reduction in L2 (shared-memory float atomics are
@@ -19,23 +20,25 @@ constexpr int kDenseTile = 32;  // 32 x 32 (o, c) tiles
 __global__ void __launch_bounds__(kDenseThreads) dense_sketch_kernel(const float* __restrict__ w, int transposed,
                                                                      const uint32_t* __restrict__ packed,
                                                                      const float* __restrict__ diag, int d_out,
-                                                                     int d_in, int64_t k, float* __restrict__ out) {
+                                                                     int d_in, int row_begin, int row_end, int64_t k,
+                                                                     float* __restrict__ out) {
   __shared__ float tile_w[kDenseTile][kDenseTile + 1];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-  const int n_to = (d_out + kDenseTile - 1) / kDenseTile, n_tc = (d_in + kDenseTile - 1) / kDenseTile;
+  const int rows = row_end - row_begin;
+  const int n_to = (rows + kDenseTile - 1) / kDenseTile, n_tc = (d_in + kDenseTile - 1) / kDenseTile;
   const int64_t n_tiles = (int64_t)n_to * n_tc;
   for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-    const int o0 = static_cast<int>(t / n_tc) * kDenseTile, c0 = static_cast<int>(t % n_tc) * kDenseTile;
+    const int o0 = row_begin + static_cast<int>(t / n_tc) * kDenseTile, c0 = static_cast<int>(t % n_tc) * kDenseTile;
     if (transposed) {
       for (int rr = ty; rr < kDenseTile; rr += 8) {
         const int c = c0 + rr, o = o0 + tx;
-        tile_w[tx][rr] = (o < d_out && c < d_in) ? w[(int64_t)c * d_out + o] : 0.0f;
+        tile_w[tx][rr] = (o < row_end && c < d_in) ? w[(int64_t)c * d_out + o] : 0.0f;
       }
       __syncthreads();
     }
     for (int rr = ty; rr < kDenseTile; rr += 8) {
       const int o = o0 + rr, c = c0 + tx;
-      if (o < d_out && c < d_in) {
+      if (o < row_end && c < d_in) {
         const int64_t idx = (int64_t)o * d_in + c;
         const uint32_t hv = packed[idx];
         float x = transposed ? tile_w[rr][tx] : w[idx];
@@ -99,15 +102,20 @@ using namespace opus;
 extern "C" {
 
 int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, const float* diag, int d_out, int d_in,
-                      int64_t k, float* sketch, int accumulate, void* stream) {
+                      int row_begin, int row_end, int64_t k, float* sketch, int accumulate, void* stream) {
   if (d_out <= 0 || d_in <= 0 || k <= 0 || k > 0x7FFFFFFF) return set_error(OPUS_ERR_INVALID, "sketch_dense: bad sizes");
+  if (row_begin < 0 || row_end > d_out || row_begin > row_end)
+    return set_error(OPUS_ERR_INVALID, "sketch_dense: rows [%d, %d) outside [0, %d)", row_begin, row_end, d_out);
   if (!w || !packed || !sketch) return set_error(OPUS_ERR_INVALID, "sketch_dense: NULL pointer");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (!accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(sketch, 0, (size_t)k * sizeof(float), st));
-  const int64_t n_tiles = (int64_t)((d_out + kDenseTile - 1) / kDenseTile) * ((d_in + kDenseTile - 1) / kDenseTile);
+  if (row_end == row_begin) return OPUS_OK;
+  const int64_t n_tiles =
+      (int64_t)((row_end - row_begin + kDenseTile - 1) / kDenseTile) * ((d_in + kDenseTile - 1) / kDenseTile);
   int64_t grid = (int64_t)sm_count() * 8;
   if (grid > n_tiles) grid = n_tiles;
-  dense_sketch_kernel<<<(int)grid, kDenseThreads, 0, st>>>(w, transposed, packed, diag, d_out, d_in, k, sketch);
+  dense_sketch_kernel<<<(int)grid, kDenseThreads, 0, st>>>(w, transposed, packed, diag, d_out, d_in, row_begin,
+                                                           row_end, k, sketch);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -148,7 +148,8 @@ __device__ long long cdf_threshold(double u, long long L) {
 template <int NT>
 __global__ void __launch_bounds__(NT, 1)
     boltzmann_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
-                     float temp, const double* __restrict__ uniforms, int64_t* __restrict__ out_idx, int* err) {
+                     int block, float temp, const double* __restrict__ uniforms, int64_t* __restrict__ out_idx,
+                     int* err) {
   constexpr int W = NT / 32;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   SelShared& s = *reinterpret_cast<SelShared*>(sel_smem);
@@ -352,9 +353,17 @@ __global__ void __launch_bounds__(NT, 1)
     const int sel = s.pidx[min(pick, m - 1)];
     if (tid == 0) out_idx[r] = sel;
     // (6) interaction penalty on every owned score (float32); the owner of
-    //     the pick retires it
+    //     the pick retires it.  Block-diagonal sim: [n/block, block, block],
+    //     and only the pick's own block has nonzero entries (x - 0 == x).
     const float* row = sim + (int64_t)sel * n;
-    for (int i = lo; i < hi; ++i) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
+    int plo = lo, phi = hi;
+    if (block > 0) {
+      const int q0 = sel - sel % block;
+      row = sim + (int64_t)sel * block - q0;
+      plo = max(lo, q0);
+      phi = min(hi, q0 + block);
+    }
+    for (int i = plo; i < phi; ++i) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
     if (sel >= lo && sel < hi) s.avail[sel] = 0;
   }
 }
@@ -376,7 +385,7 @@ __device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
 }
 
 __global__ void __launch_bounds__(kSelThreads, 1)
-    greedy_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
+    greedy_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int block, int n_select,
                   int64_t* __restrict__ out_idx) {
   extern __shared__ __align__(16) uint8_t sel_smem[];
   float* scores = reinterpret_cast<float*>(sel_smem);
@@ -413,7 +422,13 @@ __global__ void __launch_bounds__(kSelThreads, 1)
     __syncthreads();
     const int sel = pick;
     const float* row = sim + (int64_t)sel * n;
-    for (int i = tid; i < n; i += kSelThreads) scores[i] = __fsub_rn(scores[i], row[i]);
+    int plo = 0, phi = n;
+    if (block > 0) {  // block-diagonal sim, as in boltzmann_kernel
+      plo = sel - sel % block;
+      phi = plo + block;
+      row = sim + (int64_t)sel * block - plo;
+    }
+    for (int i = plo + tid; i < phi; i += kSelThreads) scores[i] = __fsub_rn(scores[i], row[i]);
     __syncthreads();
     if (tid == 0) scores[sel] = -INFINITY;
     __syncthreads();
@@ -427,11 +442,17 @@ using namespace opus;
 
 extern "C" {
 
-int opus_boltzmann_select(const float* scores, const float* sim, int n, int n_select, double temperature,
-                          const double* uniforms, int64_t* out_idx, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int launch_boltzmann(const float* scores, const float* sim, int n, int block, int n_select, double temperature,
+                     const double* uniforms, int64_t* out_idx, void* stream) {
   if (n <= 0 || n > kSelMax) return set_error(OPUS_ERR_UNSUPPORTED, "boltzmann: n=%d outside [1, %d]", n, kSelMax);
   if (n_select < 0 || n_select > n)
     return set_error(OPUS_ERR_INVALID, "boltzmann: cannot select %d of %d candidates", n_select, n);
+  if (block < 0 || (block > 0 && n % block != 0))
+    return set_error(OPUS_ERR_INVALID, "boltzmann: block %d does not divide n=%d", block, n);
   if (n_select == 0) return OPUS_OK;
   if (!scores || !sim || !uniforms || !out_idx) return set_error(OPUS_ERR_INVALID, "boltzmann: NULL pointer");
   const size_t smem = sizeof(SelShared);
@@ -441,7 +462,7 @@ int opus_boltzmann_select(const float* scores, const float* sim, int n, int n_se
   // one candidate per thread up to 1024 candidates, then 1024 threads
 #define OPUS_LAUNCH_BOLTZMANN(NT)                                                                              \
   OPUS_CUDA_TRY(cudaFuncSetAttribute(boltzmann_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-  boltzmann_kernel<NT><<<1, NT, smem, st>>>(scores, sim, n, n_select, tf, uniforms, out_idx, err)
+  boltzmann_kernel<NT><<<1, NT, smem, st>>>(scores, sim, n, n_select, block, tf, uniforms, out_idx, err)
   if (n <= 128) {
     OPUS_LAUNCH_BOLTZMANN(128);
   } else if (n <= 256) {
@@ -456,17 +477,46 @@ int opus_boltzmann_select(const float* scores, const float* sim, int n, int n_se
   return OPUS_OK;
 }
 
-int opus_greedy_select(const float* scores, const float* sim, int n, int n_select, int64_t* out_idx, void* stream) {
+int launch_greedy(const float* scores, const float* sim, int n, int block, int n_select, int64_t* out_idx,
+                  void* stream) {
   if (n <= 0 || n > 4 * kSelMax) return set_error(OPUS_ERR_UNSUPPORTED, "greedy: n=%d outside [1, %d]", n, 4 * kSelMax);
   if (n_select < 0) return set_error(OPUS_ERR_INVALID, "greedy: negative n_select");
+  if (block < 0 || (block > 0 && n % block != 0))
+    return set_error(OPUS_ERR_INVALID, "greedy: block %d does not divide n=%d", block, n);
   if (n_select == 0) return OPUS_OK;
   if (!scores || !sim || !out_idx) return set_error(OPUS_ERR_INVALID, "greedy: NULL pointer");
   const size_t smem = (size_t)n * sizeof(float);
   if (smem > 48 * 1024)
     OPUS_CUDA_TRY(cudaFuncSetAttribute(greedy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  greedy_kernel<<<1, kSelThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(scores, sim, n, n_select, out_idx);
+  greedy_kernel<<<1, kSelThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(scores, sim, n, block, n_select,
+                                                                                   out_idx);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int opus_boltzmann_select(const float* scores, const float* sim, int n, int n_select, double temperature,
+                          const double* uniforms, int64_t* out_idx, void* stream) {
+  return launch_boltzmann(scores, sim, n, 0, n_select, temperature, uniforms, out_idx, stream);
+}
+
+int opus_boltzmann_select_blocks(const float* scores, const float* sim_blocks, int n, int block, int n_select,
+                                 double temperature, const double* uniforms, int64_t* out_idx, void* stream) {
+  if (block <= 0) return set_error(OPUS_ERR_INVALID, "boltzmann: block must be positive");
+  return launch_boltzmann(scores, sim_blocks, n, block, n_select, temperature, uniforms, out_idx, stream);
+}
+
+int opus_greedy_select(const float* scores, const float* sim, int n, int n_select, int64_t* out_idx, void* stream) {
+  return launch_greedy(scores, sim, n, 0, n_select, out_idx, stream);
+}
+
+int opus_greedy_select_blocks(const float* scores, const float* sim_blocks, int n, int block, int n_select,
+                              int64_t* out_idx, void* stream) {
+  if (block <= 0) return set_error(OPUS_ERR_INVALID, "greedy: block must be positive");
+  return launch_greedy(scores, sim_blocks, n, block, n_select, out_idx, stream);
 }
 
 }  // extern "C"

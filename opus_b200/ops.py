@@ -169,19 +169,23 @@ def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int
 
 def sketch_dense(w: torch.Tensor, packed: torch.Tensor, d_out: int, d_in: int, k: int, transposed: bool = False,
                  diag: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                 accumulate: bool = False) -> torch.Tensor:
-    """sketch[h] += s * diag * W for a dense [d_out, d_in] (or [d_in, d_out] if transposed) matrix."""
+                 accumulate: bool = False, rows: tuple[int, int] | None = None) -> torch.Tensor:
+    """sketch[h] += s * diag * W for a dense [d_out, d_in] (or [d_in, d_out] if transposed) matrix.
+
+    rows=(lo, hi) adds only the rows lo <= o < hi of the [d_out, d_in] layout.
+    """
     _cuda(w, "w")
     _cuda(packed, "packed")
     if w.numel() != d_out * d_in:
         raise ValueError(f"w has {w.numel()} elements, expected {d_out * d_in}")
     w = _contig(w.to(torch.float32))
     diag = None if diag is None else _contig(diag.to(torch.float32))
+    lo, hi = (0, d_out) if rows is None else (int(rows[0]), int(rows[1]))
     if out is None:
         out = torch.empty(k, dtype=torch.float32, device=w.device)
         accumulate = False
     _lib.check(_lib.load().opus_sketch_dense(_ptr(w), int(bool(transposed)), _ptr(packed), _ptr(diag), int(d_out),
-                                            int(d_in), int(k), _ptr(out), int(accumulate), _stream(w)),
+                                            int(d_in), lo, hi, int(k), _ptr(out), int(accumulate), _stream(w)),
                "opus_sketch_dense")
     return out
 
@@ -274,34 +278,61 @@ def sketch_gram(phi_a: torch.Tensor, phi_b: torch.Tensor | None = None, alpha: f
 
 
 # --------------------------------------------------------------------- stage 5
+def _sim_operand(sim: torch.Tensor, n: int) -> tuple[torch.Tensor, int]:
+    """Dense [n, n] interaction matrix (block 0) or block-diagonal blocks [q, b, b] (block b, q*b == n)."""
+    sim = _contig(sim.to(torch.float32))
+    if sim.dim() == 3:
+        q, b, b2 = sim.shape
+        if b != b2 or q * b != n:
+            raise ValueError(f"interaction blocks must be [q, b, b] with q*b == {n}, got {tuple(sim.shape)}")
+        return sim, b
+    if sim.shape != (n, n):
+        raise ValueError(f"interaction matrix must be [{n}, {n}]")
+    return sim, 0
+
+
 def boltzmann_select(scores: torch.Tensor, sim: torch.Tensor, n_select: int, temperature: float,
                      uniforms: torch.Tensor) -> torch.Tensor:
-    """Stochastic greedy selection on the device; uniforms: float64 [n_select] (one per draw)."""
+    """Stochastic greedy selection on the device; uniforms: float64 [n_select] (one per draw).
+
+    sim is the dense [n, n] interaction matrix, or [q, b, b] blocks of a
+    block-diagonal one (candidates sharded over q ranks of b each).
+    """
     _cuda(scores, "scores")
     scores = _contig(scores.to(torch.float32).reshape(-1))
     n = scores.numel()
-    sim = _contig(sim.to(torch.float32))
-    if sim.shape != (n, n):
-        raise ValueError(f"interaction matrix must be [{n}, {n}]")
+    sim, block = _sim_operand(sim, n)
     if n_select > n:
         raise ValueError(f"cannot select {n_select} of {n} candidates")
     uniforms = _contig(uniforms.to(device=scores.device, dtype=torch.float64).reshape(-1))
     if uniforms.numel() < n_select:
         raise ValueError("need one uniform per draw")
     out = torch.empty(n_select, dtype=torch.int64, device=scores.device)
-    _lib.check(_lib.load().opus_boltzmann_select(_ptr(scores), _ptr(sim), n, int(n_select), float(temperature),
-                                                _ptr(uniforms), _ptr(out), _stream(scores)), "opus_boltzmann_select")
+    lib = _lib.load()
+    if block:
+        rc = lib.opus_boltzmann_select_blocks(_ptr(scores), _ptr(sim), n, block, int(n_select), float(temperature),
+                                              _ptr(uniforms), _ptr(out), _stream(scores))
+    else:
+        rc = lib.opus_boltzmann_select(_ptr(scores), _ptr(sim), n, int(n_select), float(temperature),
+                                       _ptr(uniforms), _ptr(out), _stream(scores))
+    _lib.check(rc, "opus_boltzmann_select")
     return out
 
 
 def greedy_select(scores: torch.Tensor, sim: torch.Tensor, n_select: int) -> torch.Tensor:
+    """Greedy selection on the device; sim dense [n, n] or block-diagonal blocks [q, b, b]."""
     _cuda(scores, "scores")
     scores = _contig(scores.to(torch.float32).reshape(-1))
     n = scores.numel()
-    sim = _contig(sim.to(torch.float32))
-    if sim.shape != (n, n):
-        raise ValueError(f"interaction matrix must be [{n}, {n}]")
+    sim, block = _sim_operand(sim, n)
     out = torch.empty(n_select, dtype=torch.int64, device=scores.device)
-    _lib.check(_lib.load().opus_greedy_select(_ptr(scores), _ptr(sim), n, int(n_select), _ptr(out), _stream(scores)),
-               "opus_greedy_select")
+    lib = _lib.load()
+    if block:
+        rc = lib.opus_greedy_select_blocks(_ptr(scores), _ptr(sim), n, block, int(n_select), _ptr(out),
+                                           _stream(scores))
+    else:
+        rc = lib.opus_greedy_select(_ptr(scores), _ptr(sim), n, int(n_select), _ptr(out), _stream(scores))
+    _lib.check(rc, "opus_greedy_select")
     return out
+
+

@@ -270,7 +270,7 @@ class _Pair:
         self.p, self.g_t, self.a_t, self.g_v, self.a_v = p, g_t, a_t, g_v, a_v
 
 
-def capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len=512):
+def capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len=512, batch_val=None):
     """Stage 1: (dL/dZ, A) of every captured layer for candidates and proxies.
 
     One forward over the candidates and the round's proxy batch with dropout
@@ -278,8 +278,13 @@ def capture_pairs(model, batch_train, validation_loader, trainable_layers, score
     dL/dZ by autograd to each layer's stored pre-activation, then each
     layer's factorisation split into candidate / proxy halves
     (data_selection.py:345-445).  Returns (pairs, n_candidates, n_proxies).
+    batch_val, when given, replaces the loader's proxy batch (a rank's share
+    of it in sharded selection).
     """
-    batch_val = _sample_proxy_batch_for_step(validation_loader)
+    if batch_val is None:
+        batch_val = _sample_proxy_batch_for_step(validation_loader)
+    else:
+        batch_val = _copy_batch_dict(batch_val)
     val_bs = batch_val["input_ids"].shape[0]
     train_bs = batch_train["input_ids"].shape[0]
 

@@ -1,0 +1,213 @@
+"""One global OPUS selection over a candidate batch sharded across ranks.
+
+One process per GPU (torchrun), NCCL between them.  The reference's global
+mode (train.py:1100-1178) all-gathers every rank's candidate token ids to
+rank 0, which scores and selects the whole batch alone and broadcasts the
+picks.  Here each rank scores the candidates it already holds:
+
+1. rank 0's proxy batch is broadcast (as the reference does) and every rank
+   takes a contiguous share of it; each rank sketches its share of the proxy
+   gradient sum for every layer, and one all-reduce(sum) of the stacked
+   [L, k] target sketches gives every rank the full target;
+2. each rank computes its candidates' scores and their local similarity
+   block (the Gram of its own sketches);
+3. one all-gather of the scores [B_loc] and one of the local blocks
+   [B_loc, B_loc];
+4. every rank runs the same global draw -- the same uniforms, drawn from
+   NumPy's global stream on rank 0 and broadcast -- over the gathered scores
+   with the block-diagonal interaction matrix, so the picks agree without a
+   broadcast; each rank keeps the picks that fall in its shard.
+
+The similarity between candidates on different ranks is zero here (only
+scores and the local blocks cross GPUs), so the picks equal a single-process
+selection over the concatenated scores with the block-diagonal matrix, not
+the reference's dense one; the per-candidate scores are the reference's.
+Every rank must hold the same number of candidates.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from . import data_selection as ds
+
+
+def rank_and_world(group=None) -> tuple[int, int]:
+    if not (dist.is_available() and dist.is_initialized()):
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous share [lo, hi) of n items for a rank; the first n % world ranks get one more."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def allreduce_target_sketches(taus: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum the ranks' partial proxy sketches [L, k] in place (NCCL all-reduce)."""
+    if rank_and_world(group)[1] > 1:
+        dist.all_reduce(taus, op=dist.ReduceOp.SUM, group=group)
+    return taus
+
+
+def gather_scores_and_blocks(score: torch.Tensor, sim: torch.Tensor, group=None):
+    """All-gather scores [B_loc] -> [W*B_loc] and similarity blocks [B_loc, B_loc] -> [W, B_loc, B_loc]."""
+    rank, world = rank_and_world(group)
+    b = score.numel()
+    if sim.shape != (b, b):
+        raise ValueError(f"local similarity must be [{b}, {b}], got {tuple(sim.shape)}")
+    score = score.reshape(-1).contiguous()
+    sim = sim.contiguous()
+    if world == 1:
+        return score, sim.unsqueeze(0)
+    scores = [torch.empty_like(score) for _ in range(world)]
+    blocks = [torch.empty_like(sim) for _ in range(world)]
+    dist.all_gather(scores, score, group=group)
+    dist.all_gather(blocks, sim, group=group)
+    return torch.cat(scores), torch.stack(blocks)
+
+
+def shared_uniforms(n_select: int, device, group=None, src: int = 0) -> torch.Tensor:
+    """n_select doubles from rank src's NumPy global stream (np.random.choice's draws), on every rank."""
+    rank, world = rank_and_world(group)
+    u = torch.empty(n_select, dtype=torch.float64)
+    if rank == src:
+        u = torch.from_numpy(np.random.random_sample(n_select).astype(np.float64))
+    u = u.to(device)
+    if world > 1:
+        dist.broadcast(u, src=dist.get_global_rank(group, src) if group is not None else src, group=group)
+    return u
+
+
+def local_picks(global_idx: torch.Tensor, rank: int, b_local: int) -> torch.Tensor:
+    """The picks that fall in this rank's shard, as local indices (pick order kept)."""
+    lo = rank * b_local
+    mask = (global_idx >= lo) & (global_idx < lo + b_local)
+    return global_idx[mask] - lo
+
+
+def select_global(score: torch.Tensor, sim: torch.Tensor, n_select: int, method: str = "stochastic",
+                  temperature: float = 1.0, uniforms: torch.Tensor | None = None, group=None):
+    """Steps 3-4: gather, then the identical global draw on every rank.
+
+    score [B_loc] and sim [B_loc, B_loc] are this rank's (CUDA tensors).
+    Returns (global indices [n_select] int64, this rank's picks as local indices).
+    """
+    rank, _ = rank_and_world(group)
+    scores, blocks = gather_scores_and_blocks(score, sim, group)
+    n = scores.numel()
+    if method == "greedy":
+        idx = ops.greedy_select(scores, blocks, int(n_select))
+    elif method == "stochastic":
+        if n_select > n:
+            raise ValueError("zero-size array to reduction operation maximum which has no identity")
+        if uniforms is None:
+            uniforms = shared_uniforms(int(n_select), scores.device, group)
+        idx = ops.boltzmann_select(scores, blocks, int(n_select), float(temperature), uniforms)
+        ops.check_device_error("global stochastic_greedy_selection")
+    else:
+        raise ValueError(f"Unknown selection method: {method}")
+    return idx, local_picks(idx, rank, score.numel())
+
+
+def broadcast_batch(batch: dict | None, device, group=None, src: int = 0) -> dict:
+    """Rank src's proxy batch dict (input_ids int32/int64, labels int64, [n, T]) on every rank."""
+    rank, world = rank_and_world(group)
+    if world == 1:
+        return batch
+    keys = ("input_ids", "labels")
+    meta = torch.zeros(4, dtype=torch.int64, device=device)
+    if rank == src:
+        ids = batch["input_ids"]
+        meta[0], meta[1] = ids.shape[0], ids.shape[1]
+        meta[2] = 1 if ids.dtype == torch.int64 else 0
+    dist.broadcast(meta, src=src, group=group)
+    n, t, ids64 = int(meta[0]), int(meta[1]), int(meta[2])
+    if rank == src:
+        out = {key: batch[key].to(device).contiguous() for key in keys}
+    else:
+        out = {"input_ids": torch.empty(n, t, dtype=torch.int64 if ids64 else torch.int32, device=device),
+               "labels": torch.empty(n, t, dtype=torch.int64, device=device)}
+    for key in keys:
+        dist.broadcast(out[key], src=src, group=group)
+    out["attention_mask"] = torch.ones_like(out["input_ids"])
+    return out
+
+
+def score_shard(model, device, batch_train, proxy_share, n_proxy_total, optimizer, trainable_layers,
+                preconditioner="adamw", score_len=512, group=None):
+    """Steps 1-2 on one rank: scores [B_loc] and local similarity [B_loc, B_loc].
+
+    proxy_share is this rank's rows of the round's proxy batch (possibly
+    none); the per-layer proxy sketch sums are all-reduced so every rank
+    scores against the mean over all n_proxy_total proxies.  Needs the
+    CountSketch projector (initialize_projector(enabled=True)).
+    """
+    projector = ds.get_projector()
+    if projector is None or not projector.enabled:
+        raise ValueError("sharded selection needs the CountSketch projector (initialize_projector(enabled=True))")
+    pairs, train_bs, _ = ds.capture_pairs(model, batch_train, None, trainable_layers, score_len,
+                                          batch_val=proxy_share)
+    plans = ds.plan_layers(pairs, optimizer, preconditioner, device)
+    del pairs
+
+    def shaped(pl):
+        if pl.g_t.dim() == 2:
+            return pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1), pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)
+        return pl.g_t, pl.a_t, pl.g_v, pl.a_v
+
+    taus = torch.zeros(len(plans), projector.sketch_dim, device=device, dtype=torch.float32)
+    for li, pl in enumerate(plans):
+        _, _, g_v, a_v = shaped(pl)
+        if g_v.shape[0] > 0:
+            projector.sketch(g_v, a_v, pl.pid, rows_div=g_v.shape[0], out=taus[li:li + 1], accumulate=True)
+    allreduce_target_sketches(taus, group)
+
+    score = torch.zeros(train_bs, device=device, dtype=torch.float32)
+    sim = torch.zeros(train_bs, train_bs, device=device, dtype=torch.float32)
+    for li, pl in enumerate(plans):
+        g_t, a_t, _, _ = shaped(pl)
+        phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
+        if n_proxy_total > 0:
+            ops.sketch_dot(phi_t, taus[li], alpha=pl.c / n_proxy_total, out=score, accumulate=True)
+        ops.sketch_gram(phi_t, alpha=pl.c * pl.c, out=sim, accumulate=True)
+        del phi_t
+    return score, sim
+
+
+def get_batch_opus_global(model, buffer_seq, buffer_labels, optimizer, trainable_layers, validation_loader,
+                          selection_ratio, seq_len, selection_method="greedy", temperature=1.5, score_len=512,
+                          preconditioner="adamw", group=None):
+    """One global OPUS selection over the candidates of all ranks (the global mode of train.py:1100-1178).
+
+    Every rank passes its own candidate shard (the same number of sequences
+    on every rank).  Returns (global indices [K] on every rank, this rank's
+    picks as indices into its buffer), K = max(1, int(N_global * ratio)).
+    """
+    rank, world = rank_and_world(group)
+    device = buffer_seq.device
+    score_len = min(score_len, seq_len)
+    if buffer_seq.dim() == 1:
+        n = buffer_seq.numel() // seq_len
+        buffer_seq = buffer_seq[: n * seq_len].view(n, seq_len)
+        buffer_labels = buffer_labels[: n * seq_len].view(n, seq_len)
+    b_local = buffer_seq.shape[0]
+    proxy = ds._sample_proxy_batch_for_step(validation_loader) if rank == 0 else None
+    proxy = broadcast_batch(proxy, device, group)
+    n_proxy = proxy["input_ids"].shape[0]
+    lo, hi = shard_range(n_proxy, rank, world)
+    share = {key: v[lo:hi] for key, v in proxy.items()}
+    # the score windows of get_batch_opus (identity when score_len == seq_len)
+    gen = ds.make_window_generator(step=ds._GBG_CALL_ID, rank=rank, device=device.type)
+    ds._GBG_CALL_ID += 1
+    win_inputs, idx = ds._random_windows(buffer_seq, score_len, align_to=128, g=gen)
+    batch_train = {"input_ids": win_inputs, "attention_mask": torch.ones_like(win_inputs),
+                   "labels": buffer_labels.gather(1, idx)}
+    score, sim = score_shard(model, device, batch_train, share, n_proxy, optimizer, trainable_layers,
+                             preconditioner=preconditioner, score_len=score_len, group=group)
+    n_select = max(1, int(b_local * world * selection_ratio))
+    return select_global(score, sim, n_select, method=selection_method, temperature=temperature, group=group)

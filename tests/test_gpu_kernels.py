@@ -210,6 +210,27 @@ def test_sketch_dense(transposed, d_out, d_in, k):
     rel_close(out.cpu().numpy(), want, 1e-5, "dense sketch")
 
 
+@pytest.mark.parametrize("transposed", [False, True])
+def test_sketch_dense_row_shards_sum_to_whole(transposed):
+    """Ranks sketch their rows of the target; the partial sketches add up to the whole one."""
+    d_out, d_in, k = 3072, 768, 16384
+    h, s, packed = cuda_tables(d_out * d_in, 6, k)
+    W = torch.randn(d_out, d_in, device=DEV)
+    src = W.T.contiguous() if transposed else W
+    whole = orc.dense_sketch(W.cpu().numpy(), h, s, k)
+    for world in (3, 8):
+        acc = torch.zeros(k, device=DEV)
+        for r in range(world):
+            lo, hi = r * d_out // world, (r + 1) * d_out // world
+            ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, out=acc, accumulate=True,
+                             rows=(lo, hi))
+        rel_close(acc.cpu().numpy(), whole, 1e-5, f"row shards x{world}")
+    empty = ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, rows=(5, 5))
+    assert not empty.any()
+    with pytest.raises(ValueError):
+        ops.sketch_dense(src, packed, d_out, d_in, k, rows=(10, d_out + 1))
+
+
 def test_sketch_dot_and_gram():
     rng = np.random.default_rng(1)
     A = rng.standard_normal((70, 3000)).astype(np.float32)

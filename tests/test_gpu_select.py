@@ -100,3 +100,47 @@ def test_public_stochastic_selection_uses_numpy_stream():
 def test_stochastic_selection_too_many_picks():
     with pytest.raises(ValueError):
         ds.stochastic_greedy_selection(np.zeros(3, np.float32), np.zeros((3, 3), np.float32), 4)
+
+
+def _block_diag(blocks):
+    q, b, _ = blocks.shape
+    out = np.zeros((q * b, q * b), np.float32)
+    for r in range(q):
+        out[r * b:(r + 1) * b, r * b:(r + 1) * b] = blocks[r]
+    return out
+
+
+@pytest.mark.parametrize("q,b,K,temp", [(2, 256, 128, 1.0), (8, 256, 512, 1.0), (3, 7, 21, 0.5), (5, 100, 60, 2.0)])
+def test_block_diagonal_boltzmann_matches_dense(q, b, K, temp):
+    """Sharded-selection sampler: blocks [q, b, b] == the dense block-diagonal matrix == the oracle."""
+    rng = np.random.default_rng(q * 1000 + b)
+    sc = rng.standard_normal(q * b).astype(np.float32)
+    m = rng.standard_normal((q, b, b)).astype(np.float32) * np.float32(0.02)
+    blocks = ((m + m.transpose(0, 2, 1)) / 2).astype(np.float32)
+    dense = _block_diag(blocks)
+    uni = rng.random(K)
+    want = orc.stochastic_greedy_selection(sc, dense, K, temperature=temp, uniforms=uni)
+    got_b = ops.boltzmann_select(dev(sc), dev(blocks), K, temp, dev(uni)).cpu().tolist()
+    got_d = ops.boltzmann_select(dev(sc), dev(dense), K, temp, dev(uni)).cpu().tolist()
+    ops.check_device_error("boltzmann blocks")
+    assert got_b == got_d == want
+
+
+@pytest.mark.parametrize("q,b,K", [(4, 64, 100), (2, 300, 650)])
+def test_block_diagonal_greedy_matches_dense(q, b, K):
+    rng = np.random.default_rng(q + b)
+    sc = rng.standard_normal(q * b).astype(np.float32)
+    m = rng.standard_normal((q, b, b)).astype(np.float32) * np.float32(0.05)
+    blocks = ((m + m.transpose(0, 2, 1)) / 2).astype(np.float32)
+    dense = _block_diag(blocks)
+    want = orc.greedy_selection(sc, dense, K)
+    assert ops.greedy_select(dev(sc), dev(blocks), K).cpu().tolist() == want
+    assert ops.greedy_select(dev(sc), dev(dense), K).cpu().tolist() == want
+
+
+def test_block_operand_validation():
+    sc = torch.zeros(12, device=DEV)
+    with pytest.raises(ValueError):
+        ops.boltzmann_select(sc, torch.zeros(5, 2, 2, device=DEV), 2, 1.0, torch.rand(2, dtype=torch.float64))
+    with pytest.raises(ValueError):
+        ops.greedy_select(sc, torch.zeros(3, 4, 5, device=DEV), 2)
