@@ -27,12 +27,22 @@ constexpr int kPwBlock = 128;
 // so the split tree has at most 8 levels of at most 128 nodes.
 constexpr int kLevels = 8;
 constexpr int kLevelSlots = 128;
+// p and exp(x) by compacted position q live at q + 8 * (q / 128): the leaves
+// of 128 that four 8-lane groups of a warp read at once fall in distinct banks
+constexpr int kSkewedMax = kSelMax + kSelMax / kPwBlock * 8;
+
+__device__ __forceinline__ int skew(int q) { return q + ((q >> 7) << 3); }
 
 struct SelShared {
-  double cdf[kSelMax];
+  // scaled scores x = score / T by original index during a draw; the float64
+  // running sum by compacted position on the rare inexact path (x is dead by then)
+  union {
+    double cdf[kSelMax];
+    float xs[kSelMax];
+  };
   float scores[kSelMax];
-  float pc[kSelMax];
-  int pidx[kSelMax];
+  float pc[kSkewedMax];  // exp(x), then p, at skew(compacted position)
+  int pos[kSelMax];    // compacted position of each available candidate
   unsigned char avail[kSelMax];
   int lvl_start[kLevels][kLevelSlots];
   int lvl_len[kLevels][kLevelSlots];   // 0 = no node in this slot
@@ -40,15 +50,16 @@ struct SelShared {
   int leaf_slot[kLevels * kLevelSlots];  // (level << 7) | slot of every leaf
   int n_leaves;
   int tree_depth;
+  int leaf_done;
   long long scan_ll[32];
   double red_d[32];
-  int red_i[32];
   int red_ne[32];
-  int red_cnt[32];
   float red_f[32];
   int red_nan[32];
   float total;
   double cdf_total;
+  int pick;  // compacted position of this draw's pick
+  int sel;   // its original index
 };
 
 // ---- numpy pairwise float32 sum, as a split tree built level by level
@@ -141,39 +152,48 @@ __device__ long long cdf_threshold(double u, long long L) {
   return static_cast<long long>(t);
 }
 
-// Thread t owns the contiguous original indices [t*per, (t+1)*per): their
-// scores, availability and interaction penalties, so no barrier separates one
-// draw from the next.  The compacted (available-only) order is thread order,
-// then index order inside a thread.
+// Warp 0 owns no candidates: it lays out the pairwise-sum tree of the next
+// draw while the others normalise.  Owner thread t (t >= 32) holds the
+// contiguous original indices [(t-32)*per, (t-31)*per): their scores,
+// availability, compacted positions and interaction penalties, so no barrier
+// separates one draw from the next.  The compacted (available-only) order is
+// thread order, then index order inside a thread; a pick at compacted
+// position q moves every later available candidate down by one.
 template <int NT>
 __global__ void __launch_bounds__(NT, 1)
     boltzmann_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
                      int block, float temp, const double* __restrict__ uniforms, int64_t* __restrict__ out_idx,
                      int* err) {
   constexpr int W = NT / 32;
+  constexpr int kOwners = NT - 32;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   SelShared& s = *reinterpret_cast<SelShared*>(sel_smem);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (n + NT - 1) / NT;
-  const int lo = min(n, tid * per), hi = min(n, lo + per);
+  int per = (n + kOwners - 1) / kOwners;
+  if (per > 2 && (per & 1) == 0) ++per;  // odd: a warp's k-th candidates fall in distinct banks
+  const int lo = tid < 32 ? n : min(n, (tid - 32) * per), hi = tid < 32 ? n : min(n, lo + per);
   for (int i = lo; i < hi; ++i) {
     s.scores[i] = scores_in[i];
     s.avail[i] = 1;
+    s.pos[i] = i;
   }
+  if (warp == 0) {
+    pw_tree_build(n, s, lane);
+    if (lane == 0) s.leaf_done = 0;
+  }
+  __syncthreads();
 
   for (int r = 0; r < n_select; ++r) {
     const int m = n - r;  // available candidates
     const double u = uniforms[r];
-    // (1) scaled scores of the owned available elements, their max and count;
-    //     warp 0 also lays out the pairwise-sum tree for m elements
-    int cnt = 0;
+    // (1) x = score / T and exp(x) at the compacted positions; max and NaN flag
     float lmax = -INFINITY;
     int lnan = 0;
     for (int i = lo; i < hi; ++i) {
       if (!s.avail[i]) continue;
-      ++cnt;
       const float x = __fdiv_rn(s.scores[i], temp);
-      s.cdf[i] = x;
+      s.xs[i] = x;
+      s.pc[skew(s.pos[i])] = static_cast<float>(exp(static_cast<double>(x)));
       if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
     }
 #pragma unroll
@@ -181,34 +201,13 @@ __global__ void __launch_bounds__(NT, 1)
       lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
       lnan |= __shfl_xor_sync(0xffffffffu, lnan, off);
     }
-    int wx = cnt;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, wx, off);
-      if (lane >= off) wx += y;
-    }
-    if (lane == 31) s.red_i[warp] = wx;
     if (lane == 0) {
       s.red_f[warp] = lmax;
       s.red_nan[warp] = lnan;
     }
-    if (warp == 0) pw_tree_build(m, s, lane);
-    __syncthreads();                                                   // barrier 1
-    // (2) every warp combines the per-warp partials itself: compacted base,
-    //     max, NaN flag; then exp at the compacted positions (shifted by the
-    //     max only above 700, as the reference does)
-    int base;
-    float smax;
-    bool any_nan;
+    __syncthreads();                                                   // barrier A
     {
-      const int ci = lane < W ? s.red_i[lane] : 0;
-      int incl = ci;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
-      }
-      base = __shfl_sync(0xffffffffu, incl - ci, warp) + (wx - cnt);
+      // the reference shifts by the max only when it exceeds 700 (and no NaN)
       float mx = lane < W ? s.red_f[lane] : -INFINITY;
       int nn = lane < W ? s.red_nan[lane] : 0;
 #pragma unroll
@@ -216,25 +215,16 @@ __global__ void __launch_bounds__(NT, 1)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         nn |= __shfl_xor_sync(0xffffffffu, nn, off);
       }
-      smax = mx;
-      any_nan = nn != 0;
-    }
-    const bool do_shift = !any_nan && smax > 700.0f;
-    {
-      int pos = base;
-      for (int i = lo; i < hi; ++i) {
-        if (!s.avail[i]) continue;
-        float x = static_cast<float>(s.cdf[i]);
-        if (do_shift) x = __fsub_rn(x, smax);
-        s.pc[pos] = static_cast<float>(exp(static_cast<double>(x)));
-        s.pidx[pos] = i;
-        ++pos;
+      if (nn == 0 && mx > 700.0f) {
+        for (int i = lo; i < hi; ++i)
+          if (s.avail[i]) s.pc[skew(s.pos[i])] = static_cast<float>(exp(static_cast<double>(__fsub_rn(s.xs[i], mx))));
+        __syncthreads();
       }
     }
-    __syncthreads();                                                   // barrier 2
-    // (3) leaf sums, 8 lanes per leaf: lane j holds numpy's accumulator r[j],
+    // (2) leaf sums, 8 lanes per leaf: lane j holds numpy's accumulator r[j],
     //     combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail;
-    //     leaves shorter than 8 are a running sum from 0
+    //     leaves shorter than 8 are a running sum from 0.  The last warp to
+    //     finish combines the tree.
     const int n_leaves = s.n_leaves;
     for (int l0 = 0; l0 < n_leaves; l0 += NT / 8) {
       const int leaf = l0 + (tid >> 3), j = tid & 7;
@@ -244,38 +234,57 @@ __global__ void __launch_bounds__(NT, 1)
       const int a0 = active ? s.lvl_start[d][sj] : 0;
       const int ln = active ? s.lvl_len[d][sj] : 0;
       const int full = ln >= 8 ? ln - (ln % 8) : 0;
-      float acc = 0.0f;
-      if (full >= 8) {
-        acc = s.pc[a0 + j];
-        for (int i = 8; i < full; i += 8) acc = __fadd_rn(acc, s.pc[a0 + i + j]);
-      }
+      float v[kPwBlock / 8];
+#pragma unroll
+      for (int t = 0; t < kPwBlock / 8; ++t) v[t] = 8 * t < full ? s.pc[skew(a0 + 8 * t + j)] : 0.0f;
+      float acc = v[0];
+#pragma unroll
+      for (int t = 1; t < kPwBlock / 8; ++t)
+        if (8 * t < full) acc = __fadd_rn(acc, v[t]);
       const float p01 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
       const float p03 = __fadd_rn(p01, __shfl_xor_sync(0xffffffffu, p01, 2));
       const float p07 = __fadd_rn(p03, __shfl_xor_sync(0xffffffffu, p03, 4));
       if (active && j == 0) {
+        float tail[7];
+#pragma unroll
+        for (int t = 0; t < 7; ++t) tail[t] = full + t < ln ? s.pc[skew(a0 + full + t)] : 0.0f;
         float res = full >= 8 ? p07 : 0.0f;
-        for (int i = full; i < ln; ++i) res = __fadd_rn(res, s.pc[a0 + i]);
+#pragma unroll
+        for (int t = 0; t < 7; ++t)
+          if (full + t < ln) res = __fadd_rn(res, tail[t]);
         s.lvl_sum[d][sj] = res;
       }
     }
-    __syncthreads();                                                   // barrier 3
-    if (warp == 0) {
-      const float root = pw_tree_sum(s, lane);
-      if (lane == 0) s.total = __fadd_rn(0.0f, root);
+    __syncwarp();
+    int done = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      done = atomicAdd(&s.leaf_done, 1);
     }
-    __syncthreads();                                                   // barrier 4
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (done == W - 1) {
+      __threadfence_block();
+      const float root = pw_tree_sum(s, lane);
+      if (lane == 0) {
+        s.total = __fadd_rn(0.0f, root);
+        s.leaf_done = 0;
+      }
+    }
+    __syncthreads();                                                   // barrier B
     const float total = s.total;
     const bool uniform = (total == 0.0f) || !isfinite(total);
     const float inv_m = __fdiv_rn(1.0f, static_cast<float>(m));
-    // (4) normalise the owned compacted range [base, base + cnt); p * 2^52
-    //     is an integer for every p >= 2^-29, and then the float64 running
-    //     sum is exact and equals an int64 scan
+    // (3) normalise the owned positions; p * 2^52 is an integer for every
+    //     p >= 2^-29, and then the float64 running sum is exact and equals an
+    //     int64 scan.  Warp 0 lays out the next draw's tree meanwhile.
     int not_exact = 0;
     long long fsum = 0;
     double dsum = 0.0;
-    for (int i = base; i < base + cnt; ++i) {
-      const float p = uniform ? inv_m : __fdiv_rn(s.pc[i], total);
-      s.pc[i] = p;
+    for (int i = lo; i < hi; ++i) {
+      if (!s.avail[i]) continue;
+      const int q = skew(s.pos[i]);
+      const float p = uniform ? inv_m : __fdiv_rn(s.pc[q], total);
+      s.pc[q] = p;
       const double x = static_cast<double>(p) * 0x1p52;
       if (x != trunc(x)) not_exact = 1;
       fsum += static_cast<long long>(x);
@@ -297,7 +306,8 @@ __global__ void __launch_bounds__(NT, 1)
       s.red_d[warp] = dsum;
       s.red_ne[warp] = not_exact;
     }
-    __syncthreads();                                                   // barrier 5
+    if (warp == 0 && r + 1 < n_select) pw_tree_build(m - 1, s, lane);
+    __syncthreads();                                                   // barrier C
     long long fbase, ftot;
     bool exact;
     {
@@ -321,40 +331,50 @@ __global__ void __launch_bounds__(NT, 1)
       // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32).
       if (tid == 0 && fabs(pd - 1.0) > 3.4526698300124393e-04) record_device_error(err, 0x301);
     }
-    // (5) searchsorted(cdf / cdf[-1], u, 'right') = #{cdf entries <= u}
-    int below = 0;
+    // (4) searchsorted(cdf / cdf[-1], u, 'right') counts the entries <= u; the
+    //     cdf is non-decreasing, so the pick is the first position whose entry
+    //     is not <= u (or the last one), and the thread holding it writes it
     if (exact) {
       const long long thr = cdf_threshold(u, ftot);
       long long run = fbase;
-      for (int i = base; i < base + cnt; ++i) {
-        run += static_cast<long long>(static_cast<double>(s.pc[i]) * 0x1p52);
-        below += run <= thr ? 1 : 0;
+      for (int i = lo; i < hi; ++i) {
+        if (!s.avail[i]) continue;
+        const int q = s.pos[i];
+        const long long prev = run;
+        run += static_cast<long long>(static_cast<double>(s.pc[skew(q)]) * 0x1p52);
+        if ((run > thr && (q == 0 || prev <= thr)) || (q == m - 1 && run <= thr)) {
+          s.pick = q;
+          s.sel = i;
+        }
       }
     } else {
       if (tid == 0) {
         double acc = 0.0;
-        for (int i = 0; i < m; ++i) {
-          acc = __dadd_rn(acc, static_cast<double>(s.pc[i]));
-          s.cdf[i] = acc;  // the scaled scores of this draw are consumed
+        for (int q = 0; q < m; ++q) {
+          acc = __dadd_rn(acc, static_cast<double>(s.pc[skew(q)]));
+          s.cdf[q] = acc;
         }
         s.cdf_total = acc;
       }
       __syncthreads();
-      const double cdf_last = s.cdf_total;
-      for (int i = base; i < base + cnt; ++i) below += (__ddiv_rn(s.cdf[i], cdf_last) <= u) ? 1 : 0;
+      const double last = s.cdf_total;
+      for (int i = lo; i < hi; ++i) {
+        if (!s.avail[i]) continue;
+        const int q = s.pos[i];
+        const bool le = __ddiv_rn(s.cdf[q], last) <= u;
+        const bool prev_le = q == 0 || __ddiv_rn(s.cdf[q - 1], last) <= u;
+        if ((!le && prev_le) || (q == m - 1 && le)) {
+          s.pick = q;
+          s.sel = i;
+        }
+      }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) below += __shfl_xor_sync(0xffffffffu, below, off);
-    if (lane == 0) s.red_cnt[warp] = below;
-    __syncthreads();                                                   // barrier 6
-    int pick = lane < W ? s.red_cnt[lane] : 0;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) pick += __shfl_xor_sync(0xffffffffu, pick, off);
-    const int sel = s.pidx[min(pick, m - 1)];
+    __syncthreads();                                                   // barrier D
+    const int pick = s.pick, sel = s.sel;
     if (tid == 0) out_idx[r] = sel;
-    // (6) interaction penalty on every owned score (float32); the owner of
-    //     the pick retires it.  Block-diagonal sim: [n/block, block, block],
-    //     and only the pick's own block has nonzero entries (x - 0 == x).
+    // (5) interaction penalty on every owned score (float32), retire the pick,
+    //     close the gap it leaves.  Block-diagonal sim: [n/block, block,
+    //     block], and only the pick's own block has nonzero entries (x - 0 == x).
     const float* row = sim + (int64_t)sel * n;
     int plo = lo, phi = hi;
     if (block > 0) {
@@ -364,6 +384,8 @@ __global__ void __launch_bounds__(NT, 1)
       phi = min(hi, q0 + block);
     }
     for (int i = plo; i < phi; ++i) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
+    for (int i = lo; i < hi; ++i)
+      if (s.avail[i] && s.pos[i] > pick) s.pos[i] -= 1;
     if (sel >= lo && sel < hi) s.avail[sel] = 0;
   }
 }
