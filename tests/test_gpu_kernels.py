@@ -244,6 +244,31 @@ def test_sketch_dot_and_gram():
     rel_close(out.cpu().numpy(), 2.0 * A.astype(np.float64) @ Bm.T, 1e-5, "gram ab")
 
 
+@pytest.mark.parametrize("ra,rb,k", [(256, 256, 16384), (300, 130, 4100), (17, 260, 64), (5, 3, 3001), (128, 128, 32768)])
+def test_sketch_gram_tensor_core_and_simt(ra, rb, k):
+    """3xTF32 tcgen05 path (k % 4 == 0) and the SIMT path (k % 4 != 0) against float64."""
+    rng = np.random.default_rng(ra * 7 + rb + k)
+    A = (rng.standard_normal((ra, k)) * rng.uniform(0.1, 10.0, (ra, 1))).astype(np.float32)
+    Bm = rng.standard_normal((rb, k)).astype(np.float32)
+    tA, tB = torch.from_numpy(A).to(DEV), torch.from_numpy(Bm).to(DEV)
+    got = ops.sketch_gram(tA, tB, alpha=0.25).cpu().numpy()
+    rel_close(got, 0.25 * A.astype(np.float64) @ Bm.T.astype(np.float64), 2e-5, f"gram {ra}x{rb}x{k}")
+    ops.check_device_error("sketch_gram")
+
+
+def test_sketch_gram_nonfinite():
+    """Entries are non-finite exactly where the f32 product is (an inf may come out as NaN:
+    the split's hi * lo term is inf * 0 when the other operand is exactly a tf32)."""
+    A = torch.randn(8, 256, device=DEV)
+    A[2, 7] = float("inf")
+    A[5, 9] = float("nan")
+    got = ops.sketch_gram(A).cpu().numpy()
+    want = A.cpu().double().numpy() @ A.cpu().double().numpy().T
+    np.testing.assert_array_equal(np.isfinite(got), np.isfinite(want))
+    fin = np.isfinite(want)
+    rel_close(got[fin], want[fin], 2e-5, "finite entries")
+
+
 def test_split_bf16():
     x = torch.randn(10001, device=DEV) * 100
     hi, lo = ops.split_bf16(x)
