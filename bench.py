@@ -41,9 +41,9 @@ N_SELECT, TEMPERATURE, SEED = 64, 1.0, 42
 METRIC = "candidate seqs scored+selected/sec"
 UNIT = "candidates/s"
 WORKLOAD = "isolated single-layer operator: 256 seqs x 1024 tokens, d_in 768 -> d_out 3072, k=16384, AdamW diag"
-# dram__bytes_read.sum + dram__bytes_write.sum per sketch_gemm launch (ncu, this workload);
-# see profiles/sketch_gemm_c2_ncu.md.  None until measured.
-SKETCH_GEMM_DRAM_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum per sketch_gemm launch of this workload
+# (ncu single-pass capture of the bench command, mean of two launches; profiles/kernels_c2.md)
+SKETCH_GEMM_DRAM_BYTES = 4.32e9
 
 
 def parse_args():
