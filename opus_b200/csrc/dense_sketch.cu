@@ -52,25 +52,31 @@ __global__ void __launch_bounds__(kDenseThreads) dense_sketch_kernel(const float
   }
 }
 
-// One CTA per row: 128-bit loads, warp shuffle + shared reduction.
+// One CTA per (row, 4096-element chunk): 128-bit loads, warp shuffle + shared
+// reduction, one f32 atomic per CTA (1024 CTAs for 256 rows of 16384).
+constexpr int kDotChunk = 4096;
+
 __global__ void __launch_bounds__(256) sketch_dot_kernel(const float* __restrict__ phi, const float* __restrict__ tau,
-                                                         int64_t k, float alpha, float* __restrict__ score,
-                                                         int accumulate) {
-  const int64_t row = blockIdx.x;
+                                                         int64_t k, int n_chunks, float alpha,
+                                                         float* __restrict__ score) {
+  const int64_t row = blockIdx.x / n_chunks;
+  const int64_t c0 = (int64_t)(blockIdx.x % n_chunks) * kDotChunk;
+  const int64_t c1 = min(k, c0 + kDotChunk);
   const float* p = phi + row * k;
   float acc = 0.0f;
   if ((k & 3) == 0) {
     const float4* p4 = reinterpret_cast<const float4*>(p);
     const float4* t4 = reinterpret_cast<const float4*>(tau);
-    for (int64_t i = threadIdx.x; i < k / 4; i += 256) {
-      const float4 a = p4[i], b = t4[i];
+#pragma unroll 4
+    for (int64_t i = c0 / 4 + threadIdx.x; i < c1 / 4; i += 256) {
+      const float4 a = __ldcs(p4 + i), b = __ldg(t4 + i);
       acc = fmaf(a.x, b.x, acc);
       acc = fmaf(a.y, b.y, acc);
       acc = fmaf(a.z, b.z, acc);
       acc = fmaf(a.w, b.w, acc);
     }
   } else {
-    for (int64_t i = threadIdx.x; i < k; i += 256) acc = fmaf(p[i], tau[i], acc);
+    for (int64_t i = c0 + threadIdx.x; i < c1; i += 256) acc = fmaf(p[i], tau[i], acc);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
@@ -78,9 +84,9 @@ __global__ void __launch_bounds__(256) sketch_dot_kernel(const float* __restrict
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int i = 0; i < 8; ++i) s += part[i];
-    score[row] = accumulate ? score[row] + alpha * s : alpha * s;
+    float t = 0.0f;
+    for (int i = 0; i < 8; ++i) t += part[i];
+    atomicAdd(score + row, alpha * t);
   }
 }
 
@@ -125,7 +131,14 @@ int opus_sketch_dot(const float* phi, const float* tau, int n_rows, int64_t k, f
   if (n_rows < 0 || k <= 0) return set_error(OPUS_ERR_INVALID, "sketch_dot: bad sizes");
   if (n_rows == 0) return OPUS_OK;
   if (!phi || !tau || !score) return set_error(OPUS_ERR_INVALID, "sketch_dot: NULL pointer");
-  sketch_dot_kernel<<<n_rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(phi, tau, k, alpha, score, accumulate);
+  if (((reinterpret_cast<uintptr_t>(phi) | reinterpret_cast<uintptr_t>(tau)) & 15) != 0 && (k & 3) == 0)
+    return set_error(OPUS_ERR_INVALID, "sketch_dot: phi and tau must be 16-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (!accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(score, 0, (size_t)n_rows * sizeof(float), st));
+  const int64_t n_chunks = (k + kDotChunk - 1) / kDotChunk;
+  const int64_t grid = (int64_t)n_rows * n_chunks;
+  if (grid > 0x7fffffff) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_dot: too many rows");
+  sketch_dot_kernel<<<(int)grid, 256, 0, st>>>(phi, tau, k, (int)n_chunks, alpha, score);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
