@@ -56,6 +56,9 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=B,
                     help="candidates per GPU (default 256; smaller only for profiling captures)")
+    ap.add_argument("--path", default="sketch", choices=["sketch", "ghost"],
+                    help="sketch: the selection step (default line); ghost: exact scores through the ghost "
+                         "contraction against the de-sketched AdamW target (stage 2 on its own, one GPU)")
     args = ap.parse_args()
     return args
 
@@ -284,6 +287,73 @@ def run_gpu(args, rank, world, local_rank):
     return ms_per_step, kern_ms, stages, e2e, clk.summary()
 
 
+def run_ghost(args):
+    """Stage 2 on its own: scores through the ghost contraction, one GPU.
+
+    Per step: tau = CS(V^T) (dense sketch), the de-sketched AdamW target
+    v = D * s * tau[h] as a bf16 hi/lo pair (K2), and the tcgen05 ghost
+    contraction score_b = <dLdZ_b^T a_b, v> (K3, two MMAs per k-step for the
+    hi/lo pair).  The scores equal phi_b . tau of the sketch path.
+    """
+    import torch
+
+    from opus_b200 import ops
+    from opus_b200.train.random_projection import GradientProjector
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nb = args.batch
+    a, dz, V, diag = make_inputs(dev, 0, nb)
+    proj = GradientProjector(sketch_dim=K_SKETCH, seed=SEED, device="cuda")
+    packed = proj.packed_table(D_OUT * D_IN, 0, dev)
+    tau = torch.empty(K_SKETCH, device=dev)
+    score = torch.empty(nb, device=dev)
+    ev = {"s": [], "e": []}
+
+    def step(time_kernel=False):
+        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau)
+        v = ops.desketch(tau, packed, D_OUT, D_IN, diag=diag)
+        if time_kernel:
+            ev["s"].append(torch.cuda.Event(enable_timing=True))
+            ev["e"].append(torch.cuda.Event(enable_timing=True))
+            ev["s"][-1].record()
+        ops.ghost_score(a, dz, v, out=score)
+        if time_kernel:
+            ev["e"][-1].record()
+        return score
+
+    for _ in range(args.warmup):
+        step()
+    ops.check_device_error("ghost warm-up")
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(time_kernel=True)
+        end.record()
+        torch.cuda.synchronize()
+    ops.check_device_error("ghost timed region")
+    ms_per_step = start.elapsed_time(end) / args.steps
+    kern_ms = sum(x.elapsed_time(y) for x, y in zip(ev["s"], ev["e"])) / args.steps
+    burst, sustained, hbm, src = measured_peaks()
+    flops = 2.0 * nb * T * D_OUT * D_IN  # one GEMM per candidate; the hi/lo pair doubles the MMAs
+    achieved = flops / (kern_ms * 1e-3) / 1e12
+    line = {"metric": "candidate seqs scored/sec (ghost path)", "value": round(nb / (ms_per_step / 1e3), 3),
+            "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD if nb == B else WORKLOAD.replace("256 seqs", f"{nb} seqs"),
+                       "path": "target sketch -> de-sketched AdamW target (bf16 hi/lo) -> ghost contraction"},
+            "roofline": {"bound": "tensor", "kernel": "ghost_score", "achieved": round(achieved, 2),
+                         "peak": sustained, "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
+                         "peak_kind": f"bf16 sustained ({src})", "kernel_ms": round(kern_ms, 4),
+                         "flops_per_launch": flops, "mma_flops_per_launch": 2 * flops, "traffic": None},
+            "clocks": clk.summary(), "gpu_launches": 3 * args.steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def cpu_sample(budget_s=10.0, chunk=4, max_cand=B):
     """The NumPy oracle (a port of the reference's CPU path) on a bounded sample of the workload.
 
@@ -366,6 +436,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.path == "ghost":
+        return run_ghost(args)
     import torch
     import torch.distributed as dist
 

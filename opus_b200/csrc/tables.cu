@@ -86,18 +86,47 @@ __global__ void __launch_bounds__(256) build_table_kernel(const uint32_t* __rest
   }
 }
 
+// Four elements per thread: 16-byte loads of the packed table and the
+// diagonal, tau gathered through the read-only cache (k floats, L1-resident
+// for the usual sketch sizes), 8-byte stores of four bf16 hi and four lo.
+__device__ __forceinline__ void desketch_one(float t, uint32_t hv, float d, float scale, __nv_bfloat16& h,
+                                             __nv_bfloat16& l) {
+  float x = __fmul_rn(__fmul_rn(scale, d), t);
+  if (hv & 0x80000000u) x = -x;
+  h = __float2bfloat16_rn(x);
+  l = __float2bfloat16_rn(x - __bfloat162float(h));
+}
+
 __global__ void desketch_kernel(const float* __restrict__ tau, const uint32_t* __restrict__ packed,
                                 const float* __restrict__ diag, const float* __restrict__ v, float eps,
                                 int64_t numel, float scale, __nv_bfloat16* __restrict__ hi,
-                                __nv_bfloat16* __restrict__ lo) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < numel; i += (int64_t)gridDim.x * blockDim.x) {
+                                __nv_bfloat16* __restrict__ lo, int vec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t start = 0;
+  if (vec) {
+    const int64_t n4 = numel / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const uint4 hv = __ldcs(reinterpret_cast<const uint4*>(packed) + i);
+      float4 d = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      if (diag != nullptr) {
+        d = __ldcs(reinterpret_cast<const float4*>(diag) + i);
+      } else if (v != nullptr) {
+        const float4 q = __ldcs(reinterpret_cast<const float4*>(v) + i);
+        d = make_float4(adam_diag(q.x, eps), adam_diag(q.y, eps), adam_diag(q.z, eps), adam_diag(q.w, eps));
+      }
+      __align__(8) __nv_bfloat16 h[4], l[4];
+      desketch_one(__ldg(tau + (hv.x & 0x7FFFFFFFu)), hv.x, d.x, scale, h[0], l[0]);
+      desketch_one(__ldg(tau + (hv.y & 0x7FFFFFFFu)), hv.y, d.y, scale, h[1], l[1]);
+      desketch_one(__ldg(tau + (hv.z & 0x7FFFFFFFu)), hv.z, d.z, scale, h[2], l[2]);
+      desketch_one(__ldg(tau + (hv.w & 0x7FFFFFFFu)), hv.w, d.w, scale, h[3], l[3]);
+      __stcs(reinterpret_cast<uint2*>(hi) + i, *reinterpret_cast<const uint2*>(h));
+      __stcs(reinterpret_cast<uint2*>(lo) + i, *reinterpret_cast<const uint2*>(l));
+    }
+    start = n4 * 4;
+  }
+  for (int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < numel; i += stride) {
     const uint32_t hv = packed[i];
-    const float d = element_weight(diag, v, eps, i);
-    float x = __fmul_rn(__fmul_rn(scale, d), tau[hv & 0x7FFFFFFFu]);
-    if (hv & 0x80000000u) x = -x;
-    const __nv_bfloat16 h = __float2bfloat16_rn(x);
-    hi[i] = h;
-    lo[i] = __float2bfloat16_rn(x - __bfloat162float(h));
+    desketch_one(tau[hv & 0x7FFFFFFFu], hv, element_weight(diag, v, eps, i), scale, hi[i], lo[i]);
   }
 }
 
@@ -329,8 +358,12 @@ int opus_desketch(const float* tau, const uint32_t* packed, const float* diag, c
   if (!tau || !packed || !v_bf16) return set_error(OPUS_ERR_INVALID, "desketch: NULL pointer");
   const int64_t numel = (int64_t)d_out * d_in;
   __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(v_bf16);
-  desketch_kernel<<<grid_for(numel, 256), 256, 0, (cudaStream_t)stream>>>(tau, packed, diag, exp_avg_sq, eps, numel,
-                                                                          scale, hi, hi + numel);
+  __nv_bfloat16* lo = hi + numel;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(diag) |
+                       reinterpret_cast<uintptr_t>(exp_avg_sq);
+  const int vec = (al & 15) == 0 && (reinterpret_cast<uintptr_t>(hi) & 7) == 0 && (reinterpret_cast<uintptr_t>(lo) & 7) == 0;
+  desketch_kernel<<<grid_for(vec ? numel / 4 + 1 : numel, 256), 256, 0, (cudaStream_t)stream>>>(
+      tau, packed, diag, exp_avg_sq, eps, numel, scale, hi, lo, vec);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -290,6 +290,28 @@ def test_ghost_score_matches_oracle(B, T, d_in, d_out):
     rel_close(got.cpu().numpy(), want, 1e-4, "ghost")
 
 
+@pytest.mark.parametrize("d_out,d_in,precond", [(384, 256, "diag"), (384, 256, "adam"), (64, 96, "none"),
+                                                 (7, 9, "adam"), (3, 5, "diag")])
+def test_desketch_bit_exact(d_out, d_in, precond):
+    """v = scale * D * s * tau[h] as bf16 hi and lo = bf16(v - hi); 4-wide and scalar paths."""
+    k = 1000
+    h, s, packed = cuda_tables(d_out * d_in, 2, k)
+    rng = np.random.default_rng(d_out * d_in)
+    tau = rng.standard_normal(k).astype(np.float32)
+    w = rng.uniform(1e-9, 1e-3, (d_out, d_in)).astype(np.float32)
+    kw = {"diag": dict(diag=torch.from_numpy(w).to(DEV)), "adam": dict(exp_avg_sq=torch.from_numpy(w).to(DEV)),
+          "none": {}}[precond]
+    got = ops.desketch(torch.from_numpy(tau).to(DEV), packed, d_out, d_in, scale=0.75, eps=1e-8, **kw)
+    d = {"diag": w, "adam": orc.inv_rms(w, 1e-8), "none": np.ones_like(w)}[precond].reshape(-1)
+    x = (np.float32(0.75) * d) * tau[h]
+    x = np.where(s < 0, -x, x).astype(np.float32)
+    hi = orc.bf16_round(x)
+    lo = orc.bf16_round((x - hi).astype(np.float32))
+    g = got.float().cpu().numpy().reshape(2, -1)
+    np.testing.assert_array_equal(g[0], hi)
+    np.testing.assert_array_equal(g[1], lo)
+
+
 def test_ghost_equals_sketch_dot_through_desketch():
     """<G_b, D s tau[h]> by the ghost kernel == CS(D o G_b) . tau by the sketch kernels."""
     B, T, d_out, d_in, k = 4, 256, 384, 256, 4096
