@@ -21,7 +21,7 @@ import torch
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))  # tests/ for tiny_model
 
-from tiny_model import MuonLike, ProxyLoader, TinyLM, state_to_numpy, zipf_tokens  # noqa: E402
+from tiny_model import MuonLike, ProxyLoader, TinyLM, lora_factory, state_to_numpy, zipf_tokens  # noqa: E402
 
 
 def save(name: str, **arrays) -> None:
@@ -192,6 +192,50 @@ def gen_wholepath(ds, ref_linear):
              np_seed=np.array(77), **{f"w/{k}": v for k, v in weights.items()}, **opt_arrays)
 
 
+LORA_SCENARIOS = {"lora_proj": True, "lora_noproj": False}
+
+
+def build_lora_workload(rng, ref_lora, B=6, n=2, T=128, vocab=256):
+    """TinyLM whose capture layers are rank-4 LoRA linears, with nonzero B so both factors carry gradient."""
+    torch.manual_seed(0)
+    model = TinyLM(lora_factory(ref_lora), vocab=vocab)
+    gc = [m for m in model.modules() if isinstance(m, ref_lora)]
+    with torch.no_grad():
+        for m in gc:
+            m.lora_B.copy_(torch.from_numpy((rng.standard_normal(tuple(m.lora_B.shape)) * 0.1).astype(np.float32)))
+    params = [p for m in gc for p in (m.lora_A, m.lora_B)]
+    adam = torch.optim.AdamW(params, lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    opt_arrays = {}
+    for j, p in enumerate(params):
+        v = rng.uniform(1e-6, 1e-3, tuple(p.shape)).astype(np.float32)
+        adam.state[p] = {"step": torch.tensor(3.0), "exp_avg": torch.zeros_like(p), "exp_avg_sq": torch.from_numpy(v)}
+        opt_arrays[f"adam_v{j}"] = v
+    cand = zipf_tokens(rng, B, T, vocab)
+    prox = zipf_tokens(rng, n, T, vocab)
+    return model, cand, prox, adam, opt_arrays
+
+
+def gen_wholepath_lora(ds, ref_lora):
+    for si, (name, proj_on) in enumerate(LORA_SCENARIOS.items()):
+        rng = np.random.default_rng(300 + si)
+        model, cand, prox, adam, opt_arrays = build_lora_workload(rng, ref_lora)
+        weights = state_to_numpy(model)
+        if proj_on:
+            ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+        else:
+            ds.initialize_projector(enabled=False)
+        ct, pt = torch.from_numpy(cand), torch.from_numpy(prox)
+        batch_train = {"input_ids": ct, "attention_mask": torch.ones_like(ct), "labels": ct.clone()}
+        loader = ProxyLoader({"input_ids": pt, "attention_mask": torch.ones_like(pt), "labels": pt.clone()})
+        layers = ds.find_GClayers(model)
+        scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device("cpu"), batch_train, loader, adam, layers,
+                                                      preconditioner="adamw", score_len=128, per_val=False,
+                                                      return_tracin_and_similarity=True)
+        save(f"wholepath_{name}", cand=cand, prox=prox, scores=scores, sim=sim,
+             cfg=np.array([int(proj_on), 0]), precond=np.array("adamw"), opt_kind=np.array("lora_adamw"),
+             **{f"w/{k}": v for k, v in weights.items()}, **opt_arrays)
+
+
 def gen_windows(ds):
     out = {}
     x = torch.arange(6 * 512, dtype=torch.int64).view(6, 512)
@@ -241,13 +285,18 @@ def gen_muon(ds):
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", default=None, help="regenerate one fixture family (e.g. lora)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import OPUS.train.data_selection as ds  # reference package
     import OPUS.train.random_projection as rp
     from OPUS.layers.linear import GCLinear
+    from OPUS.layers.lora_layers import GCLoRALinear
 
     torch.set_num_threads(8)
+    if args.only == "lora":
+        gen_wholepath_lora(ds, GCLoRALinear)
+        return 0
     gen_tables(rp)
     gen_project(rp)
     gen_select(ds)
@@ -255,6 +304,7 @@ def main() -> int:
     gen_layer_bf16(rp)
     gen_muon(ds)
     gen_wholepath(ds, GCLinear)
+    gen_wholepath_lora(ds, GCLoRALinear)
     return 0
 
 

@@ -5,7 +5,7 @@ import torch
 
 from conftest import load_golden
 from opus_b200.train import data_selection as ds
-from test_host_logic import SCENARIOS, assert_close_scores, rebuild
+from test_host_logic import LORA_SCENARIOS, SCENARIOS, assert_close_scores, rebuild, rebuild_lora
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -25,6 +25,21 @@ def test_compute_scores_match_reference(name):
                                                   ds.find_GClayers(model), preconditioner=str(g["precond"]),
                                                   score_len=128, per_val=per_val)
     assert isinstance(scores, np.ndarray) and scores.dtype == np.float32
+    assert_close_scores(scores, g["scores"])
+    assert_close_scores(sim, g["sim"])
+
+
+@pytest.mark.parametrize("name", LORA_SCENARIOS)
+def test_lora_scores_match_reference(name):
+    """GCLoRALinear layers through the device path: rank-4 factors padded to the kernels' widths."""
+    g = load_golden(f"wholepath_{name}")
+    model, opt, loader, batch = rebuild_lora(g, device=DEV)
+    if bool(g["cfg"][0]):
+        ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    else:
+        ds.initialize_projector(enabled=False)
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), batch, loader, opt,
+                                                  ds.find_GClayers(model), preconditioner="adamw", score_len=128)
     assert_close_scores(scores, g["scores"])
     assert_close_scores(sim, g["sim"])
 

@@ -8,7 +8,7 @@ from conftest import load_golden
 from oracle import opus_oracle as orc
 from opus_b200.layers import GCLinear, GCLoRALinear, LoRALinear
 from opus_b200.train import data_selection as ds
-from tiny_model import MuonLike, ProxyLoader, TinyLM, load_numpy_state
+from tiny_model import MuonLike, ProxyLoader, TinyLM, load_numpy_state, lora_factory
 
 SCENARIOS = ["adamw_proj", "adamw_proj_perval", "adamw_noproj", "sgd_proj", "sgd_noproj", "muon_proj", "auto_mixed"]
 
@@ -41,6 +41,27 @@ def rebuild(g, device="cpu"):
     return model, (opts if len(opts) > 1 else opts[0]), loader, batch
 
 
+LORA_SCENARIOS = ["lora_proj", "lora_noproj"]
+
+
+def rebuild_lora(g, device="cpu"):
+    """TinyLM with this package's rank-4 GCLoRALinear layers, weights and AdamW state from a fixture."""
+    model = TinyLM(lora_factory(GCLoRALinear))
+    load_numpy_state(model, g)
+    model.to(device)
+    gc = [m for m in model.modules() if isinstance(m, GCLoRALinear)]
+    params = [p for m in gc for p in (m.lora_A, m.lora_B)]
+    adam = torch.optim.AdamW(params, lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for j, p in enumerate(params):
+        adam.state[p] = {"step": torch.tensor(3.0), "exp_avg": torch.zeros_like(p),
+                         "exp_avg_sq": torch.from_numpy(g[f"adam_v{j}"]).to(device)}
+    cand = torch.from_numpy(g["cand"]).to(device)
+    prox = torch.from_numpy(g["prox"]).to(device)
+    loader = ProxyLoader({"input_ids": prox, "attention_mask": torch.ones_like(prox), "labels": prox.clone()})
+    batch = {"input_ids": cand, "attention_mask": torch.ones_like(cand), "labels": cand.clone()}
+    return model, adam, loader, batch
+
+
 def assert_close_scores(got, want, rtol=1e-3):
     got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
     scale = np.abs(want).max()
@@ -63,6 +84,29 @@ def test_wholepath_oracle_matches_reference(name):
         diag = None if pl.exp_avg_sq is None else orc.inv_rms(pl.exp_avg_sq.numpy(), pl.eps)
         sc, sm = orc.layer_scores(pl.g_t.float().numpy(), pl.a_t.numpy(), pl.g_v.numpy(), pl.a_v.numpy(), h, s,
                                   1024, C=pl.c, diag=diag, per_val=per_val, projection=proj_on)
+        score += sc
+        sim += sm
+    assert_close_scores(score, g["scores"])
+    assert_close_scores(sim, g["sim"])
+
+
+@pytest.mark.parametrize("name", LORA_SCENARIOS)
+def test_wholepath_lora_oracle_matches_reference(name):
+    """LoRA layers: two (dL/dZ, A) pairs per layer, AdamW state on lora_A and lora_B."""
+    g = load_golden(f"wholepath_{name}")
+    proj_on = bool(g["cfg"][0])
+    model, opt, loader, batch = rebuild_lora(g)
+    layers = ds.find_GClayers(model)
+    pairs, B, n = ds.capture_pairs(model, batch, loader, layers, score_len=128)
+    assert len(pairs) == 2 * len(layers)
+    plans = ds.plan_layers(pairs, opt, "adamw", "cpu")
+    score, sim = np.zeros(B), np.zeros((B, B))
+    for pl in plans:
+        d_out, d_in = pl.g_t.shape[-1], pl.a_t.shape[-1]
+        h, s = orc.hash_sign_tables(d_out * d_in, pl.pid, 1024, seed=42)
+        diag = None if pl.exp_avg_sq is None else orc.inv_rms(pl.exp_avg_sq.numpy(), pl.eps)
+        sc, sm = orc.layer_scores(pl.g_t.float().numpy(), pl.a_t.numpy(), pl.g_v.numpy(), pl.a_v.numpy(), h, s,
+                                  1024, C=pl.c, diag=diag, projection=proj_on)
         score += sc
         sim += sm
     assert_close_scores(score, g["scores"])

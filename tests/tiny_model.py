@@ -41,6 +41,15 @@ class TinyLM(nn.Module):
         return logits
 
 
+def lora_factory(cls, r: int = 4, alpha: int = 8):
+    """TinyLM capture-layer constructor for a LoRA linear of rank r (LoRALinear has no bias)."""
+
+    def make(in_features: int, out_features: int, bias: bool = False):
+        return cls(in_features, out_features, r=r, lora_alpha=alpha)
+
+    return make
+
+
 class MuonLike:
     """Minimal optimizer exposing a momentum group and momentum buffers (Muon's state layout)."""
 
