@@ -56,6 +56,12 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=B,
                     help="candidates per GPU (default 256; smaller only for profiling captures)")
+    ap.add_argument("--workload", default="operator", choices=["operator", "gpt2-small"],
+                    help="operator: the single-layer operator (default line); gpt2-small: the whole selection "
+                         "path (capture, 48 layers, selection) on a GPT-2-small-shaped model, with the "
+                         "selection overhead as a share of one training step")
+    ap.add_argument("--model-dtype", default="f32", choices=["f32", "bf16"],
+                    help="gpt2-small: parameter and activation dtype (f32 as in the GPT-2-small config)")
     ap.add_argument("--path", default="sketch", choices=["sketch", "ghost"],
                     help="sketch: the selection step (default line); ghost: exact scores through the ghost "
                          "contraction against the de-sketched AdamW target (stage 2 on its own, one GPU)")
@@ -354,6 +360,156 @@ def run_ghost(args):
     return 0
 
 
+def gpt2_small(linear_cls, vocab=50257, d=768, n_layer=12, n_head=12, ctx=1024):
+    """A GPT-2-small-shaped causal LM (random init) whose four linears per block are capture layers.
+
+    The selection path's workload only: 12 blocks of pre-LayerNorm attention
+    (fused qkv, output projection) and a 4x GELU MLP, tied output embedding;
+    48 capture layers holding 84,934,656 weights.  The forward signature is
+    the one the selection code calls.
+    """
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln1, self.ln2 = nn.LayerNorm(d), nn.LayerNorm(d)
+            self.qkv, self.proj = linear_cls(d, 3 * d), linear_cls(d, d)
+            self.fc, self.out = linear_cls(d, 4 * d), linear_cls(4 * d, d)
+
+        def forward(self, x):
+            b, t, _ = x.shape
+            q, k, v = self.qkv(self.ln1(x)).split(d, dim=2)
+            q, k, v = (z.view(b, t, n_head, d // n_head).transpose(1, 2) for z in (q, k, v))
+            y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            x = x + self.proj(y.transpose(1, 2).reshape(b, t, d))
+            return x + self.out(F.gelu(self.fc(self.ln2(x))))
+
+    class GPT(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.wte, self.wpe = nn.Embedding(vocab, d), nn.Embedding(ctx, d)
+            self.blocks = nn.ModuleList(Block() for _ in range(n_layer))
+            self.ln_f = nn.LayerNorm(d)
+
+        def forward(self, input_seq, target_seq=None, sliding_window_num_blocks=None):
+            if input_seq.ndim == 1:
+                input_seq = input_seq[None]
+            x = self.wte(input_seq) + self.wpe(torch.arange(input_seq.shape[1], device=input_seq.device))
+            for blk in self.blocks:
+                x = blk(x)
+            logits = F.linear(self.ln_f(x), self.wte.weight)
+            if target_seq is not None:
+                return F.cross_entropy(logits.float().view(-1, logits.size(-1)), target_seq.reshape(-1))
+            return logits
+
+    return GPT()
+
+
+def run_gpt2(args):
+    """The whole selection path on a GPT-2-small-shaped model, one GPU.
+
+    Candidates: 64 sequences x 1024 tokens drawn Zipf(1.1) over the 50257-token
+    vocabulary; proxy: 16 more; k = 8192; AdamW preconditioner (beta2 0.95,
+    second moments 1e-4); keep 16 by Boltzmann sampling at temperature 1.0.
+    The model is random-init f32.  One step is one get_batch_opus call
+    (capture forward + backward, 48 layers of sketches, scores, similarity,
+    selection); the training step it is compared with is forward, backward and
+    AdamW on the 16 kept sequences.
+    """
+    import numpy as np
+    import torch
+
+    from opus_b200 import ops
+    from opus_b200.layers import GCLinear
+    from opus_b200.train import data_selection as ds
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    n_cand, n_proxy, seq, vocab, k_dim, keep = 64, 16, 1024, 50257, 8192, 16
+    mdt = torch.bfloat16 if args.model_dtype == "bf16" else torch.float32
+    model = gpt2_small(GCLinear, vocab=vocab).to(device=dev, dtype=mdt)
+    layers = ds.find_GClayers(model)
+    opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for p in model.parameters():
+        opt.state[p] = {"step": torch.tensor(1.0), "exp_avg": torch.zeros_like(p),
+                        "exp_avg_sq": torch.full_like(p, 1e-4, dtype=torch.float32)}
+    rng = np.random.default_rng(0)
+    ranks = np.arange(1, vocab + 1, dtype=np.float64) ** -1.1
+    zipf = lambda n: torch.from_numpy(rng.choice(vocab, size=(n, seq), p=ranks / ranks.sum())).to(dev)  # noqa: E731
+    buf = zipf(n_cand)
+    prox = zipf(n_proxy)
+
+    class Loader:
+        _fixed_batch = {"input_ids": prox, "attention_mask": torch.ones_like(prox), "labels": prox.clone()}
+
+    loader = Loader()
+    ds.initialize_projector(sketch_dim=k_dim, seed=SEED, device="cuda", enabled=True)
+    np.random.seed(1)
+
+    def select():
+        return ds.get_batch_opus(model, buf, buf.clone(), None, None, opt, layers, loader, keep / n_cand, seq,
+                                 selection_method="stochastic", temperature=1.0, score_len=seq,
+                                 preconditioner="adamw")
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    for _ in range(max(1, args.warmup)):
+        idx = select()
+    ops.check_device_error("gpt2 warm-up")
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 5))
+    s0, s1 = ev(), ev()
+    with ClockSampler(0) as clk:
+        s0.record()
+        for _ in range(steps):
+            idx = select()
+        s1.record()
+        torch.cuda.synchronize()
+    sel_ms = s0.elapsed_time(s1) / steps
+    # stage 1 alone: forward over candidates + proxies, dL/dZ of every capture layer
+    c0, c1 = ev(), ev()
+    batch = {"input_ids": buf, "attention_mask": torch.ones_like(buf), "labels": buf.clone()}
+    c0.record()
+    pairs, _, _ = ds.capture_pairs(model, dict(batch), loader, layers, seq)
+    c1.record()
+    torch.cuda.synchronize()
+    cap_ms = c0.elapsed_time(c1)
+    del pairs
+    # the training step on the kept sequences: forward, backward, AdamW
+    train_opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    kept = buf[idx]
+    for _ in range(2):
+        train_opt.zero_grad(set_to_none=True)
+        model(kept, kept).backward()
+        train_opt.step()
+    torch.cuda.synchronize()
+    t0, t1 = ev(), ev()
+    t0.record()
+    for _ in range(steps):
+        train_opt.zero_grad(set_to_none=True)
+        model(kept, kept).backward()
+        train_opt.step()
+    t1.record()
+    torch.cuda.synchronize()
+    train_ms = t0.elapsed_time(t1) / steps
+    line = {"metric": METRIC, "value": round(n_cand / (sel_ms / 1e3), 3), "unit": UNIT, "n_gpus": 1,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(sel_ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": args.model_dtype, "data": "synthetic",
+            "config": {"workload": "GPT-2-small-shaped model (12 x 768, MLP 3072, vocab 50257, T 1024), random "
+                                   f"init {args.model_dtype}: 64 candidates + 16 proxies, 48 capture layers, "
+                                   "k=8192, AdamW, keep 16 by Boltzmann T=1.0", "api": "get_batch_opus"},
+            "selection_overhead_pct_of_train_step": round(100.0 * sel_ms / train_ms, 2),
+            "capture_ms": round(cap_ms, 3), "train_step_ms_16_seqs": round(train_ms, 3),
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def cpu_sample(budget_s=10.0, chunk=4, max_cand=B):
     """The NumPy oracle (a port of the reference's CPU path) on a bounded sample of the workload.
 
@@ -438,6 +594,8 @@ def main():
         return run_reference(args)
     if args.path == "ghost":
         return run_ghost(args)
+    if args.workload == "gpt2-small":
+        return run_gpt2(args)
     import torch
     import torch.distributed as dist
 
