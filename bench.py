@@ -60,6 +60,9 @@ def parse_args():
                     help="operator: the single-layer operator (default line); gpt2-small: the whole selection "
                          "path (capture, 48 layers, selection) on a GPT-2-small-shaped model, with the "
                          "selection overhead as a share of one training step")
+    ap.add_argument("--selection", default="global", choices=["global", "local"],
+                    help="N>1: one global draw over all ranks' candidates (default), or each rank drawing from "
+                         "its own shard (the reference's default training mode)")
     ap.add_argument("--model-dtype", default="f32", choices=["f32", "bf16"],
                     help="gpt2-small: parameter and activation dtype (f32 as in the GPT-2-small config)")
     ap.add_argument("--path", default="sketch", choices=["sketch", "ghost"],
@@ -156,7 +159,8 @@ def run_gpu(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     nb = args.batch
     n_sel_local = max(1, nb // 4)
-    n_sel = n_sel_local * world  # one global draw over all ranks' candidates
+    local = args.selection == "local" or world == 1
+    n_sel = n_sel_local if local else n_sel_local * world  # global: one draw over all ranks' candidates
     a, dz, V, diag = make_inputs(dev, rank, nb)
     proj = GradientProjector(sketch_dim=K_SKETCH, seed=SEED, device="cuda")
     pid = 0
@@ -171,7 +175,7 @@ def run_gpu(args, rank, world, local_rank):
     ev = {}
 
     def select(score_, sim_):
-        if world == 1:
+        if local:
             return ops.boltzmann_select(score_, sim_, n_sel, TEMPERATURE, uni)
         scores_all, blocks = sd.gather_scores_and_blocks(score_, sim_)
         return ops.boltzmann_select(scores_all, blocks, n_sel, TEMPERATURE, uni)
@@ -236,14 +240,15 @@ def run_gpu(args, rank, world, local_rank):
         evs[5].record()
         ops.sketch_gram(phi, out=sim)
         evs[6].record()
-        scores_all, blocks = sd.gather_scores_and_blocks(score, sim) if world > 1 else (score, sim)
+        scores_all, blocks = sd.gather_scores_and_blocks(score, sim) if not local else (score, sim)
         evs[7].record()
         ops.boltzmann_select(scores_all, blocks, n_sel, TEMPERATURE, uni)
         evs[8].record()
         torch.cuda.synchronize()
         for i in range(len(names)):
             acc[i] += evs[i].elapsed_time(evs[i + 1]) / reps
-    stages = {n: round(x, 4) for n, x in zip(names, acc) if world > 1 or n not in ("allreduce", "gather")}
+    stages = {n: round(x, 4) for n, x in zip(names, acc)
+              if (world > 1 or n != "allreduce") and (not local or n != "gather")}
 
     # end to end through the public API with host buffers
     e2e = None
@@ -263,7 +268,7 @@ def run_gpu(args, rank, world, local_rank):
             tau_e = proj.project_vector(V_d.T, pid)
             sc = ops.sketch_dot(phi_e, tau_e)
             sm = ops.sketch_gram(phi_e)
-            if world == 1:
+            if local:
                 return ds.stochastic_greedy_selection(sc, sm, n_sel, temperature=TEMPERATURE)
             gidx, _ = sd.select_global(sc, sm, n_sel, method="stochastic", temperature=TEMPERATURE)
             return gidx.cpu()
@@ -288,7 +293,7 @@ def run_gpu(args, rank, world, local_rank):
         h2d = sum(x.numel() * x.element_size() for x in (a_h, dz_h, V_h, diag_h))
         e2e = {"value": round(nb * world / (e_ms / e2e_steps / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": n_sel * 8, "api": "GradientProjector.project_full_gradient + "
-               "project_vector + " + ("stochastic_greedy_selection" if world == 1 else "distributed.select_global"),
+               "project_vector + " + ("stochastic_greedy_selection" if local else "distributed.select_global"),
                "steps": e2e_steps}
     return ms_per_step, kern_ms, stages, e2e, clk.summary()
 
@@ -633,11 +638,16 @@ def main():
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": WORKLOAD if nb == B else WORKLOAD.replace("256 seqs", f"{nb} seqs"),
                            "global_batch": nb * world, "seq_len": T, "k": K_SKETCH,
-                           "select": f"{max(1, nb // 4) * world} of {nb * world} in one global Boltzmann draw, "
-                                     f"T={TEMPERATURE}",
-                           "parallelism": (f"dp{world}: candidates sharded, target sketch rows sharded + NCCL "
-                                           "all-reduce, scores and similarity blocks all-gathered, global draw "
-                                           "with the block-diagonal interaction matrix") if world > 1 else "dp1",
+                           "select": (f"{max(1, nb // 4) * world} of {nb * world} in one global Boltzmann draw, "
+                                      f"T={TEMPERATURE}") if (world > 1 and args.selection == "global") else
+                                     (f"{max(1, nb // 4)} of {nb} per GPU, Boltzmann T={TEMPERATURE}"),
+                           "parallelism": ((f"dp{world}: candidates sharded, target sketch rows sharded + NCCL "
+                                            "all-reduce, scores and similarity blocks all-gathered, global draw "
+                                            "with the block-diagonal interaction matrix")
+                                           if args.selection == "global" else
+                                           (f"dp{world}: candidates sharded, target sketch rows sharded + NCCL "
+                                            "all-reduce, each rank draws from its own shard"))
+                                          if world > 1 else "dp1",
                            "l2": "inputs 2.0 GB per GPU > 126 MB L2, no flush"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
                 "gpu_launches": 6 * args.steps, "stage_ms": stages}
