@@ -63,6 +63,10 @@ def parse_args():
     ap.add_argument("--selection", default="global", choices=["global", "local"],
                     help="N>1: one global draw over all ranks' candidates (default), or each rank drawing from "
                          "its own shard (the reference's default training mode)")
+    ap.add_argument("--global-sim", default="block", choices=["block", "exact"],
+                    help="global draw: block-diagonal similarity (only scores and local blocks cross GPUs) or "
+                         "the exact dense one (every layer's sketches all-gathered, as the reference's global "
+                         "mode scores everything on one rank)")
     ap.add_argument("--model-dtype", default="f32", choices=["f32", "bf16"],
                     help="gpt2-small: parameter and activation dtype (f32 as in the GPT-2-small config)")
     ap.add_argument("--path", default="sketch", choices=["sketch", "ghost"],
@@ -171,14 +175,23 @@ def run_gpu(args, rank, world, local_rank):
     phi = torch.empty(nb, K_SKETCH, device=dev)
     tau = torch.empty(K_SKETCH, device=dev)
     score = torch.empty(nb, device=dev)
-    sim = torch.empty(nb, nb, device=dev)
+    exact = args.global_sim == "exact" and not local
+    sim = torch.empty(nb, nb * world if exact else nb, device=dev)
     ev = {}
 
-    def select(score_, sim_):
+    def similarity(phi_):
+        ops.sketch_gram(phi_, sd.gather_sketches(phi_) if exact else phi_, out=sim)
+
+    def gather(score_, sim_):
         if local:
-            return ops.boltzmann_select(score_, sim_, n_sel, TEMPERATURE, uni)
-        scores_all, blocks = sd.gather_scores_and_blocks(score_, sim_)
-        return ops.boltzmann_select(scores_all, blocks, n_sel, TEMPERATURE, uni)
+            return score_, sim_
+        if exact:
+            return sd._gather_scores(score_), sd.gather_similarity_rows(sim_)
+        return sd.gather_scores_and_blocks(score_, sim_)
+
+    def select(score_, sim_):
+        scores_all, mat = gather(score_, sim_)
+        return ops.boltzmann_select(scores_all, mat, n_sel, TEMPERATURE, uni)
 
     def step(time_kernel=False):
         table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
@@ -193,7 +206,7 @@ def run_gpu(args, rank, world, local_rank):
         if time_kernel:
             ev["e"][-1].record()
         ops.sketch_dot(phi, tau, out=score)
-        ops.sketch_gram(phi, out=sim)
+        similarity(phi)
         return select(score, sim)
 
     for _ in range(args.warmup):
@@ -238,9 +251,9 @@ def run_gpu(args, rank, world, local_rank):
         evs[4].record()
         ops.sketch_dot(phi, tau, out=score)
         evs[5].record()
-        ops.sketch_gram(phi, out=sim)
+        similarity(phi)
         evs[6].record()
-        scores_all, blocks = sd.gather_scores_and_blocks(score, sim) if not local else (score, sim)
+        scores_all, blocks = gather(score, sim)
         evs[7].record()
         ops.boltzmann_select(scores_all, blocks, n_sel, TEMPERATURE, uni)
         evs[8].record()
@@ -644,6 +657,8 @@ def main():
                            "parallelism": ((f"dp{world}: candidates sharded, target sketch rows sharded + NCCL "
                                             "all-reduce, scores and similarity blocks all-gathered, global draw "
                                             "with the block-diagonal interaction matrix")
+                                           + ("; exact dense similarity: each layer's sketches all-gathered"
+                                              if args.global_sim == "exact" else "")
                                            if args.selection == "global" else
                                            (f"dp{world}: candidates sharded, target sketch rows sharded + NCCL "
                                             "all-reduce, each rank draws from its own shard"))

@@ -18,11 +18,15 @@ picks.  Here each rank scores the candidates it already holds:
    with the block-diagonal interaction matrix, so the picks agree without a
    broadcast; each rank keeps the picks that fall in its shard.
 
-The similarity between candidates on different ranks is zero here (only
-scores and the local blocks cross GPUs), so the picks equal a single-process
-selection over the concatenated scores with the block-diagonal matrix, not
-the reference's dense one; the per-candidate scores are the reference's.
-Every rank must hold the same number of candidates.
+By default the similarity between candidates on different ranks is zero
+(only scores and the local blocks cross GPUs), so the picks equal a
+single-process selection over the concatenated scores with the
+block-diagonal matrix.  With exact_similarity=True every rank also
+all-gathers each layer's candidate sketches and forms its full row block of
+the similarity, the row blocks are all-gathered, and the draw uses the dense
+matrix: the picks are then those of the reference's global mode, which
+scores every candidate on rank 0.  Every rank must hold the same number of
+candidates.
 """
 from __future__ import annotations
 
@@ -71,6 +75,16 @@ def gather_scores_and_blocks(score: torch.Tensor, sim: torch.Tensor, group=None)
     return torch.cat(scores), torch.stack(blocks)
 
 
+def _gather_scores(score: torch.Tensor, group=None) -> torch.Tensor:
+    _, world = rank_and_world(group)
+    score = score.reshape(-1).contiguous()
+    if world == 1:
+        return score
+    parts = [torch.empty_like(score) for _ in range(world)]
+    dist.all_gather(parts, score, group=group)
+    return torch.cat(parts)
+
+
 def shared_uniforms(n_select: int, device, group=None, src: int = 0) -> torch.Tensor:
     """n_select doubles from rank src's NumPy global stream (np.random.choice's draws), on every rank."""
     rank, world = rank_and_world(group)
@@ -90,15 +104,44 @@ def local_picks(global_idx: torch.Tensor, rank: int, b_local: int) -> torch.Tens
     return global_idx[mask] - lo
 
 
+def gather_sketches(phi: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather one layer's candidate sketches [B_loc, k] -> [W*B_loc, k] in rank order."""
+    _, world = rank_and_world(group)
+    phi = phi.contiguous()
+    if world == 1:
+        return phi
+    parts = [torch.empty_like(phi) for _ in range(world)]
+    dist.all_gather(parts, phi, group=group)
+    return torch.cat(parts)
+
+
+def gather_similarity_rows(sim_rows: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather row blocks [B_loc, W*B_loc] of the dense similarity -> [W*B_loc, W*B_loc]."""
+    _, world = rank_and_world(group)
+    sim_rows = sim_rows.contiguous()
+    if world == 1:
+        return sim_rows
+    parts = [torch.empty_like(sim_rows) for _ in range(world)]
+    dist.all_gather(parts, sim_rows, group=group)
+    return torch.cat(parts)
+
+
 def select_global(score: torch.Tensor, sim: torch.Tensor, n_select: int, method: str = "stochastic",
                   temperature: float = 1.0, uniforms: torch.Tensor | None = None, group=None):
     """Steps 3-4: gather, then the identical global draw on every rank.
 
-    score [B_loc] and sim [B_loc, B_loc] are this rank's (CUDA tensors).
-    Returns (global indices [n_select] int64, this rank's picks as local indices).
+    score [B_loc] is this rank's; sim is its local block [B_loc, B_loc], or
+    its row block [B_loc, W*B_loc] of the dense similarity (exact global
+    similarity).  Returns (global indices [n_select] int64, this rank's picks
+    as local indices).
     """
-    rank, _ = rank_and_world(group)
-    scores, blocks = gather_scores_and_blocks(score, sim, group)
+    rank, world = rank_and_world(group)
+    b = score.numel()
+    if sim.dim() == 2 and sim.shape == (b, b * world) and world > 1:
+        scores = _gather_scores(score, group)
+        blocks = gather_similarity_rows(sim, group)
+    else:
+        scores, blocks = gather_scores_and_blocks(score, sim, group)
     n = scores.numel()
     if method == "greedy":
         idx = ops.greedy_select(scores, blocks, int(n_select))
@@ -139,13 +182,16 @@ def broadcast_batch(batch: dict | None, device, group=None, src: int = 0) -> dic
 
 
 def score_shard(model, device, batch_train, proxy_share, n_proxy_total, optimizer, trainable_layers,
-                preconditioner="adamw", score_len=512, group=None):
-    """Steps 1-2 on one rank: scores [B_loc] and local similarity [B_loc, B_loc].
+                preconditioner="adamw", score_len=512, group=None, exact_similarity=False):
+    """Steps 1-2 on one rank: scores [B_loc] and similarity.
 
     proxy_share is this rank's rows of the round's proxy batch (possibly
     none); the per-layer proxy sketch sums are all-reduced so every rank
-    scores against the mean over all n_proxy_total proxies.  Needs the
-    CountSketch projector (initialize_projector(enabled=True)).
+    scores against the mean over all n_proxy_total proxies.  The similarity
+    is the local block [B_loc, B_loc], or with exact_similarity the row block
+    [B_loc, W*B_loc] against every rank's candidates (one all-gather of the
+    sketches per layer).  Needs the CountSketch projector
+    (initialize_projector(enabled=True)).
     """
     projector = ds.get_projector()
     if projector is None or not projector.enabled:
@@ -167,26 +213,31 @@ def score_shard(model, device, batch_train, proxy_share, n_proxy_total, optimize
             projector.sketch(g_v, a_v, pl.pid, rows_div=g_v.shape[0], out=taus[li:li + 1], accumulate=True)
     allreduce_target_sketches(taus, group)
 
+    _, world = rank_and_world(group)
     score = torch.zeros(train_bs, device=device, dtype=torch.float32)
-    sim = torch.zeros(train_bs, train_bs, device=device, dtype=torch.float32)
+    cols = train_bs * world if exact_similarity else train_bs
+    sim = torch.zeros(train_bs, cols, device=device, dtype=torch.float32)
     for li, pl in enumerate(plans):
         g_t, a_t, _, _ = shaped(pl)
         phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
         if n_proxy_total > 0:
             ops.sketch_dot(phi_t, taus[li], alpha=pl.c / n_proxy_total, out=score, accumulate=True)
-        ops.sketch_gram(phi_t, alpha=pl.c * pl.c, out=sim, accumulate=True)
-        del phi_t
+        other = gather_sketches(phi_t, group) if exact_similarity else phi_t
+        ops.sketch_gram(phi_t, other, alpha=pl.c * pl.c, out=sim, accumulate=True)
+        del phi_t, other
     return score, sim
 
 
 def get_batch_opus_global(model, buffer_seq, buffer_labels, optimizer, trainable_layers, validation_loader,
                           selection_ratio, seq_len, selection_method="greedy", temperature=1.5, score_len=512,
-                          preconditioner="adamw", group=None):
+                          preconditioner="adamw", group=None, exact_similarity=False):
     """One global OPUS selection over the candidates of all ranks (the global mode of train.py:1100-1178).
 
     Every rank passes its own candidate shard (the same number of sequences
     on every rank).  Returns (global indices [K] on every rank, this rank's
     picks as indices into its buffer), K = max(1, int(N_global * ratio)).
+    exact_similarity: the dense cross-rank similarity (the reference's global
+    mode) instead of the block-diagonal one.
     """
     rank, world = rank_and_world(group)
     device = buffer_seq.device
@@ -208,6 +259,7 @@ def get_batch_opus_global(model, buffer_seq, buffer_labels, optimizer, trainable
     batch_train = {"input_ids": win_inputs, "attention_mask": torch.ones_like(win_inputs),
                    "labels": buffer_labels.gather(1, idx)}
     score, sim = score_shard(model, device, batch_train, share, n_proxy, optimizer, trainable_layers,
-                             preconditioner=preconditioner, score_len=score_len, group=group)
+                             preconditioner=preconditioner, score_len=score_len, group=group,
+                             exact_similarity=exact_similarity)
     n_select = max(1, int(b_local * world * selection_ratio))
     return select_global(score, sim, n_select, method=selection_method, temperature=temperature, group=group)

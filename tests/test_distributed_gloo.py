@@ -75,18 +75,24 @@ def _rank_worker(rank, world, port, scenario, out_q):
         sd.allreduce_target_sketches(taus)
         score = np.zeros(b)
         sim = np.zeros((b, b))
+        rows = np.zeros((b, b * world))  # exact global similarity: this rank's row block
         for li, pl in enumerate(plans):
             c = float(np.float32(pl.c))
             score += c / n * (phis[li] @ taus[li].numpy())
             sim += c * c * (phis[li] @ phis[li].T)
+            every = sd.gather_sketches(torch.from_numpy(phis[li])).numpy()
+            rows += c * c * (phis[li] @ every.T)
         scores, blocks = sd.gather_scores_and_blocks(torch.from_numpy(score), torch.from_numpy(sim))
+        dense = sd.gather_similarity_rows(torch.from_numpy(rows)).numpy()
         np.random.seed(NP_SEED)  # only rank 0's stream is drawn from
         u = sd.shared_uniforms(N_PICK, torch.device("cpu"))
         picks = orc.stochastic_greedy_selection(scores.numpy().astype(np.float32),
                                                 block_diag(blocks.numpy()).astype(np.float32), N_PICK,
                                                 temperature=1.0, uniforms=u.numpy())
         local = sd.local_picks(torch.tensor(picks, dtype=torch.int64), rank, b).tolist()
-        out_q.put((rank, scores.numpy(), blocks.numpy(), u.numpy(), picks, local))
+        exact_picks = orc.stochastic_greedy_selection(scores.numpy().astype(np.float32), dense.astype(np.float32),
+                                                      N_PICK, temperature=1.0, uniforms=u.numpy())
+        out_q.put((rank, scores.numpy(), blocks.numpy(), u.numpy(), picks, local, dense, exact_picks))
     finally:
         dist.destroy_process_group()
 
@@ -120,7 +126,9 @@ def test_sharded_selection_choreography(scenario, world):
     picks0 = results[0][3]
     mapped = []
     for r in range(world):
-        scores, blocks, u, picks, local = results[r]
+        scores, blocks, u, picks, local, dense, exact_picks = results[r]
+        assert_close_scores(dense, g["sim"])  # exact global similarity == the reference's whole-batch matrix
+        assert exact_picks == results[0][6]
         assert_close_scores(scores, g["scores"])  # sharded scores == the reference's whole-batch scores
         for q in range(world):
             assert_close_scores(blocks[q], g["sim"][q * b:(q + 1) * b, q * b:(q + 1) * b])

@@ -58,6 +58,12 @@ def _worker(rank, world, port, scenario, out_q):
         np.random.seed(NP_SEED)
         gidx, lidx = sd.select_global(score, sim, N_PICK, method="stochastic", temperature=1.0)
         ggreedy, _ = sd.select_global(score, sim, N_PICK, method="greedy")
+        # exact global similarity: row blocks against every rank's sketches
+        score_x, rows = sd.score_shard(model, dev, mine, share, n, opt, layers, preconditioner=str(g["precond"]),
+                                       score_len=128, exact_similarity=True)
+        dense = sd.gather_similarity_rows(rows)
+        np.random.seed(NP_SEED)
+        gexact, _ = sd.select_global(score_x, rows, N_PICK, method="stochastic", temperature=1.0)
         # the whole public call: same picks on every rank
         np.random.seed(NP_SEED)
         cand = batch["input_ids"][rank * b:(rank + 1) * b]
@@ -66,7 +72,7 @@ def _worker(rank, world, port, scenario, out_q):
                                                preconditioner=str(g["precond"]))
         torch.cuda.synchronize()
         out_q.put((rank, scores.cpu().numpy(), blocks.cpu().numpy(), gidx.cpu().tolist(), lidx.cpu().tolist(),
-                   ggreedy.cpu().tolist(), full_idx.cpu().tolist()))
+                   ggreedy.cpu().tolist(), full_idx.cpu().tolist(), dense.cpu().numpy(), gexact.cpu().tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -108,9 +114,13 @@ def test_sharded_selection_on_gpus(scenario):
     uni = np.random.RandomState(NP_SEED).random_sample(N_PICK)
     want = orc.stochastic_greedy_selection(scores.astype(np.float32), dense, N_PICK, temperature=1.0, uniforms=uni)
     want_greedy = orc.greedy_selection(scores.astype(np.float32), dense, N_PICK)
+    want_exact = orc.stochastic_greedy_selection(scores.astype(np.float32), g["sim"].astype(np.float32), N_PICK,
+                                                 temperature=1.0, uniforms=uni)
     mapped = []
     for r in range(world):
-        _, _, gidx, lidx, ggreedy, full_idx = results[r]
+        _, _, gidx, lidx, ggreedy, full_idx, dense_r, gexact = results[r]
+        assert_close_scores(dense_r, g["sim"])  # the reference's whole-batch similarity
+        assert gexact == want_exact
         assert gidx == want and ggreedy == want_greedy
         assert full_idx == results[0][5]
         mapped += [r * b + i for i in lidx]
