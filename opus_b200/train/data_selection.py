@@ -281,6 +281,24 @@ def capture_pairs(model, batch_train, validation_loader, trainable_layers, score
     batch_val, when given, replaces the loader's proxy batch (a rank's share
     of it in sharded selection).
     """
+    loss, layers_kept, z_list, train_bs, val_bs = _capture_forward(model, batch_train, validation_loader,
+                                                                   trainable_layers, score_len, batch_val)
+    z_grads = torch.autograd.grad(loss.mean(), z_list, retain_graph=False, allow_unused=True)
+    del loss
+
+    pairs: list[_Pair] = []
+    for layer, zg in zip(layers_kept, z_grads):
+        if zg is None:
+            continue
+        pairs.extend(_layer_pairs(layer, zg, train_bs))
+    return pairs, train_bs, val_bs
+
+
+def _capture_forward(model, batch_train, validation_loader, trainable_layers, score_len, batch_val):
+    """The capture forward: per-sample mean token loss over candidates + proxies, and the kept layers.
+
+    Returns (loss [N], kept layers, their pre-activations Z, n_candidates, n_proxies).
+    """
     if batch_val is None:
         batch_val = _sample_proxy_batch_for_step(validation_loader)
     else:
@@ -310,30 +328,29 @@ def capture_pairs(model, batch_train, validation_loader, trainable_layers, score
                                                  reduction="none", ignore_index=-100).view(shift_labels.size())
     mask = (shift_labels != -100).float()
     loss = (tok_loss * mask).sum(dim=-1) / mask.sum(dim=-1)
+    del logits, shift_logits, tok_loss
 
     raw = [layer.pre_activation for layer in trainable_layers]
     keep = [i for i, z in enumerate(raw) if isinstance(z, torch.Tensor) and z.requires_grad and z.grad_fn is not None]
     if not keep:
         raise RuntimeError("No usable pre_activations captured. Check GC hooks / forward path.")
-    layers_kept = [trainable_layers[i] for i in keep]
-    z_grads = torch.autograd.grad(loss.mean(), [raw[i] for i in keep], retain_graph=False, allow_unused=True)
-    del logits, shift_logits, tok_loss
+    return loss, [trainable_layers[i] for i in keep], [raw[i] for i in keep], train_bs, val_bs
 
-    pairs: list[_Pair] = []
-    for layer, zg in zip(layers_kept, z_grads):
-        if zg is None:
-            continue
-        parts = layer.pe_grad_gradcomp(zg, per_sample=True)
-        if isinstance(parts, tuple) and len(parts) == 2 and all(isinstance(x, torch.Tensor) for x in parts):
-            parts = [parts]
-        else:
-            parts = list(parts)
-        lparams = [getattr(layer, n) for n in ("lora_A", "lora_B") if hasattr(layer, n)]
-        for i, (g, a) in enumerate(parts):
-            p = lparams[i] if i < len(lparams) else getattr(layer, "weight", None)
-            g, a = g.detach(), a.detach()
-            pairs.append(_Pair(p, g[:train_bs], a[:train_bs], g[train_bs:], a[train_bs:]))
-    return pairs, train_bs, val_bs
+
+def _layer_pairs(layer, zg, train_bs):
+    """(dL/dZ, A) factor pairs of one layer split into candidate / proxy halves (data_selection.py:413-445)."""
+    parts = layer.pe_grad_gradcomp(zg, per_sample=True)
+    if isinstance(parts, tuple) and len(parts) == 2 and all(isinstance(x, torch.Tensor) for x in parts):
+        parts = [parts]
+    else:
+        parts = list(parts)
+    lparams = [getattr(layer, n) for n in ("lora_A", "lora_B") if hasattr(layer, n)]
+    out = []
+    for i, (g, a) in enumerate(parts):
+        p = lparams[i] if i < len(lparams) else getattr(layer, "weight", None)
+        g, a = g.detach(), a.detach()
+        out.append(_Pair(p, g[:train_bs], a[:train_bs], g[train_bs:], a[train_bs:]))
+    return out
 
 
 class LayerPlan:
@@ -350,6 +367,52 @@ class LayerPlan:
         self.c, self.exp_avg_sq, self.eps = c, exp_avg_sq, eps
 
 
+class _PrecondTables:
+    """Per-parameter preconditioner state (data_selection.py:447-506, :545-569)."""
+
+    def __init__(self, params, optimizer, preconditioner):
+        self.param2opt = _build_param2opt_map(_as_opt_list(optimizer))
+        self.auto_mode = preconditioner == "auto"
+        self.preconditioner = preconditioner
+        self.S_map, self.muon_scale, self.adamw = {}, {}, {}
+        for p in {q for q in params if q is not None}:
+            opt_p = self.param2opt.get(p, None)
+            if opt_p is None:
+                continue
+            group = _find_group_for_param(opt_p, p)
+            kind = _group_kind(group) if self.auto_mode else preconditioner
+            if kind == "muon":
+                if p in opt_p.state:
+                    self.S_map[p] = _get_muon_S_matrix(p, opt_p)
+                self.muon_scale[p] = global_C_t_muon(opt_p, p).to(dtype=torch.float32)
+            elif kind == "adamw":
+                self.adamw[p] = (global_C_t(opt_p, p).to(dtype=torch.float32), group, opt_p.state.get(p, {}))
+
+    def plan(self, pid, pr, device):
+        p, g_t = pr.p, pr.g_t
+        scale = torch.tensor(1.0)
+        layer_scale = 1.0
+        v_sq, eps = None, 1e-8
+        eff = "sgd"
+        if p is not None:
+            opt_p = self.param2opt.get(p, None)
+            if opt_p is not None:
+                eff = _group_kind(_find_group_for_param(opt_p, p)) if self.auto_mode else self.preconditioner
+                if eff == "muon" and p in self.S_map:
+                    g_t = (g_t.float() @ self.S_map[p].to(g_t.device).float()).to(g_t.dtype)
+                    scale = self.muon_scale[p]
+                elif eff == "adamw" and p in self.adamw:
+                    scale, group_p, state_p = self.adamw[p]
+                    if state_p.get("exp_avg_sq", None) is not None:
+                        v_sq, eps = state_p["exp_avg_sq"], group_p.get("eps", 1e-8)
+                if eff != "sgd" and p.ndim >= 2:
+                    layer_scale = 1.0 / float((p.shape[-1] * p.shape[-2]) ** 0.5)
+        c = float((scale.detach().cpu().to(torch.float32) * layer_scale).item())
+        if v_sq is not None:
+            v_sq = v_sq.detach().to(device=device, dtype=torch.float32)
+        return LayerPlan(pid, eff, g_t, pr.a_t, pr.g_v, pr.a_v, c, v_sq, eps)
+
+
 def plan_layers(pairs, optimizer, preconditioner, device):
     """Preconditioner per pair, as data_selection.py:447-506 and :545-569 resolve it.
 
@@ -358,85 +421,124 @@ def plan_layers(pairs, optimizer, preconditioner, device):
     AdamW contributes C_t and its diagonal 1/(sqrt(v)+eps); a preconditioned
     matrix parameter also gets layer_scale = 1/sqrt(d_out d_in).
     """
-    param2opt = _build_param2opt_map(_as_opt_list(optimizer))
-    auto_mode = preconditioner == "auto"
-    S_map, muon_scale, adamw = {}, {}, {}
-    for p in {pr.p for pr in pairs if pr.p is not None}:
-        opt_p = param2opt.get(p, None)
-        if opt_p is None:
-            continue
-        group = _find_group_for_param(opt_p, p)
-        kind = _group_kind(group) if auto_mode else preconditioner
-        if kind == "muon":
-            if p in opt_p.state:
-                S_map[p] = _get_muon_S_matrix(p, opt_p)
-            muon_scale[p] = global_C_t_muon(opt_p, p).to(dtype=torch.float32)
-        elif kind == "adamw":
-            adamw[p] = (global_C_t(opt_p, p).to(dtype=torch.float32), group, opt_p.state.get(p, {}))
+    tables = _PrecondTables([pr.p for pr in pairs], optimizer, preconditioner)
+    return [tables.plan(pid, pr, device) for pid, pr in enumerate(pairs)]
 
-    plans = []
-    for pid, pr in enumerate(pairs):
-        p, g_t = pr.p, pr.g_t
-        scale = torch.tensor(1.0)
-        layer_scale = 1.0
-        v_sq, eps = None, 1e-8
-        eff = "sgd"
-        if p is not None:
-            opt_p = param2opt.get(p, None)
-            if opt_p is not None:
-                eff = _group_kind(_find_group_for_param(opt_p, p)) if auto_mode else preconditioner
-                if eff == "muon" and p in S_map:
-                    g_t = (g_t.float() @ S_map[p].to(g_t.device).float()).to(g_t.dtype)
-                    scale = muon_scale[p]
-                elif eff == "adamw" and p in adamw:
-                    scale, group_p, state_p = adamw[p]
-                    if state_p.get("exp_avg_sq", None) is not None:
-                        v_sq, eps = state_p["exp_avg_sq"], group_p.get("eps", 1e-8)
-                if eff != "sgd" and p.ndim >= 2:
-                    layer_scale = 1.0 / float((p.shape[-1] * p.shape[-2]) ** 0.5)
-        c = float((scale.detach().cpu().to(torch.float32) * layer_scale).item())
-        if v_sq is not None:
-            v_sq = v_sq.detach().to(device=device, dtype=torch.float32)
-        plans.append(LayerPlan(pid, eff, g_t, pr.a_t, pr.g_v, pr.a_v, c, v_sq, eps))
-    return plans
+
+# Capture mode of _score_and_similarity: "stream" scores each layer from a
+# backward hook as soon as its dL/dZ exists (no layer's gradient outlives its
+# use); "batch" takes every layer's dL/dZ from one autograd call first.
+CAPTURE_MODE = "stream"
+
+
+def _score_plan(pl, projector, score, sim, val_bs, per_val):
+    """One (dL/dZ, A) pair's contribution to score and sim (data_selection.py:469-591)."""
+    if pl.g_t.dim() == 2:
+        g_t, a_t, g_v, a_v = pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1), pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)
+    else:
+        g_t, a_t, g_v, a_v = pl.g_t, pl.a_t, pl.g_v, pl.a_v
+    c = pl.c
+    if projector is not None and projector.enabled:
+        # stage 3 + 4: one fused sketch pass for the candidates (AdamW
+        # diagonal in the table), one for the proxy batch summed to a row
+        phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
+        if per_val:
+            phi_v = projector.sketch(g_v, a_v, pl.pid)
+            ops.sketch_gram(phi_t, phi_v, alpha=c, out=score, accumulate=True)
+        elif val_bs > 0:
+            tau = projector.sketch(g_v, a_v, pl.pid, rows_div=val_bs)
+            ops.sketch_dot(phi_t, tau[0], alpha=c / val_bs, out=score, accumulate=True)
+        if sim is not None:
+            ops.sketch_gram(phi_t, alpha=c * c, out=sim, accumulate=True)
+    else:
+        _score_dense(g_t, a_t, g_v, a_v, pl.exp_avg_sq, pl.eps, c, per_val, score)
+        if sim is not None:
+            d_out, d_in = g_t.shape[2], a_t.shape[2]
+            diag = None if pl.exp_avg_sq is None else ops_inv_rms(pl.exp_avg_sq, pl.eps).reshape(d_out, d_in)
+            ops.sketch_gram(_materialize(g_t, a_t, diag), alpha=c * c, out=sim, accumulate=True)
+
+
+def _pairs_per_layer(layer) -> int:
+    """Factor pairs pe_grad_gradcomp returns: two for LoRA layers (A and B), one otherwise."""
+    return 2 if (hasattr(layer, "lora_A") and hasattr(layer, "lora_B")) else 1
 
 
 def _score_and_similarity(model, device, batch_train, validation_loader, optimizer, trainable_layers,
                           preconditioner="adamw", score_len=512, per_val=False, with_similarity=True):
     """Device tensors (score [B] or [B, n], sim [B, B] or None) for one window."""
-    pairs, train_bs, val_bs = capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len)
+    batch_val = _sample_proxy_batch_for_step(validation_loader)  # one proxy batch per round, whichever mode
+    if CAPTURE_MODE == "stream":
+        out = _score_and_similarity_stream(model, device, batch_train, batch_val, optimizer, trainable_layers,
+                                           preconditioner, score_len, per_val, with_similarity)
+        if out is not None:
+            return out
+    pairs, train_bs, val_bs = capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len,
+                                            batch_val=batch_val)
     plans = plan_layers(pairs, optimizer, preconditioner, device)
     del pairs
     projector = get_projector()
-    use_projection = projector is not None and projector.enabled
     score = torch.zeros((train_bs, val_bs) if per_val else (train_bs,), device=device, dtype=torch.float32)
     sim = torch.zeros((train_bs, train_bs), device=device, dtype=torch.float32) if with_similarity else None
-
     for pl in plans:
-        if pl.g_t.dim() == 2:
-            g_t, a_t, g_v, a_v = pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1), pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)
-        else:
-            g_t, a_t, g_v, a_v = pl.g_t, pl.a_t, pl.g_v, pl.a_v
-        c = pl.c
-        if use_projection:
-            # stage 3 + 4: one fused sketch pass for the candidates (AdamW
-            # diagonal in the table), one for the proxy batch summed to a row
-            phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
-            if per_val:
-                phi_v = projector.sketch(g_v, a_v, pl.pid)
-                ops.sketch_gram(phi_t, phi_v, alpha=c, out=score, accumulate=True)
-            elif val_bs > 0:
-                tau = projector.sketch(g_v, a_v, pl.pid, rows_div=val_bs)
-                ops.sketch_dot(phi_t, tau[0], alpha=c / val_bs, out=score, accumulate=True)
-            if sim is not None:
-                ops.sketch_gram(phi_t, alpha=c * c, out=sim, accumulate=True)
-            del phi_t
-        else:
-            _score_dense(g_t, a_t, g_v, a_v, pl.exp_avg_sq, pl.eps, c, per_val, score)
-            if sim is not None:
-                d_out, d_in = g_t.shape[2], a_t.shape[2]
-                diag = None if pl.exp_avg_sq is None else ops_inv_rms(pl.exp_avg_sq, pl.eps).reshape(d_out, d_in)
-                ops.sketch_gram(_materialize(g_t, a_t, diag), alpha=c * c, out=sim, accumulate=True)
+        _score_plan(pl, projector, score, sim, val_bs, per_val)
+    return score, sim
+
+
+def _score_and_similarity_stream(model, device, batch_train, batch_val, optimizer, trainable_layers,
+                                 preconditioner, score_len, per_val, with_similarity):
+    """Streaming capture: each layer is scored from a backward hook on its Z.
+
+    The backward pass is asked only for the gradient of the first kept
+    layer's input, which every captured Z feeds, so autograd frees each dL/dZ
+    once its hook has sketched it.  Pair ids follow the forward order, as in
+    the batch capture.  Returns None, after clearing its partial sums, when a
+    layer's hook did not fire (a captured output the loss does not reach, or
+    no usable root); the caller then falls back to the batch capture.
+    """
+    loss, layers_kept, z_list, train_bs, val_bs = _capture_forward(
+        model, dict(batch_train), None, trainable_layers, score_len, batch_val)
+    root = getattr(layers_kept[0], "layer_input", None)
+    if not (isinstance(root, torch.Tensor) and root.requires_grad):
+        return None
+    params = []
+    pid_base = []
+    for layer in layers_kept:
+        pid_base.append(len(params))
+        names = ("lora_A", "lora_B") if _pairs_per_layer(layer) == 2 else ()
+        params.extend([getattr(layer, n) for n in names] or [getattr(layer, "weight", None)])
+    tables = _PrecondTables(params, optimizer, preconditioner)
+    projector = get_projector()
+    score = torch.zeros((train_bs, val_bs) if per_val else (train_bs,), device=device, dtype=torch.float32)
+    sim = torch.zeros((train_bs, train_bs), device=device, dtype=torch.float32) if with_similarity else None
+    fired = [False] * len(layers_kept)
+    bad = []
+
+    def make_hook(li):
+        def hook(grad):
+            try:
+                pairs = _layer_pairs(layers_kept[li], grad, train_bs)
+                if len(pairs) != _pairs_per_layer(layers_kept[li]):
+                    bad.append(li)
+                    return None
+                for i, pr in enumerate(pairs):
+                    _score_plan(tables.plan(pid_base[li] + i, pr, device), projector, score, sim, val_bs, per_val)
+                fired[li] = True
+            except Exception as exc:  # surfaced after backward: an exception inside autograd loses context
+                bad.append(exc)
+            return None
+        return hook
+
+    handles = [z.register_hook(make_hook(li)) for li, z in enumerate(z_list)]
+    try:
+        torch.autograd.grad(loss.mean(), [root], retain_graph=False, allow_unused=True)
+    finally:
+        for h in handles:
+            h.remove()
+    for b in bad:
+        if isinstance(b, Exception):
+            raise b
+    if bad or not all(fired):
+        return None
     return score, sim
 
 

@@ -65,3 +65,70 @@ def test_get_batch_opus_matches_reference(method):
                             n_windows=2)
     assert idx.dtype == torch.int64 and idx.device.type == "cuda"
     assert idx.cpu().tolist() == list(g["idx"])
+
+
+def _scores_both_modes(model, opt, loader, batch, layers, precond="adamw"):
+    out = {}
+    for mode in ("batch", "stream"):
+        ds.CAPTURE_MODE = mode
+        try:
+            out[mode] = ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), dict(batch), loader, opt, layers,
+                                                        preconditioner=precond, score_len=128)
+        finally:
+            ds.CAPTURE_MODE = "stream"
+    return out
+
+
+@pytest.mark.parametrize("name", ["adamw_proj", "muon_proj", "auto_mixed", "adamw_noproj"])
+def test_streaming_capture_equals_batch_capture(name):
+    """Scoring from backward hooks (each dL/dZ used as it appears) == one autograd call for every layer."""
+    g = load_golden(f"wholepath_{name}")
+    model, opt, loader, batch = rebuild(g, device=DEV)
+    if bool(g["cfg"][0]):
+        ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    else:
+        ds.initialize_projector(enabled=False)
+    out = _scores_both_modes(model, opt, loader, batch, ds.find_GClayers(model), str(g["precond"]))
+    assert_close_scores(out["stream"][0], out["batch"][0], rtol=1e-5)
+    assert_close_scores(out["stream"][1], out["batch"][1], rtol=1e-5)
+    assert_close_scores(out["stream"][0], g["scores"])
+
+
+def test_streaming_capture_falls_back_without_a_root():
+    """A frozen embedding leaves the first layer's input without grad: the batch capture takes over."""
+    g = load_golden("wholepath_adamw_proj")
+    model, opt, loader, batch = rebuild(g, device=DEV)
+    model.embed.weight.requires_grad_(False)
+    ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    out = _scores_both_modes(model, opt, loader, batch, ds.find_GClayers(model))
+    np.testing.assert_array_equal(out["stream"][0], out["batch"][0])
+
+
+def test_streaming_capture_lowers_peak_memory():
+    """No layer's dL/dZ outlives its hook: the capture's peak device memory drops."""
+    from opus_b200.layers import GCLinear
+    from tiny_model import ProxyLoader, TinyLM
+
+    torch.manual_seed(0)
+    model = TinyLM(GCLinear, vocab=512, d=256, hidden=2048, n_layers=6).to(DEV)
+    layers = ds.find_GClayers(model)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, betas=(0.9, 0.95))
+    cand = torch.randint(0, 512, (24, 256), device=DEV)
+    prox = torch.randint(0, 512, (4, 256), device=DEV)
+    loader = ProxyLoader({"input_ids": prox, "attention_mask": torch.ones_like(prox), "labels": prox.clone()})
+    batch = {"input_ids": cand, "attention_mask": torch.ones_like(cand), "labels": cand.clone()}
+    ds.initialize_projector(sketch_dim=4096, seed=42, device="cuda", enabled=True)
+    peaks = {}
+    for mode in ("batch", "stream", "batch", "stream"):
+        ds.CAPTURE_MODE = mode
+        try:
+            torch.cuda.synchronize()
+            torch.cuda.reset_peak_memory_stats()
+            base = torch.cuda.memory_allocated()
+            ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), dict(batch), loader, opt, layers,
+                                            preconditioner="adamw", score_len=256)
+            torch.cuda.synchronize()
+            peaks[mode] = torch.cuda.max_memory_allocated() - base
+        finally:
+            ds.CAPTURE_MODE = "stream"
+    assert peaks["stream"] < peaks["batch"], peaks
