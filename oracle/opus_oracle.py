@@ -272,3 +272,38 @@ def greedy_selection(scores, interaction_matrix, K):
         scores -= sim[i, :]
         scores[i] = -np.inf
     return picked
+
+
+# ------------------------------------------------------- candidate buffer stream
+def candidate_buffers(file_tokens, buffer_size: int, world: int, n_buffers: int):
+    """The reference's rank-0 buffer fill (train.py:1038-1079), then each rank's slice (:1081-1084).
+
+    file_tokens: the payload of each training file in cycle order.  Rank 0
+    keeps a current file and position, copies buffer_size * world + 1 tokens
+    per buffer, moving to the next file (cyclically) whenever the current one
+    cannot supply the rest.  Returns, per buffer, the list of every rank's
+    [rank*B, rank*B + B + 1) slice as int32.
+    """
+    files = [np.asarray(t) for t in file_tokens]
+    fi = 0
+    tokens, pos = files[0], 0
+    out = []
+    for _ in range(n_buffers):
+        needed = buffer_size * world + 1
+        cand = np.empty(needed, dtype=np.int32)
+        filled = 0
+        while filled < needed:
+            remaining = needed - filled
+            if pos + remaining >= len(tokens):
+                available = len(tokens) - pos
+                if available > 0:
+                    cand[filled:filled + available] = tokens[pos:].astype(np.int32)
+                    filled += available
+                fi = (fi + 1) % len(files)
+                tokens, pos = files[fi], 0
+            else:
+                cand[filled:filled + remaining] = tokens[pos:pos + remaining].astype(np.int32)
+                pos += remaining
+                filled += remaining
+        out.append([cand[r * buffer_size:r * buffer_size + buffer_size + 1] for r in range(world)])
+    return out
