@@ -86,12 +86,9 @@ __global__ void __launch_bounds__(256) build_table_kernel(const uint32_t* __rest
   }
 }
 
-// Four elements per 16-byte item and up to four items per thread, every
-// table and diagonal load issued before the dependent tau gathers (tau: k
-// floats through the read-only cache, L1-resident for the usual sketch
-// sizes), then 8-byte stores of four bf16 hi and four lo per item.
-constexpr int kDesketchIlp = 4;
-
+// Four elements per thread: 16-byte loads of the packed table and the
+// diagonal, tau gathered through the read-only cache (k floats, L1-resident
+// for the usual sketch sizes), 8-byte stores of four bf16 hi and four lo.
 __device__ __forceinline__ void desketch_one(float t, uint32_t hv, float d, float scale, __nv_bfloat16& h,
                                              __nv_bfloat16& l) {
   float x = __fmul_rn(__fmul_rn(scale, d), t);
@@ -104,56 +101,30 @@ __global__ void desketch_kernel(const float* __restrict__ tau, const uint32_t* _
                                 const float* __restrict__ diag, const float* __restrict__ v, float eps,
                                 int64_t numel, float scale, __nv_bfloat16* __restrict__ hi,
                                 __nv_bfloat16* __restrict__ lo, int vec) {
-  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t start = 0;
   if (vec) {
     const int64_t n4 = numel / 4;
-    const uint4* p4 = reinterpret_cast<const uint4*>(packed);
-    for (int64_t base = tid; base < n4; base += stride * kDesketchIlp) {
-      uint4 hv[kDesketchIlp];
-      float4 d[kDesketchIlp];
-#pragma unroll
-      for (int u = 0; u < kDesketchIlp; ++u) {
-        const int64_t i = base + u * stride;
-        hv[u] = make_uint4(0, 0, 0, 0);
-        d[u] = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-        if (i < n4) {
-          hv[u] = __ldcs(p4 + i);
-          if (diag != nullptr) {
-            d[u] = __ldcs(reinterpret_cast<const float4*>(diag) + i);
-          } else if (v != nullptr) {
-            const float4 q = __ldcs(reinterpret_cast<const float4*>(v) + i);
-            d[u] = make_float4(adam_diag(q.x, eps), adam_diag(q.y, eps), adam_diag(q.z, eps), adam_diag(q.w, eps));
-          }
-        }
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const uint4 hv = __ldcs(reinterpret_cast<const uint4*>(packed) + i);
+      float4 d = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      if (diag != nullptr) {
+        d = __ldcs(reinterpret_cast<const float4*>(diag) + i);
+      } else if (v != nullptr) {
+        const float4 q = __ldcs(reinterpret_cast<const float4*>(v) + i);
+        d = make_float4(adam_diag(q.x, eps), adam_diag(q.y, eps), adam_diag(q.z, eps), adam_diag(q.w, eps));
       }
-      float t[kDesketchIlp][4];
-#pragma unroll
-      for (int u = 0; u < kDesketchIlp; ++u) {
-        if (base + u * stride < n4) {
-          t[u][0] = __ldg(tau + (hv[u].x & 0x7FFFFFFFu));
-          t[u][1] = __ldg(tau + (hv[u].y & 0x7FFFFFFFu));
-          t[u][2] = __ldg(tau + (hv[u].z & 0x7FFFFFFFu));
-          t[u][3] = __ldg(tau + (hv[u].w & 0x7FFFFFFFu));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kDesketchIlp; ++u) {
-        const int64_t i = base + u * stride;
-        if (i >= n4) continue;
-        __align__(8) __nv_bfloat16 h[4], l[4];
-        desketch_one(t[u][0], hv[u].x, d[u].x, scale, h[0], l[0]);
-        desketch_one(t[u][1], hv[u].y, d[u].y, scale, h[1], l[1]);
-        desketch_one(t[u][2], hv[u].z, d[u].z, scale, h[2], l[2]);
-        desketch_one(t[u][3], hv[u].w, d[u].w, scale, h[3], l[3]);
-        __stcs(reinterpret_cast<uint2*>(hi) + i, *reinterpret_cast<const uint2*>(h));
-        __stcs(reinterpret_cast<uint2*>(lo) + i, *reinterpret_cast<const uint2*>(l));
-      }
+      __align__(8) __nv_bfloat16 h[4], l[4];
+      desketch_one(__ldg(tau + (hv.x & 0x7FFFFFFFu)), hv.x, d.x, scale, h[0], l[0]);
+      desketch_one(__ldg(tau + (hv.y & 0x7FFFFFFFu)), hv.y, d.y, scale, h[1], l[1]);
+      desketch_one(__ldg(tau + (hv.z & 0x7FFFFFFFu)), hv.z, d.z, scale, h[2], l[2]);
+      desketch_one(__ldg(tau + (hv.w & 0x7FFFFFFFu)), hv.w, d.w, scale, h[3], l[3]);
+      __stcs(reinterpret_cast<uint2*>(hi) + i, *reinterpret_cast<const uint2*>(h));
+      __stcs(reinterpret_cast<uint2*>(lo) + i, *reinterpret_cast<const uint2*>(l));
     }
     start = n4 * 4;
   }
-  for (int64_t i = start + tid; i < numel; i += stride) {
+  for (int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < numel; i += stride) {
     const uint32_t hv = packed[i];
     desketch_one(tau[hv & 0x7FFFFFFFu], hv, element_weight(diag, v, eps, i), scale, hi[i], lo[i]);
   }
@@ -391,7 +362,7 @@ int opus_desketch(const float* tau, const uint32_t* packed, const float* diag, c
   const uintptr_t al = reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(diag) |
                        reinterpret_cast<uintptr_t>(exp_avg_sq);
   const int vec = (al & 15) == 0 && (reinterpret_cast<uintptr_t>(hi) & 7) == 0 && (reinterpret_cast<uintptr_t>(lo) & 7) == 0;
-  desketch_kernel<<<grid_for(vec ? numel / (4 * kDesketchIlp) + 1 : numel, 256), 256, 0, (cudaStream_t)stream>>>(
+  desketch_kernel<<<grid_for(vec ? numel / 4 + 1 : numel, 256), 256, 0, (cudaStream_t)stream>>>(
       tau, packed, diag, exp_avg_sq, eps, numel, scale, hi, lo, vec);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
