@@ -186,7 +186,7 @@ def run_gpu(args, rank, world, local_rank):
         if local:
             return score_, sim_
         if exact:
-            return sd._gather_scores(score_), sd.gather_similarity_rows(sim_)
+            return sd.gather_scores(score_), sd.gather_similarity_rows(sim_)
         return sd.gather_scores_and_blocks(score_, sim_)
 
     def select(score_, sim_):

@@ -75,7 +75,7 @@ def gather_scores_and_blocks(score: torch.Tensor, sim: torch.Tensor, group=None)
     return torch.cat(scores), torch.stack(blocks)
 
 
-def _gather_scores(score: torch.Tensor, group=None) -> torch.Tensor:
+def gather_scores(score: torch.Tensor, group=None) -> torch.Tensor:
     _, world = rank_and_world(group)
     score = score.reshape(-1).contiguous()
     if world == 1:
@@ -138,7 +138,7 @@ def select_global(score: torch.Tensor, sim: torch.Tensor, n_select: int, method:
     rank, world = rank_and_world(group)
     b = score.numel()
     if sim.dim() == 2 and sim.shape == (b, b * world) and world > 1:
-        scores = _gather_scores(score, group)
+        scores = gather_scores(score, group)
         blocks = gather_similarity_rows(sim, group)
     else:
         scores, blocks = gather_scores_and_blocks(score, sim, group)
