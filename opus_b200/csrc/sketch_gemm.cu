@@ -72,11 +72,13 @@ struct SmemPlan {
 
 // Read-only table load that bypasses L1 (each entry is read once per tile).
 // Not volatile: independent loads may be hoisted and kept in flight together.
-__device__ __forceinline__ uint4 ld_nc_na(const uint4* p) {
+// Table entries: read once per candidate tile, never kept in L1, kept in L2
+// (every candidate re-reads the layer's table).
+__device__ __forceinline__ uint4 ld_table(const uint4* p, uint64_t l2_policy) {
   uint4 v;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "l"(p));
+      : "l"(p), "l"(l2_policy));
   return v;
 }
 
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      const uint64_t pol_last = l2_policy_evict_last(), pol_first = l2_policy_evict_first();
       for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
       for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
       for (int cb = 0; cb < n_cb && ok; ++cb) {
@@ -204,10 +207,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sg = stage_mem + (size_t)s * kStageBytes;
           uint8_t* sa = sg + kGTileBytes;
           const int t0 = kb * kBK;
+          // L2 policy: the dLdZ rows of this o-block are not read again after
+          // its last column block; the activations serve every o-block
+          const uint64_t gpol = cb == n_cb - 1 ? pol_first : pol_last;
 #pragma unroll
-          for (int i = 0; i < kGBoxes; ++i) tma_load_3d(sg + i * kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b);
+          for (int i = 0; i < kGBoxes; ++i)
+            tma_load_3d_hint(sg + i * kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b, gpol);
 #pragma unroll
-          for (int i = 0; i < kABoxes; ++i) tma_load_3d(sa + i * kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b);
+          for (int i = 0; i < kABoxes; ++i)
+            tma_load_3d_hint(sa + i * kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, pol_last);
           if (++s == stages) {
             s = 0;
             ph ^= 1;
@@ -268,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;              // tile row owned by this thread
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t kk32 = static_cast<uint32_t>(k);
+    const uint64_t table_policy = l2_policy_evict_last();
     int acc = 0;
     uint32_t aph = 0;
     uint32_t epi_phase = 0;
@@ -305,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int j = half * kChunksPerWarp + jj;
           uint4 ent[kPairsPerChunk];
 #pragma unroll
-          for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
+          for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_table(tp + (j * kPairsPerChunk + p) * kTileM, table_policy);
           uint32_t v[32];
           tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
           tmem_ld_wait();
@@ -348,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // all 16 table entries of the chunk in flight before the accumulator wait
         uint4 ent[kPairsPerChunk];
 #pragma unroll
-        for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_nc_na(tp + (j * kPairsPerChunk + p) * kTileM);
+        for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_table(tp + (j * kPairsPerChunk + p) * kTileM, table_policy);
         uint32_t v[32];
         tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
         tmem_ld_wait();
