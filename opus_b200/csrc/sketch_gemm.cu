@@ -436,7 +436,8 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   if (n_rows < 0 || seq_len < 0 || d_out <= 0 || d_in <= 0 || k <= 0 || k > 0x7FFFFFFF || rows_div <= 0)
     return set_error(OPUS_ERR_INVALID, "sketch_gemm: bad sizes (n=%d T=%d d_out=%d d_in=%d k=%lld rows_div=%d)",
                      n_rows, seq_len, d_out, d_in, (long long)k, rows_div);
-  if (!table || !phi || (n_rows > 0 && (!dLdZ || !a))) return set_error(OPUS_ERR_INVALID, "sketch_gemm: NULL pointer");
+  if (!table || (n_rows > 0 && !phi) || (n_rows > 0 && seq_len > 0 && (!dLdZ || !a)))
+    return set_error(OPUS_ERR_INVALID, "sketch_gemm: NULL pointer");
   if (table_entries_given < table_entries(d_out, d_in))
     return set_error(OPUS_ERR_INVALID, "sketch_gemm: table holds %lld entries, need %lld",
                      (long long)table_entries_given, (long long)table_entries(d_out, d_in));

@@ -326,3 +326,23 @@ def test_ghost_equals_sketch_dot_through_desketch():
     vt = ops.desketch(tau, packed, d_out, d_in, scale=0.25, exp_avg_sq=v)
     via_ghost = ops.ghost_score(a, g, vt)
     rel_close(via_ghost.cpu().numpy(), via_sketch.cpu().numpy(), 1e-4, "ghost vs sketch")
+
+
+def test_empty_inputs():
+    """Zero candidates, zero tokens or zero picks: every entry point returns without a launch error."""
+    k = 512
+    h, s, packed = cuda_tables(64 * 64, 0, k)
+    table = ops.build_sketch_table(packed, 64, 64)
+    phi = ops.sketch_gemm(torch.empty(0, 16, 64, device=DEV, dtype=torch.bfloat16),
+                          torch.empty(0, 16, 64, device=DEV, dtype=torch.bfloat16), table, k)
+    assert phi.shape == (0, k)
+    phi0 = ops.sketch_gemm(torch.empty(3, 0, 64, device=DEV, dtype=torch.bfloat16),
+                           torch.empty(3, 0, 64, device=DEV, dtype=torch.bfloat16), table, k)
+    assert phi0.shape == (3, k) and not phi0.any()
+    assert ops.sketch_dot(torch.empty(0, k, device=DEV), torch.zeros(k, device=DEV)).numel() == 0
+    assert ops.sketch_gram(torch.empty(0, k, device=DEV)).numel() == 0
+    sc = torch.randn(5, device=DEV)
+    sim = torch.zeros(5, 5, device=DEV)
+    assert ops.boltzmann_select(sc, sim, 0, 1.0, torch.empty(0, dtype=torch.float64)).numel() == 0
+    assert ops.greedy_select(sc, sim, 0).numel() == 0
+    ops.check_device_error("empty inputs")
