@@ -486,7 +486,7 @@ def _score_and_similarity(model, device, batch_train, validation_loader, optimiz
 
 def _score_and_similarity_stream(model, device, batch_train, batch_val, optimizer, trainable_layers,
                                  preconditioner, score_len, per_val, with_similarity):
-    """Streaming capture (SURVEY 8(f) item 1): each layer is scored from a backward hook on its Z.
+    """Streaming capture: each layer is scored from a backward hook on its Z.
 
     The backward pass is asked only for the gradient of the first kept
     layer's input, which every captured Z feeds, so autograd frees each dL/dZ
