@@ -19,7 +19,6 @@
 namespace opus {
 namespace {
 
-constexpr int kSelThreads = 1024;
 constexpr int kSelMax = 8192;
 constexpr int kPwBlock = 128;
 // numpy splits a length-m sum at m/2 rounded down to a multiple of 8 until a
@@ -50,9 +49,7 @@ struct SelShared {
   int leaf_slot[kLevels * kLevelSlots];  // (level << 7) | slot of every leaf
   int n_leaves;
   int tree_depth;
-  int leaf_done;
   long long scan_ll[32];
-  double red_d[32];
   int red_ne[32];
   float red_f[32];
   int red_nan[32];
@@ -131,6 +128,35 @@ __device__ __forceinline__ unsigned long long shr128(unsigned long long h, unsig
 // below the midpoint (2U+1) * 2^(e-1) between u = U * 2^e and its successor,
 // or equal to it with U even (ties to even); with R = (2U+1) * L that is
 // X * 2^(1-e) < R (or == R), evaluated in 128-bit integers.
+// p * 2^52 for a float32 p in [0, 1], read from its bits: P gets the integer
+// part, and the result says whether p is a whole multiple of 2^-52 (then the
+// float64 sum of such p is exact and equals the int64 sum of the P).
+__device__ __forceinline__ bool fixed52(float p, long long& P) {
+  const uint32_t u = __float_as_uint(p);
+  const int e = static_cast<int>((u >> 23) & 0xFFu);
+  uint32_t mant = u & 0x7FFFFFu;
+  if (e == 0) {  // zero or subnormal: p * 2^52 < 1
+    P = 0;
+    return mant == 0;
+  }
+  mant |= 0x800000u;
+  const int sh = e - 98;  // p * 2^52 = mant * 2^(e - 127 - 23 + 52)
+  if (sh > 29) {          // p > 1 cannot come out of the normalisation
+    P = 0;
+    return false;
+  }
+  if (sh >= 0) {
+    P = static_cast<long long>(mant) << sh;
+    return true;
+  }
+  if (sh <= -32) {
+    P = 0;
+    return false;
+  }
+  P = static_cast<long long>(mant >> -sh);
+  return (mant & ((1u << -sh) - 1u)) == 0;
+}
+
 __device__ long long cdf_threshold(double u, long long L) {
   if (isnan(u) || u < 0.0) return -1;
   if (u >= 1.0) return 0x7fffffffffffffffll;
@@ -177,10 +203,7 @@ __global__ void __launch_bounds__(NT, 1)
     s.avail[i] = 1;
     s.pos[i] = i;
   }
-  if (warp == 0) {
-    pw_tree_build(n, s, lane);
-    if (lane == 0) s.leaf_done = 0;
-  }
+  if (warp == 0) pw_tree_build(n, s, lane);
   __syncthreads();
 
   for (int r = 0; r < n_select; ++r) {
@@ -223,8 +246,8 @@ __global__ void __launch_bounds__(NT, 1)
     }
     // (2) leaf sums, 8 lanes per leaf: lane j holds numpy's accumulator r[j],
     //     combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail;
-    //     leaves shorter than 8 are a running sum from 0.  The last warp to
-    //     finish combines the tree.
+    //     leaves shorter than 8 are a running sum from 0.  After a barrier
+    //     warp 0 combines the tree.
     const int n_leaves = s.n_leaves;
     for (int l0 = 0; l0 < n_leaves; l0 += NT / 8) {
       const int leaf = l0 + (tid >> 3), j = tid & 7;
@@ -255,20 +278,10 @@ __global__ void __launch_bounds__(NT, 1)
         s.lvl_sum[d][sj] = res;
       }
     }
-    __syncwarp();
-    int done = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      done = atomicAdd(&s.leaf_done, 1);
-    }
-    done = __shfl_sync(0xffffffffu, done, 0);
-    if (done == W - 1) {
-      __threadfence_block();
+    __syncthreads();
+    if (warp == 0) {
       const float root = pw_tree_sum(s, lane);
-      if (lane == 0) {
-        s.total = __fadd_rn(0.0f, root);
-        s.leaf_done = 0;
-      }
+      if (lane == 0) s.total = __fadd_rn(0.0f, root);
     }
     __syncthreads();                                                   // barrier B
     const float total = s.total;
@@ -279,16 +292,14 @@ __global__ void __launch_bounds__(NT, 1)
     //     int64 scan.  Warp 0 lays out the next draw's tree meanwhile.
     int not_exact = 0;
     long long fsum = 0;
-    double dsum = 0.0;
     for (int i = lo; i < hi; ++i) {
       if (!s.avail[i]) continue;
       const int q = skew(s.pos[i]);
       const float p = uniform ? inv_m : __fdiv_rn(s.pc[q], total);
       s.pc[q] = p;
-      const double x = static_cast<double>(p) * 0x1p52;
-      if (x != trunc(x)) not_exact = 1;
-      fsum += static_cast<long long>(x);
-      dsum += static_cast<double>(p);
+      long long P;
+      if (!fixed52(p, P)) not_exact = 1;
+      fsum += P;
     }
     long long fx = fsum;
 #pragma unroll
@@ -297,15 +308,9 @@ __global__ void __launch_bounds__(NT, 1)
       if (lane >= off) fx += y;
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      dsum += __shfl_xor_sync(0xffffffffu, dsum, off);
-      not_exact |= __shfl_xor_sync(0xffffffffu, not_exact, off);
-    }
+    for (int off = 16; off > 0; off >>= 1) not_exact |= __shfl_xor_sync(0xffffffffu, not_exact, off);
     if (lane == 31) s.scan_ll[warp] = fx;
-    if (lane == 0) {
-      s.red_d[warp] = dsum;
-      s.red_ne[warp] = not_exact;
-    }
+    if (lane == 0) s.red_ne[warp] = not_exact;
     if (warp == 0 && r + 1 < n_select) pw_tree_build(m - 1, s, lane);
     __syncthreads();                                                   // barrier C
     long long fbase, ftot;
@@ -320,16 +325,14 @@ __global__ void __launch_bounds__(NT, 1)
       }
       fbase = __shfl_sync(0xffffffffu, incl - wt, warp) + (fx - fsum);
       ftot = __shfl_sync(0xffffffffu, incl, 31);
-      double pd = lane < W ? s.red_d[lane] : 0.0;
       int ne = lane < W ? s.red_ne[lane] : 0;
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        pd += __shfl_xor_sync(0xffffffffu, pd, off);
-        ne |= __shfl_xor_sync(0xffffffffu, ne, off);
-      }
+      for (int off = 16; off > 0; off >>= 1) ne |= __shfl_xor_sync(0xffffffffu, ne, off);
       exact = ne == 0;
-      // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32).
-      if (tid == 0 && fabs(pd - 1.0) > 3.4526698300124393e-04) record_device_error(err, 0x301);
+      // np.random.choice rejects p whose sum is off by more than sqrt(eps_f32);
+      // the truncated int64 total is within n * 2^-52 of the float64 sum.
+      if (tid == 0 && fabs(static_cast<double>(ftot) * 0x1p-52 - 1.0) > 3.4526698300124393e-04)
+        record_device_error(err, 0x301);
     }
     // (4) searchsorted(cdf / cdf[-1], u, 'right') counts the entries <= u; the
     //     cdf is non-decreasing, so the pick is the first position whose entry
@@ -341,7 +344,9 @@ __global__ void __launch_bounds__(NT, 1)
         if (!s.avail[i]) continue;
         const int q = s.pos[i];
         const long long prev = run;
-        run += static_cast<long long>(static_cast<double>(s.pc[skew(q)]) * 0x1p52);
+        long long P;
+        fixed52(s.pc[skew(q)], P);
+        run += P;
         if ((run > thr && (q == 0 || prev <= thr)) || (q == m - 1 && run <= thr)) {
           s.pick = q;
           s.sel = i;
@@ -406,22 +411,25 @@ __device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
   return a.i < b.i ? a : b;
 }
 
-__global__ void __launch_bounds__(kSelThreads, 1)
+// Thread t owns the candidates i = t, t + NT, t + 2 NT, ...: it alone reads and
+// writes their scores (the penalty row is then read coalesced), so the one
+// barrier of a draw is the one that publishes the warps' maxima; they sit in
+// two buffers by draw parity, so the next draw's writes cannot meet this
+// draw's reads.  Every warp finishes the argmax itself.
+template <int NT>
+__global__ void __launch_bounds__(NT, 1)
     greedy_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int block, int n_select,
                   int64_t* __restrict__ out_idx) {
+  constexpr int W = NT / 32;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   float* scores = reinterpret_cast<float*>(sel_smem);
-  __shared__ float rv[32];
-  __shared__ int ri[32];
-  __shared__ int pick;
+  __shared__ float rv[2][W];
+  __shared__ int ri[2][W];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < n; i += kSelThreads) scores[i] = scores_in[i];
-  __syncthreads();
-  const int per = (n + kSelThreads - 1) / kSelThreads;
-  const int lo = min(n, tid * per), hi = min(n, lo + per);
+  for (int i = tid; i < n; i += NT) scores[i] = scores_in[i];
   for (int r = 0; r < n_select; ++r) {
     ArgMax best{-INFINITY, 0x7fffffff};
-    for (int i = lo; i < hi; ++i) best = better(best, ArgMax{scores[i], i});
+    for (int i = tid; i < n; i += NT) best = better(best, ArgMax{scores[i], i});
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       ArgMax o;
@@ -430,19 +438,22 @@ __global__ void __launch_bounds__(kSelThreads, 1)
       best = better(best, o);
     }
     if (lane == 0) {
-      rv[warp] = best.v;
-      ri[warp] = best.i;
+      rv[r & 1][warp] = best.v;
+      ri[r & 1][warp] = best.i;
     }
     __syncthreads();
-    if (tid == 0) {
-      ArgMax b{rv[0], ri[0]};
-      for (int w = 1; w < 32; ++w) b = better(b, ArgMax{rv[w], ri[w]});
-      // all entries -inf: np.argmax returns 0
-      pick = (b.i == 0x7fffffff) ? 0 : b.i;
-      out_idx[r] = pick;
+    ArgMax b{-INFINITY, 0x7fffffff};
+    if (lane < W) b = ArgMax{rv[r & 1][lane], ri[r & 1][lane]};
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      ArgMax o;
+      o.v = __shfl_xor_sync(0xffffffffu, b.v, off);
+      o.i = __shfl_xor_sync(0xffffffffu, b.i, off);
+      b = better(b, o);
     }
-    __syncthreads();
-    const int sel = pick;
+    // all entries -inf: np.argmax returns 0
+    const int sel = (b.i == 0x7fffffff) ? 0 : b.i;
+    if (tid == 0) out_idx[r] = sel;
     const float* row = sim + (int64_t)sel * n;
     int plo = 0, phi = n;
     if (block > 0) {  // block-diagonal sim, as in boltzmann_kernel
@@ -450,10 +461,9 @@ __global__ void __launch_bounds__(kSelThreads, 1)
       phi = plo + block;
       row = sim + (int64_t)sel * block - plo;
     }
-    for (int i = plo + tid; i < phi; i += kSelThreads) scores[i] = __fsub_rn(scores[i], row[i]);
-    __syncthreads();
-    if (tid == 0) scores[sel] = -INFINITY;
-    __syncthreads();
+    // the first owned candidate at or after plo
+    for (int i = plo + ((tid - plo % NT) + NT) % NT; i < phi; i += NT) scores[i] = __fsub_rn(scores[i], row[i]);
+    if (sel % NT == tid) scores[sel] = -INFINITY;
   }
 }
 
@@ -508,10 +518,21 @@ int launch_greedy(const float* scores, const float* sim, int n, int block, int n
   if (n_select == 0) return OPUS_OK;
   if (!scores || !sim || !out_idx) return set_error(OPUS_ERR_INVALID, "greedy: NULL pointer");
   const size_t smem = (size_t)n * sizeof(float);
-  if (smem > 48 * 1024)
-    OPUS_CUDA_TRY(cudaFuncSetAttribute(greedy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  greedy_kernel<<<1, kSelThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(scores, sim, n, block, n_select,
-                                                                                   out_idx);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define OPUS_LAUNCH_GREEDY(NT)                                                                                 \
+  if (smem > 48 * 1024)                                                                                        \
+    OPUS_CUDA_TRY(cudaFuncSetAttribute(greedy_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+  greedy_kernel<NT><<<1, NT, smem, st>>>(scores, sim, n, block, n_select, out_idx)
+  if (n <= 128) {
+    OPUS_LAUNCH_GREEDY(128);
+  } else if (n <= 256) {
+    OPUS_LAUNCH_GREEDY(256);
+  } else if (n <= 512) {
+    OPUS_LAUNCH_GREEDY(512);
+  } else {
+    OPUS_LAUNCH_GREEDY(1024);
+  }
+#undef OPUS_LAUNCH_GREEDY
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

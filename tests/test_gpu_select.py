@@ -42,6 +42,16 @@ def test_greedy_more_picks_than_candidates():
     assert got == orc.greedy_selection(sc, sim, 5)
 
 
+@pytest.mark.parametrize("n,K", [(20, 20), (300, 299), (1500, 300), (6000, 200)])
+def test_greedy_matches_oracle_random(n, K):
+    """One to six candidates per thread, ties broken to the lowest index."""
+    rng = np.random.default_rng(n)
+    sc = np.round(rng.standard_normal(n), 1).astype(np.float32)  # many exact ties
+    m = np.round(rng.standard_normal((n, n)) * 0.05, 2).astype(np.float32)
+    sim = ((m + m.T) / 2).astype(np.float32)
+    assert ops.greedy_select(dev(sc), dev(sim), K).cpu().tolist() == orc.greedy_selection(sc, sim, K)
+
+
 @pytest.mark.parametrize("n,K,temp,spread", [(1024, 256, 1.0, 1.0), (4096, 64, 0.7, 3.0), (8192, 32, 1.5, 1.0),
                                              (257, 100, 0.5, 30.0), (129, 129, 1.0, 1.0)])
 def test_boltzmann_matches_oracle_random(n, K, temp, spread):
@@ -126,7 +136,7 @@ def test_block_diagonal_boltzmann_matches_dense(q, b, K, temp):
     assert got_b == got_d == want
 
 
-@pytest.mark.parametrize("q,b,K", [(4, 64, 100), (2, 300, 650)])
+@pytest.mark.parametrize("q,b,K", [(4, 64, 100), (2, 300, 650), (3, 2000, 150)])
 def test_block_diagonal_greedy_matches_dense(q, b, K):
     rng = np.random.default_rng(q + b)
     sc = rng.standard_normal(q * b).astype(np.float32)
