@@ -104,6 +104,70 @@ def local_picks(global_idx: torch.Tensor, rank: int, b_local: int) -> torch.Tens
     return global_idx[mask] - lo
 
 
+def redistribution_plan(global_idx, b_local: int, world: int) -> list[list[tuple[int, int]]]:
+    """Every rank's share of the selected rows as (source rank, local row), in receive order.
+
+    The reference's global mode (train.py:1184-1247) orders the selected rows
+    by source rank, pick order inside a rank, and gives rank d the rows
+    [d*per + min(d, rem), that + per + (d < rem)) of that order, with
+    per, rem = divmod(total, world); a rank whose share is empty takes the
+    first row of the order.  With no picks at all every rank keeps its own
+    row 0.
+    """
+    idx = [int(g) for g in global_idx]
+    if any(g < 0 or g >= b_local * world for g in idx):
+        raise ValueError(f"global indices must lie in [0, {b_local * world})")
+    by_source: list[list[int]] = [[] for _ in range(world)]
+    for g in idx:
+        by_source[g // b_local].append(g % b_local)
+    order = [(q, i) for q in range(world) for i in by_source[q]]
+    if not order:
+        return [[(d, 0)] for d in range(world)]
+    per, rem = divmod(len(order), world)
+    shares = []
+    for d in range(world):
+        start, cnt = d * per + min(d, rem), per + (1 if d < rem else 0)
+        shares.append(order[start:start + cnt] if cnt else order[:1])
+    return shares
+
+
+def redistribute_selected(global_idx, inputs: torch.Tensor, targets: torch.Tensor, group=None):
+    """This rank's share of the globally selected sequences (train.py:1181-1249).
+
+    inputs / targets: this rank's candidate rows [b, seq_len] (every rank the
+    same b); global_idx: the picks over all ranks' candidates, the same on
+    every rank.  The reference all-gathers every rank's selected rows padded
+    to the largest count and keeps a slice; here every rank derives the whole
+    plan from the picks it already has, and one all_to_all of the packed
+    rows (inputs and targets side by side as bytes) moves each row that
+    changes rank exactly once, with no padding.  Returns (inputs, targets) of
+    this rank's share, on the inputs' device, equal to the reference's.
+    """
+    rank, world = rank_and_world(group)
+    if inputs.shape[0] != targets.shape[0]:
+        raise ValueError("inputs and targets must hold the same number of rows")
+    b = inputs.shape[0]
+    picks = global_idx.tolist() if torch.is_tensor(global_idx) else list(global_idx)
+    shares = redistribution_plan(picks, b, world)
+    device = inputs.device
+    if world == 1:
+        rows = torch.tensor([i for _, i in shares[0]], dtype=torch.long, device=device)
+        return inputs.index_select(0, rows), targets.index_select(0, rows)
+    send = [[i for q, i in shares[d] if q == rank] for d in range(world)]
+    rows = torch.tensor([i for part in send for i in part], dtype=torch.long, device=device)
+    recv = [sum(1 for q, _ in shares[rank] if q == src) for src in range(world)]
+    x = inputs.index_select(0, rows).contiguous().view(torch.uint8)
+    y = targets.index_select(0, rows).contiguous().view(torch.uint8)
+    nx = x.shape[1]
+    packed = torch.cat([x, y], dim=1)
+    out = torch.empty(sum(recv), packed.shape[1], dtype=torch.uint8, device=device)
+    dist.all_to_all_single(out, packed, recv, [len(part) for part in send], group=group)
+    # fresh row-major storage: a one-row slice keeps its offset and row stride into out
+    got_x = torch.empty(out.shape[0], nx, dtype=torch.uint8, device=device).copy_(out[:, :nx])
+    got_y = torch.empty(out.shape[0], out.shape[1] - nx, dtype=torch.uint8, device=device).copy_(out[:, nx:])
+    return got_x.view(inputs.dtype), got_y.view(targets.dtype)
+
+
 def gather_sketches(phi: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather one layer's candidate sketches [B_loc, k] -> [W*B_loc, k] in rank order."""
     _, world = rank_and_world(group)

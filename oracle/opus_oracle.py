@@ -307,3 +307,45 @@ def candidate_buffers(file_tokens, buffer_size: int, world: int, n_buffers: int)
                 filled += remaining
         out.append([cand[r * buffer_size:r * buffer_size + buffer_size + 1] for r in range(world)])
     return out
+
+
+# ------------------------------------------- redistribution of the selection
+def redistribute_selected(global_idx, inputs_per_rank, targets_per_rank):
+    """The reference's steps 5a-5e after a global selection (train.py:1181-1249).
+
+    global_idx: the picks over the concatenated candidates of all ranks, the
+    same on every rank.  inputs_per_rank / targets_per_rank: each rank's
+    candidate rows [b, seq_len].  Each rank masks the picks that fall in its
+    range (pick order kept), all ranks all-gather their selected rows padded
+    to the largest count, concatenate the real rows in rank order and take an
+    even share, the first (total % world) ranks one row more; a rank whose
+    share is empty takes row 0 of the concatenation.  Returns each rank's
+    (inputs, targets).
+    """
+    world = len(inputs_per_rank)
+    b = inputs_per_rank[0].shape[0]
+    g = np.asarray(global_idx, dtype=np.int64)
+    sel_in, sel_tg = [], []
+    for r in range(world):
+        mask = (g >= r * b) & (g < r * b + b)
+        local = g[mask] - r * b
+        sel_in.append(inputs_per_rank[r][local])
+        sel_tg.append(targets_per_rank[r][local])
+    counts = [len(x) for x in sel_in]
+    if sum(counts) > 0:
+        all_in = np.concatenate([x for x, c in zip(sel_in, counts) if c > 0])
+        all_tg = np.concatenate([x for x, c in zip(sel_tg, counts) if c > 0])
+    out = []
+    for r in range(world):
+        if sum(counts) == 0:  # no picks at all: every rank keeps its own first row
+            out.append((inputs_per_rank[r][:1], targets_per_rank[r][:1]))
+            continue
+        total = all_in.shape[0]
+        per, rem = divmod(total, world)
+        start = r * per + min(r, rem)
+        cnt = per + (1 if r < rem else 0)
+        end = start + cnt
+        if cnt == 0:
+            start, end = 0, 1
+        out.append((all_in[start:end], all_tg[start:end]))
+    return out

@@ -161,3 +161,86 @@ def test_single_process_gather_is_identity():
     assert torch.equal(scores, s) and blocks.shape == (1, 4, 4)
     with pytest.raises(ValueError):
         sd.gather_scores_and_blocks(s, torch.eye(3))
+
+
+def _redistribution_case(world, b, T, picks, seed):
+    rng = np.random.default_rng(seed)
+    inputs = [rng.integers(0, 50257, (b, T)).astype(np.int32) for _ in range(world)]
+    targets = [rng.integers(-100, 50257, (b, T)).astype(np.int64) for _ in range(world)]
+    return inputs, targets, orc.redistribute_selected(picks, inputs, targets)
+
+
+REDISTRIBUTION_CASES = [
+    (2, 6, 5, [7, 1, 3, 11, 0, 8]),      # mixed sources, pick order kept inside a source
+    (3, 4, 3, [9]),                       # one pick: ranks 1 and 2 take row 0 of the order
+    (3, 4, 3, [5, 6, 4, 7]),              # every pick on rank 1
+    (4, 8, 2, list(range(31, -1, -2))),   # total % world == 0
+    (4, 3, 4, [2, 11, 5, 6, 0]),          # remainder 1
+]
+
+
+@pytest.mark.parametrize("world,b,T,picks", REDISTRIBUTION_CASES)
+def test_redistribution_plan_matches_reference(world, b, T, picks):
+    inputs, targets, want = _redistribution_case(world, b, T, picks, seed=world * 100 + b)
+    shares = sd.redistribution_plan(picks, b, world)
+    for d in range(world):
+        got_in = np.stack([inputs[q][i] for q, i in shares[d]])
+        got_tg = np.stack([targets[q][i] for q, i in shares[d]])
+        np.testing.assert_array_equal(got_in, want[d][0])
+        np.testing.assert_array_equal(got_tg, want[d][1])
+    with pytest.raises(ValueError):
+        sd.redistribution_plan([b * world], b, world)
+
+
+def _redistribute_worker(rank, world, port, b, T, picks, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        inputs, targets, _ = _redistribution_case(world, b, T, picks, seed=world * 100 + b)
+        x, y = sd.redistribute_selected(torch.tensor(picks), torch.from_numpy(inputs[rank]),
+                                        torch.from_numpy(targets[rank]))
+        out_q.put((rank, x.numpy(), y.numpy(), str(x.dtype), str(y.dtype)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(180)
+@pytest.mark.parametrize("world,b,T,picks", REDISTRIBUTION_CASES[:3])
+def test_redistribute_selected_over_gloo(world, b, T, picks):
+    """One all_to_all of the packed rows gives every rank the reference's share."""
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_redistribute_worker, args=(r, world, port, b, T, picks, out_q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            rank, *rest = out_q.get(timeout=150)
+            results[rank] = rest
+    except queue.Empty:
+        pytest.fail("a rank did not report")
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    _, _, want = _redistribution_case(world, b, T, picks, seed=world * 100 + b)
+    for r in range(world):
+        x, y, dx, dy = results[r]
+        assert (dx, dy) == ("torch.int32", "torch.int64")
+        np.testing.assert_array_equal(x, want[r][0])
+        np.testing.assert_array_equal(y, want[r][1])
+
+
+def test_redistribute_selected_single_process():
+    inputs, targets, want = _redistribution_case(1, 5, 3, [4, 0, 2], seed=1)
+    x, y = sd.redistribute_selected(torch.tensor([4, 0, 2]), torch.from_numpy(inputs[0]),
+                                    torch.from_numpy(targets[0]))
+    np.testing.assert_array_equal(x.numpy(), want[0][0])
+    np.testing.assert_array_equal(y.numpy(), want[0][1])

@@ -4,7 +4,8 @@ Each rank scores its candidate shard with the device kernels, the proxy
 sketches are all-reduced and the scores and local similarity blocks are
 all-gathered; the gathered scores must match the reference's single-process
 scores, and every rank must draw the same picks as the oracle on the gathered
-block-diagonal data.
+block-diagonal data; the selected rows then reach the ranks the reference's
+redistribution gives them.
 """
 import os
 import queue
@@ -70,9 +71,12 @@ def _worker(rank, world, port, scenario, out_q):
         full_idx, _ = sd.get_batch_opus_global(model, cand, cand.clone(), opt, layers, loader, 0.5, 128,
                                                selection_method="stochastic", temperature=1.0, score_len=128,
                                                preconditioner=str(g["precond"]))
+        # the selected rows moved to their ranks (one all_to_all over NCCL)
+        rx, ry = sd.redistribute_selected(full_idx, cand.to(torch.int32), cand.to(torch.int64) + 1)
         torch.cuda.synchronize()
         out_q.put((rank, scores.cpu().numpy(), blocks.cpu().numpy(), gidx.cpu().tolist(), lidx.cpu().tolist(),
-                   ggreedy.cpu().tolist(), full_idx.cpu().tolist(), dense.cpu().numpy(), gexact.cpu().tolist()))
+                   ggreedy.cpu().tolist(), full_idx.cpu().tolist(), dense.cpu().numpy(), gexact.cpu().tolist(),
+                   cand.cpu().numpy(), rx.cpu().numpy(), ry.cpu().numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -116,9 +120,13 @@ def test_sharded_selection_on_gpus(scenario):
     want_greedy = orc.greedy_selection(scores.astype(np.float32), dense, N_PICK)
     want_exact = orc.stochastic_greedy_selection(scores.astype(np.float32), g["sim"].astype(np.float32), N_PICK,
                                                  temperature=1.0, uniforms=uni)
+    cands = [results[r][8].astype(np.int32) for r in range(world)]
+    moved = orc.redistribute_selected(results[0][5], cands, [c.astype(np.int64) + 1 for c in cands])
     mapped = []
     for r in range(world):
-        _, _, gidx, lidx, ggreedy, full_idx, dense_r, gexact = results[r]
+        _, _, gidx, lidx, ggreedy, full_idx, dense_r, gexact, _, rx, ry = results[r]
+        np.testing.assert_array_equal(rx, moved[r][0])
+        np.testing.assert_array_equal(ry, moved[r][1])
         assert_close_scores(dense_r, g["sim"])  # the reference's whole-batch similarity
         assert gexact == want_exact
         assert gidx == want and ggreedy == want_greedy
