@@ -482,6 +482,8 @@ def run_gpt2(args):
     torch.cuda.synchronize()
     steps = max(1, min(args.steps, 5))
     s0, s1 = ev(), ev()
+    torch.cuda.reset_peak_memory_stats(dev)
+    held = torch.cuda.memory_allocated(dev)
     with ClockSampler(0) as clk:
         s0.record()
         for _ in range(steps):
@@ -489,6 +491,7 @@ def run_gpt2(args):
         s1.record()
         torch.cuda.synchronize()
     sel_ms = s0.elapsed_time(s1) / steps
+    sel_peak = torch.cuda.max_memory_allocated(dev) - held
     # stage 1 alone: forward over candidates + proxies, dL/dZ of every capture layer
     c0, c1 = ev(), ev()
     batch = {"input_ids": buf, "attention_mask": torch.ones_like(buf), "labels": buf.clone()}
@@ -523,6 +526,7 @@ def run_gpt2(args):
                                    "k=8192, AdamW, keep 16 by Boltzmann T=1.0", "api": "get_batch_opus"},
             "selection_overhead_pct_of_train_step": round(100.0 * sel_ms / train_ms, 2),
             "capture_ms": round(cap_ms, 3), "train_step_ms_16_seqs": round(train_ms, 3),
+            "selection_peak_gb_above_model": round(sel_peak / 1e9, 2),
             "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0

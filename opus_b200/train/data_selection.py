@@ -19,6 +19,8 @@ proxy-side dot products, which equals one dot with the summed proxy sketch
 """
 from __future__ import annotations
 
+import math
+
 import numpy as np
 import torch
 
@@ -294,6 +296,98 @@ def capture_pairs(model, batch_train, validation_loader, trainable_layers, score
     return pairs, train_bs, val_bs
 
 
+# bytes of logits one chunk of the per-position loss covers
+TOKEN_LOSS_CHUNK_BYTES = 1 << 30
+
+
+class _ShiftedTokenLoss(torch.autograd.Function):
+    """Per-position next-token cross entropy [N, T-1] from logits [N, T, V], by chunks of samples.
+
+    The reference (data_selection.py:381-387) copies logits[:, :-1] into a
+    contiguous tensor and runs cross_entropy over all of it.  That keeps the
+    copy and the whole log-softmax alive for the backward, whose dense
+    [N*(T-1), V] temporaries and zero-filled [N, T, V] slice gradient come on
+    top.  Here each chunk of samples runs the same torch cross_entropy and
+    nothing is kept but the logits; the backward recomputes each chunk and
+    writes its gradient into one [N, T, V] tensor.
+
+    Rows are independent in log_softmax / nll_loss, but inside a row torch's
+    CUDA kernels pick their reduction order from the row's 16-byte alignment.
+    So when a row (V elements) is a multiple of 16 bytes -- GPT-2's padded
+    50304-entry vocabulary, Llama's, Qwen's -- a chunk runs on all T
+    positions of the logits in place, the last one taking label -100 so that
+    position t meets label t+1.  Otherwise a chunk copies its shifted rows,
+    as the reference does, and chunks start at sample multiples that give
+    every row the alignment it has in the reference's copy.  Either way every
+    loss and gradient value equals the reference's.
+    """
+
+    @staticmethod
+    def forward(ctx, logits, labels):
+        N, T, _ = logits.shape
+        out = torch.zeros(N, T - 1, dtype=logits.dtype, device=logits.device)
+        for s, e, rows, lab in _token_loss_chunks(logits, labels):
+            loss = torch.nn.functional.cross_entropy(rows, lab, reduction="none", ignore_index=-100)
+            out[s:e] = loss.view(e - s, -1)[:, :T - 1]
+        ctx.save_for_backward(logits, labels)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        logits, labels = ctx.saved_tensors
+        N, T, V = logits.shape
+        grad = torch.empty_like(logits)
+        for s, e, rows, lab in _token_loss_chunks(logits, labels):
+            in_place = rows.shape[0] == (e - s) * T
+            g = grad_out[s:e]
+            if in_place:  # the last position carries label -100 and gradient 0
+                g = torch.cat([g, g.new_zeros(e - s, 1)], dim=1)
+            with torch.enable_grad():
+                rows = rows.detach().requires_grad_()
+                loss = torch.nn.functional.cross_entropy(rows, lab, reduction="none", ignore_index=-100)
+                (part,) = torch.autograd.grad(loss, rows, g.reshape(-1))
+            if in_place:
+                grad[s:e] = part.view(e - s, T, V)
+            else:
+                grad[s:e, :-1] = part.view(e - s, T - 1, V)
+                grad[s:e, -1] = 0
+        return grad, None
+
+
+def _token_loss_chunks(logits, labels):
+    """(first sample, end sample, rows [R, V], their labels [R]) of each chunk of the shifted loss."""
+    N, T, V = logits.shape
+    esz = logits.element_size()
+    step = max(1, TOKEN_LOSS_CHUNK_BYTES // max(1, T * V * esz))
+    in_place = (V * esz) % 16 == 0
+    if not in_place:  # chunk starts s with s * (T-1) * V * esz a multiple of 16 bytes
+        m = 16 // math.gcd(16, (T - 1) * V * esz)
+        step = max(m, step - step % m)
+    for s in range(0, N, step):
+        e = min(N, s + step)
+        if in_place:
+            lab = torch.full((e - s, T), -100, dtype=labels.dtype, device=labels.device)
+            lab[:, :-1] = labels[s:e, 1:]
+            yield s, e, logits[s:e].view(-1, V), lab.view(-1)
+        else:
+            yield s, e, logits[s:e, :-1].contiguous().view(-1, V), labels[s:e, 1:].reshape(-1)
+
+
+def per_sample_token_loss(logits, labels):
+    """Mean next-token cross entropy of each sample over its non-ignored positions (data_selection.py:380-389)."""
+    if logits.dim() != 3 or logits.shape[1] < 2:
+        shift_logits = logits[..., :-1, :].contiguous()
+        shift_labels = labels[..., 1:].contiguous()
+        tok_loss = torch.nn.functional.cross_entropy(shift_logits.view(-1, shift_logits.size(-1)),
+                                                     shift_labels.view(-1), reduction="none",
+                                                     ignore_index=-100).view(shift_labels.size())
+    else:
+        shift_labels = labels[..., 1:]
+        tok_loss = _ShiftedTokenLoss.apply(logits.contiguous(), labels)
+    mask = (shift_labels != -100).float()
+    return (tok_loss * mask).sum(dim=-1) / mask.sum(dim=-1)
+
+
 def _capture_forward(model, batch_train, validation_loader, trainable_layers, score_len, batch_val):
     """The capture forward: per-sample mean token loss over candidates + proxies, and the kept layers.
 
@@ -322,13 +416,8 @@ def _capture_forward(model, batch_train, validation_loader, trainable_layers, sc
     if was_training:
         model.train()
 
-    shift_logits = logits[..., :-1, :].contiguous()
-    shift_labels = labels[..., 1:].contiguous()
-    tok_loss = torch.nn.functional.cross_entropy(shift_logits.view(-1, shift_logits.size(-1)), shift_labels.view(-1),
-                                                 reduction="none", ignore_index=-100).view(shift_labels.size())
-    mask = (shift_labels != -100).float()
-    loss = (tok_loss * mask).sum(dim=-1) / mask.sum(dim=-1)
-    del logits, shift_logits, tok_loss
+    loss = per_sample_token_loss(logits, labels)
+    del logits
 
     raw = [layer.pre_activation for layer in trainable_layers]
     keep = [i for i, z in enumerate(raw) if isinstance(z, torch.Tensor) and z.requires_grad and z.grad_fn is not None]

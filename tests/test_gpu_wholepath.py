@@ -132,3 +132,39 @@ def test_streaming_capture_lowers_peak_memory():
         finally:
             ds.CAPTURE_MODE = "stream"
     assert peaks["stream"] < peaks["batch"], peaks
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("V", [50257, 50304])
+def test_chunked_token_loss_bit_identical_on_gpu(dtype, V, monkeypatch):
+    """GPT-2 vocabularies (odd and 16-byte-aligned rows): values equal the reference's on CUDA too."""
+    from test_host_logic import token_loss_pair
+    torch.manual_seed(0)
+    N, T = 6, 257
+    logits = (torch.randn(N, T, V, device=DEV) * 4).to(dtype)
+    labels = torch.randint(0, V, (N, T), device=DEV)
+    labels[2, 100:140] = -100
+    chunk = 2 * T * V * logits.element_size()  # three chunks of two samples
+    ref_l, ref_g, l, g = token_loss_pair(logits, labels, chunk, monkeypatch)
+    assert torch.equal(ref_l, l) and torch.equal(ref_g, g)
+
+
+def test_chunked_token_loss_lowers_peak_memory(monkeypatch):
+    """Forward + backward peak above the logits: about one gradient-sized buffer instead of several."""
+    torch.manual_seed(0)
+    N, T, V = 8, 512, 50304
+    logits = torch.randn(N, T, V, device=DEV)
+    labels = torch.randint(0, V, (N, T), device=DEV)
+    size = logits.numel() * logits.element_size()
+    monkeypatch.setattr(ds, "TOKEN_LOSS_CHUNK_BYTES", size // 8)
+    peaks = []
+    for f in (__import__("test_host_logic")._reference_token_loss, ds.per_sample_token_loss):
+        x = logits.clone().requires_grad_()
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        f(x, labels).mean().backward()
+        torch.cuda.synchronize()
+        peaks.append((torch.cuda.max_memory_allocated() - base) / size)
+        del x
+    assert peaks[1] < 1.6 and peaks[0] > peaks[1] + 1.0, peaks

@@ -257,3 +257,40 @@ def test_lora_layers():
 def test_find_gc_layers():
     model = TinyLM(GCLinear)
     assert len(ds.find_GClayers(model)) == 4
+
+
+def _reference_token_loss(logits, labels):
+    """data_selection.py:380-389 verbatim in behaviour: shifted copy, cross entropy over every row."""
+    shift_logits = logits[..., :-1, :].contiguous()
+    shift_labels = labels[..., 1:].contiguous()
+    tok = torch.nn.functional.cross_entropy(shift_logits.view(-1, shift_logits.size(-1)), shift_labels.view(-1),
+                                            reduction="none", ignore_index=-100).view(shift_labels.size())
+    mask = (shift_labels != -100).float()
+    return (tok * mask).sum(dim=-1) / mask.sum(dim=-1)
+
+
+def token_loss_pair(logits, labels, chunk_bytes, monkeypatch):
+    """(reference loss, reference grad, chunked loss, chunked grad) for the same logits."""
+    monkeypatch.setattr(ds, "TOKEN_LOSS_CHUNK_BYTES", chunk_bytes)
+    out = []
+    for f in (_reference_token_loss, ds.per_sample_token_loss):
+        x = logits.clone().requires_grad_()
+        loss = f(x, labels)
+        loss.mean().backward()
+        out += [loss.detach(), x.grad]
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("V", [97, 128])
+@pytest.mark.parametrize("chunk_bytes", [1, 20000, 1 << 30])
+def test_chunked_token_loss_bit_identical(dtype, V, chunk_bytes, monkeypatch):
+    """Chunked per-sample loss == the reference's loss and dL/dlogits, bit for bit, ignored labels included."""
+    torch.manual_seed(V)
+    logits = (torch.randn(7, 34, V) * 3).to(dtype)  # 33 shifted rows: odd chunk alignment
+    labels = torch.randint(0, V, (7, 34))
+    labels[1, 5:9] = -100
+    labels[3, :] = -100
+    labels[3, 4] = 2
+    ref_l, ref_g, l, g = token_loss_pair(logits, labels, chunk_bytes, monkeypatch)
+    assert torch.equal(ref_l, l) and torch.equal(ref_g, g)
