@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=B,
                     help="candidates per GPU (default 256; smaller only for profiling captures)")
+    ap.add_argument("--layer", default=None, metavar="D_IN,D_OUT,K",
+                    help="operator workload: another layer shape and sketch size (profiling; default 768,3072,16384)")
     ap.add_argument("--workload", default="operator", choices=["operator", "gpt2-small"],
                     help="operator: the single-layer operator (default line); gpt2-small: the whole selection "
                          "path (capture, 48 layers, selection) on a GPT-2-small-shaped model, with the "
@@ -610,8 +612,21 @@ def run_reference(args):
     return 0
 
 
+def set_layer(spec: str) -> None:
+    """Rebind the operator workload's layer shape and sketch size (d_in,d_out,k)."""
+    global D_IN, D_OUT, K_SKETCH, WORKLOAD, SKETCH_GEMM_DRAM_BYTES
+    d_in, d_out, k = (int(x) for x in spec.split(","))
+    if (d_in, d_out, k) != (D_IN, D_OUT, K_SKETCH):
+        D_IN, D_OUT, K_SKETCH = d_in, d_out, k
+        WORKLOAD = (f"isolated single-layer operator: 256 seqs x 1024 tokens, d_in {d_in} -> d_out {d_out}, "
+                    f"k={k}, AdamW diag")
+        SKETCH_GEMM_DRAM_BYTES = None  # captured for the default layer only
+
+
 def main():
     args = parse_args()
+    if args.layer:
+        set_layer(args.layer)
     if args.impl == "reference":
         return run_reference(args)
     if args.path == "ghost":

@@ -26,8 +26,10 @@
 // The sketch is converted back to f32 and added to the output row (vector
 // reductions) whenever the candidate changes.  Quantisation error per update
 // is at most (max |w G| of the first tile) * 2^-(log2(cap) - 4 + 1), i.e.
-// ~1e-6 of the tile maximum for the GPT-2 layer shapes.  When k is too large
-// for shared memory every update is an f32 global atomic add.
+// ~1e-6 of the tile maximum for the GPT-2 layer shapes.  When the k buckets
+// do not fit next to two pipeline stages (k > 32768), the sketch covers the
+// largest prefix of them that does (32768 buckets) and the updates of the
+// other buckets are f32 global atomic adds.
 //
 // Work: a job is one candidate's tiles for a contiguous range of o-blocks
 // (every column block); jobs are numbered candidate-major and dealt to CTAs
@@ -66,7 +68,7 @@ constexpr int kTmemCols = 2 * kTileN;  // two accumulators
 
 struct SmemPlan {
   int stages;
-  int smem_sketch;   // 1: CTA-private fixed-point sketch in shared memory
+  int64_t k_sm;      // buckets [0, k_sm) have a CTA-private fixed-point sketch in shared memory
   size_t bytes;      // dynamic shared memory to request
 };
 
@@ -100,12 +102,13 @@ __device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatil
   return ok;
 }
 
-// Add the fixed-point sketch (scaled by 2^-scale_exp) into dst and clear it.
+// Add the fixed-point sketch of buckets [0, k) (scaled by 2^-scale_exp) into
+// dst and clear it.
 __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int et, uint64_t* bar,
                              uint32_t& phase, volatile int* abort_flag, int* err) {
   if (!epi_sync(bar, phase, abort_flag, err)) return false;
   const float inv = ldexpf(1.0f, -scale_exp);
-  if ((k & 3) == 0) {
+  if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     int4* s4 = reinterpret_cast<int4*>(sk);
     for (int64_t i = et; i < k / 4; i += kEpiThreads) {
       const int4 q = s4[i];
@@ -129,14 +132,15 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
-                       int n_cb, int groups, int64_t k, int rows_div, int stages, int smem_sketch, float cap,
+                       int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
                        int cap_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* stage_mem = smem;
   int* sk = reinterpret_cast<int*>(smem + (size_t)stages * kStageBytes);
-  uint8_t* tail = smem + (size_t)stages * kStageBytes + (smem_sketch ? (size_t)k * 4 : 0);
+  const bool smem_sketch = k_sm > 0;
+  uint8_t* tail = smem + (size_t)stages * kStageBytes + (size_t)k_sm * 4;
   tail = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tail) + 15) & ~uintptr_t(15));
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
@@ -179,9 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
-  if (smem_sketch) {
-    for (int64_t i = threadIdx.x; i < k; i += kThreads) sk[i] = 0;
-  }
+  for (int64_t i = threadIdx.x; i < k_sm; i += kThreads) sk[i] = 0;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -276,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;              // tile row owned by this thread
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t kk32 = static_cast<uint32_t>(k);
+    const uint32_t ksm32 = static_cast<uint32_t>(k_sm);
     const uint64_t table_policy = l2_policy_evict_last();
     int acc = 0;
     uint32_t aph = 0;
@@ -292,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t tile = (int64_t)ob * n_cb + cb;
       float* out_row = phi + (int64_t)(b / rows_div) * k;
       if (smem_sketch && job != cur_job) {
-        if (cur_job >= 0 && !flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k, scale_exp, et, epi_bar,
+        if (cur_job >= 0 && !flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, epi_bar,
                                           epi_phase, abort_flag, err)) {
           ok = false;
           break;
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               continue;
             }
             const float y = x * S;
-            if (use_int && fabsf(y) < cap) {
+            if (use_int && bucket < ksm32 && fabsf(y) < cap) {
               atomicAdd(sk + bucket, __float2int_rn(y));
             } else if (x != 0.0f) {
               atomicAdd(out_row + bucket, x);   // outlier, non-finite, unscaled or no shared sketch
@@ -392,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (ok && smem_sketch && cur_job >= 0)
-      flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k, scale_exp, et, epi_bar, epi_phase, abort_flag,
+      flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, epi_bar, epi_phase, abort_flag,
                    err);
     if (bad) record_device_error(err, kDevBadBucket);
   }
@@ -410,11 +413,19 @@ SmemPlan plan_smem(int64_t k) {
   for (int st = 6; st >= 2; --st) {
     const size_t need = fixed + (size_t)st * kStageBytes + (size_t)k * 4;
     if (need <= limit) {
-      p = {st, 1, need};
+      p = {st, k, need};
       return p;
     }
   }
-  // Sketch does not fit next to two stages: scatter straight into HBM/L2.
+  // The whole sketch does not fit next to two stages.  Keep the largest
+  // prefix of the buckets (a multiple of 1024) that does: updates of those
+  // buckets stay in shared memory, the rest go to L2 atomics, whose rate
+  // bounds the kernel at this size, so coverage beats a third stage.
+  if (fixed + 2 * (size_t)kStageBytes < limit) {
+    const int64_t k_sm = static_cast<int64_t>((limit - fixed - 2 * (size_t)kStageBytes) / 4) & ~int64_t(1023);
+    if (k_sm >= 4096) return {2, k_sm < k ? k_sm : k, fixed + 2 * (size_t)kStageBytes + (size_t)k_sm * 4};
+  }
+  // No room for a useful prefix: scatter straight into HBM/L2.
   for (int st = 4; st >= 2; --st) {
     const size_t need = fixed + (size_t)st * kStageBytes;
     if (need <= limit) return {st, 0, need};
@@ -478,10 +489,11 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
     while ((int64_t(1) << (cap_log2 + 1)) <= cap_int) ++cap_log2;
     if (cap_log2 < 2 * kHeadroomLog2) max_bucket_load = 0;  // too little range left for fixed point
   }
-  if (max_bucket_load <= 0 && plan.smem_sketch) {
+  if (max_bucket_load <= 0 && plan.k_sm > 0) {
     // No usable bound: every update goes to global f32 atomics; use the smem for stages.
     for (int stg = 4; stg >= 2; --stg) {
-      const size_t need = plan.bytes - (size_t)plan.stages * kStageBytes - (size_t)k * 4 + (size_t)stg * kStageBytes;
+      const size_t need =
+          plan.bytes - (size_t)plan.stages * kStageBytes - (size_t)plan.k_sm * 4 + (size_t)stg * kStageBytes;
       if (need <= static_cast<size_t>(max_smem_optin())) {
         plan = {stg, 0, need};
         break;
@@ -510,7 +522,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   int* err = device_error_word();
   sketch_gemm_kernel<<<grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows,
                                                         seq_len, n_ob, n_cb, groups, k, rows_div, plan.stages,
-                                                        plan.smem_sketch, cap, cap_log2, err);
+                                                        plan.k_sm, cap, cap_log2, err);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

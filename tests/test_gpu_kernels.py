@@ -113,7 +113,9 @@ SKETCH_SHAPES = [
     (2, 130, 200, 264, 1000),
     (4, 64, 384, 768, 16384),
     (2, 70, 128, 256, 32768),
-    (2, 64, 136, 264, 65536),
+    (2, 64, 136, 264, 65536),     # shared-memory sketch of the first 32768 buckets, L2 atomics above
+    (3, 40, 136, 264, 40001),     # odd k: rows of phi start off 16-byte boundaries
+    (2, 64, 128, 512, 131072),
     (5, 33, 136, 520, 8192),
 ]
 
