@@ -192,6 +192,22 @@ def gen_wholepath(ds, ref_linear):
              np_seed=np.array(77), **{f"w/{k}": v for k, v in weights.items()}, **opt_arrays)
 
 
+def gen_ppl(ds, ref_linear):
+    """get_batch_opus with selection_strategy="ppl": per-sequence model loss ranked high / low / mid."""
+    rng = np.random.default_rng(21)
+    torch.manual_seed(3)
+    model = TinyLM(ref_linear, vocab=256)
+    cand = zipf_tokens(rng, 10, 128, 256)
+    ct = torch.from_numpy(cand)
+    out = {}
+    for mode in ("high", "low", "mid"):
+        for ratio in (0.3, 0.9):  # mid: enough candidates near the median, and the fill path
+            idx = ds.get_batch_opus(model, ct, ct.clone(), None, None, None, [], None, ratio, 128,
+                                    selection_strategy="ppl", selection_method=mode, score_len=128)
+            out[f"{mode}_{ratio}"] = idx.numpy()
+    save("ppl", cand=cand, **out, **{f"w/{k}": v for k, v in state_to_numpy(model).items()})
+
+
 LORA_SCENARIOS = {"lora_proj": True, "lora_noproj": False}
 
 
@@ -297,6 +313,9 @@ def main() -> int:
     if args.only == "lora":
         gen_wholepath_lora(ds, GCLoRALinear)
         return 0
+    if args.only == "ppl":
+        gen_ppl(ds, GCLinear)
+        return 0
     gen_tables(rp)
     gen_project(rp)
     gen_select(ds)
@@ -305,6 +324,7 @@ def main() -> int:
     gen_muon(ds)
     gen_wholepath(ds, GCLinear)
     gen_wholepath_lora(ds, GCLoRALinear)
+    gen_ppl(ds, GCLinear)
     return 0
 
 

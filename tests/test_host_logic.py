@@ -294,3 +294,17 @@ def test_chunked_token_loss_bit_identical(dtype, V, chunk_bytes, monkeypatch):
     labels[3, 4] = 2
     ref_l, ref_g, l, g = token_loss_pair(logits, labels, chunk_bytes, monkeypatch)
     assert torch.equal(ref_l, l) and torch.equal(ref_g, g)
+
+
+@pytest.mark.parametrize("mode", ["high", "low", "mid"])
+@pytest.mark.parametrize("ratio", [0.3, 0.9])
+def test_ppl_strategy_matches_reference(mode, ratio):
+    """selection_strategy="ppl": the reference's loss ranking, mid quantile band and fill path included."""
+    g = load_golden("ppl")
+    torch.manual_seed(3)
+    model = TinyLM(GCLinear, vocab=256)
+    load_numpy_state(model, g)
+    ct = torch.from_numpy(g["cand"])
+    idx = ds.get_batch_opus(model, ct, ct.clone(), None, None, None, [], None, ratio, 128,
+                            selection_strategy="ppl", selection_method=mode, score_len=128)
+    assert idx.tolist() == g[f"{mode}_{ratio}"].tolist()
