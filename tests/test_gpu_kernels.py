@@ -201,8 +201,10 @@ def test_project_full_gradient_golden():
 
 
 @pytest.mark.parametrize("transposed", [False, True])
-@pytest.mark.parametrize("d_out,d_in,k", [(64, 96, 256), (3072, 768, 16384), (100, 36, 100000)])
+@pytest.mark.parametrize("d_out,d_in,k", [(64, 96, 256), (3072, 768, 16384), (200, 300, 1001), (512, 1024, 40000),
+                                         (100, 36, 100000)])
 def test_sketch_dense(transposed, d_out, d_in, k):
+    """Shared-memory sketch per CTA (k up to ~55000; odd k flushes scalar), L2 atomics above."""
     h, s, packed = cuda_tables(d_out * d_in, 5, k)
     W = torch.randn(d_out, d_in, device=DEV)
     diag = torch.rand(d_out, d_in, device=DEV)
