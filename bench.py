@@ -42,7 +42,7 @@ METRIC = "candidate seqs scored+selected/sec"
 UNIT = "candidates/s"
 WORKLOAD = "isolated single-layer operator: 256 seqs x 1024 tokens, d_in 768 -> d_out 3072, k=16384, AdamW diag"
 # dram__bytes_read.sum + dram__bytes_write.sum per sketch_gemm launch of this workload
-# (ncu single-pass capture of the bench command with dram__bytes_read.sum and dram__bytes_write.sum, mean of its two launches)
+# (single-pass ncu capture of the bench command, mean of its two sketch_gemm launches)
 SKETCH_GEMM_DRAM_BYTES = 3.20e9
 
 
