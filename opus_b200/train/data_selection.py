@@ -144,14 +144,18 @@ def _find_group_for_param(optimizer, p):
     return optimizer.param_groups[0]
 
 
-def global_C_t(optimizer, p):
-    """AdamW scalar lr*(1-b1)*sqrt(1-b2^t)/(1-b1^t) as a float32 tensor (data_selection.py:182-195)."""
+def _C_t_value(optimizer, p) -> float:
     g = _find_group_for_param(optimizer, p)
     beta1, beta2 = g["betas"]
     t = _get_step_from_optimizer(optimizer)
     num = max(1e-16, 1.0 - beta2 ** t) ** 0.5
     den = max(1e-16, 1.0 - beta1 ** t)
-    return torch.tensor(g["lr"] * (1.0 - beta1) * num / den, dtype=torch.float32, device=p.device)
+    return g["lr"] * (1.0 - beta1) * num / den
+
+
+def global_C_t(optimizer, p):
+    """AdamW scalar lr*(1-b1)*sqrt(1-b2^t)/(1-b1^t) as a float32 tensor (data_selection.py:182-195)."""
+    return torch.tensor(_C_t_value(optimizer, p), dtype=torch.float32, device=p.device)
 
 
 def _inv_rms_scalar_for_param(p, group, state):
@@ -170,12 +174,16 @@ def _inv_rms_tensor_for_param(group, state):
     return (v.sqrt() + group.get("eps", 1e-8)).reciprocal().to(dtype=torch.float32)
 
 
-def global_C_t_muon(optimizer, p):
-    """Muon scalar eff_lr * (1 - momentum^2) (data_selection.py:217-225)."""
+def _C_t_muon_value(optimizer, p) -> float:
     g = _find_group_for_param(optimizer, p)
     lr = g["lr"] * max(1, p.size(-2) / p.size(-1)) ** 0.5 * getattr(p, "lr_mul", 1.0)
     mu = g.get("momentum", 0.0)
-    return torch.tensor(lr * (1.0 - mu ** 2), dtype=torch.float32, device=p.device)
+    return lr * (1.0 - mu ** 2)
+
+
+def global_C_t_muon(optimizer, p):
+    """Muon scalar eff_lr * (1 - momentum^2) (data_selection.py:217-225)."""
+    return torch.tensor(_C_t_muon_value(optimizer, p), dtype=torch.float32, device=p.device)
 
 
 _MUON_COEFFS = (3.4445, -4.7750, 2.0315)
@@ -473,13 +481,14 @@ class _PrecondTables:
             if kind == "muon":
                 if p in opt_p.state:
                     self.S_map[p] = _get_muon_S_matrix(p, opt_p)
-                self.muon_scale[p] = global_C_t_muon(opt_p, p).to(dtype=torch.float32)
+                # the float32 scalars stay on the host: no device round trip per layer
+                self.muon_scale[p] = np.float32(_C_t_muon_value(opt_p, p))
             elif kind == "adamw":
-                self.adamw[p] = (global_C_t(opt_p, p).to(dtype=torch.float32), group, opt_p.state.get(p, {}))
+                self.adamw[p] = (np.float32(_C_t_value(opt_p, p)), group, opt_p.state.get(p, {}))
 
     def plan(self, pid, pr, device):
         p, g_t = pr.p, pr.g_t
-        scale = torch.tensor(1.0)
+        scale = np.float32(1.0)
         layer_scale = 1.0
         v_sq, eps = None, 1e-8
         eff = "sgd"
@@ -496,7 +505,7 @@ class _PrecondTables:
                         v_sq, eps = state_p["exp_avg_sq"], group_p.get("eps", 1e-8)
                 if eff != "sgd" and p.ndim >= 2:
                     layer_scale = 1.0 / float((p.shape[-1] * p.shape[-2]) ** 0.5)
-        c = float((scale.detach().cpu().to(torch.float32) * layer_scale).item())
+        c = float(np.float32(scale * np.float32(layer_scale)))  # float32 C * ls, as the tensor product
         if v_sq is not None:
             v_sq = v_sq.detach().to(device=device, dtype=torch.float32)
         return LayerPlan(pid, eff, g_t, pr.a_t, pr.g_v, pr.a_v, c, v_sq, eps)
