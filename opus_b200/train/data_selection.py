@@ -144,10 +144,11 @@ def _find_group_for_param(optimizer, p):
     return optimizer.param_groups[0]
 
 
-def _C_t_value(optimizer, p) -> float:
+def _C_t_value(optimizer, p, t=None) -> float:
     g = _find_group_for_param(optimizer, p)
     beta1, beta2 = g["betas"]
-    t = _get_step_from_optimizer(optimizer)
+    if t is None:
+        t = _get_step_from_optimizer(optimizer)
     num = max(1e-16, 1.0 - beta2 ** t) ** 0.5
     den = max(1e-16, 1.0 - beta1 ** t)
     return g["lr"] * (1.0 - beta1) * num / den
@@ -472,6 +473,7 @@ class _PrecondTables:
         self.auto_mode = preconditioner == "auto"
         self.preconditioner = preconditioner
         self.S_map, self.muon_scale, self.adamw = {}, {}, {}
+        steps = {}  # the optimizer-wide step, once per optimizer rather than once per parameter
         for p in {q for q in params if q is not None}:
             opt_p = self.param2opt.get(p, None)
             if opt_p is None:
@@ -484,7 +486,9 @@ class _PrecondTables:
                 # the float32 scalars stay on the host: no device round trip per layer
                 self.muon_scale[p] = np.float32(_C_t_muon_value(opt_p, p))
             elif kind == "adamw":
-                self.adamw[p] = (np.float32(_C_t_value(opt_p, p)), group, opt_p.state.get(p, {}))
+                if id(opt_p) not in steps:
+                    steps[id(opt_p)] = _get_step_from_optimizer(opt_p)
+                self.adamw[p] = (np.float32(_C_t_value(opt_p, p, steps[id(opt_p)])), group, opt_p.state.get(p, {}))
 
     def plan(self, pid, pr, device):
         p, g_t = pr.p, pr.g_t
