@@ -146,6 +146,23 @@ OPUS_API int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_
                      int rows_div, float* phi, int accumulate, void* stream);
 
 /*
+ * G-ghost (projection off) — exact per-sample gradients for the similarity.
+ * Replaces the per-sample gradient materialisation of weighted_grad_dotprod
+ * (OPUS/train/data_selection.py:255-292, 32-row chunks of the per-example
+ * gradient of OPUS/layers/linear.py:41-68, times the diagonal) and of
+ * grad_dotprod (OPUS/train/data_selection.py:597-619).
+ *   out[b, o*d_in + c] (+)= diag[o, c] * sum_t dLdZ[b, t, o] * a[b, t, c]
+ * dLdZ [n_rows, seq_len, d_out] and a [n_rows, seq_len, d_in] bf16 (dtype
+ * OPUS_DTYPE_BF16), d_out and d_in multiples of 8; diag [d_out, d_in] f32 or
+ * NULL (no weighting); out [n_rows, d_out*d_in] f32, written in full unless
+ * accumulate.  The tcgen05 GEMM of opus_sketch_gemm with a dense epilogue:
+ * each element has one writer, so no scatter and no atomics (vector
+ * reductions when accumulating).
+ */
+OPUS_API int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
+                         int d_in, const float* diag, float* out, int accumulate, void* stream);
+
+/*
  * K1 — dense CountSketch of one [d_out,d_in] f32 matrix (the proxy target
  * direction): sketch[h(o,c)] += s(o,c) * diag(o,c) * w(o,c), with w read as
  * w[o*d_in+c] (transposed = 0) or w[c*d_out+o] (transposed = 1); diag may be

@@ -84,6 +84,16 @@ __device__ __forceinline__ uint4 ld_table(const uint4* p, uint64_t l2_policy) {
   return v;
 }
 
+// Read-only 16-byte load kept in L2 with the given policy (the dense
+// epilogue's diagonal, read again by every candidate).
+__device__ __forceinline__ float4 ld_f4_hint(const float* p, uint64_t l2_policy) {
+  float4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p), "l"(l2_policy));
+  return v;
+}
+
 // O-block range [begin, end) of job j: each candidate's o-blocks are split
 // into `groups` contiguous ranges.
 __device__ __forceinline__ int job_ob_begin(int64_t job, int groups, int n_ob) {
@@ -133,7 +143,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
                        int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
-                       int cap_log2, int* err) {
+                       int cap_log2, int* err, int dense, const float* __restrict__ dense_diag, int d_out,
+                       int d_in, int accumulate) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -269,6 +280,80 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Drain: every MMA issued above must be complete before TMEM is freed.
       umma_commit(drain_bar);
       mbar_wait(drain_bar, 0, nullptr, err, kDevTimeoutDrain);
+    }
+  } else if (dense) {
+    // ------------------------------------------------- dense epilogue
+    // Per-sample gradients: element (o, c) of G_b, times dense_diag[o, c]
+    // when given, goes to phi[b, o * d_in + c].  Every element has exactly
+    // one writer, so 16-byte streaming stores (vector reductions when
+    // accumulating) replace the scatter; each thread writes 128 contiguous
+    // bytes of its row per chunk.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    const uint64_t diag_policy = l2_policy_evict_last();  // every candidate re-reads the diagonal
+    const int64_t numel = (int64_t)d_out * d_in;
+    const bool vec = ((reinterpret_cast<uintptr_t>(phi) | reinterpret_cast<uintptr_t>(dense_diag)) & 15) == 0;
+    int acc = 0;
+    uint32_t aph = 0;
+    bool ok = true;
+    for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+    for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
+    for (int cb = 0; cb < n_cb && ok; ++cb) {
+      const int b = static_cast<int>(job / groups);
+      if (!mbar_wait(&tfull[acc], aph, abort_flag, err, kDevTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int o = ob * kTileM + r;
+      const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
+#pragma unroll 1
+      for (int jj = 0; jj < kChunksPerWarp; ++jj) {
+        const int j = half * kChunksPerWarp + jj;
+        const int c0 = cb * kTileN + j * kChunkCols;
+        uint32_t v[32];
+        tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
+        tmem_ld_wait();
+        if (jj == kChunksPerWarp - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        if (o >= d_out || c0 >= d_in) continue;
+        float* dst = phi + (int64_t)b * numel + (int64_t)o * d_in + c0;
+        const float* drow = dense_diag != nullptr ? dense_diag + (int64_t)o * d_in + c0 : nullptr;
+        if (vec && c0 + kChunkCols <= d_in) {
+#pragma unroll
+          for (int u = 0; u < kChunkCols / 4; ++u) {
+            float4 w = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+            if (drow != nullptr) w = ld_f4_hint(drow + 4 * u, diag_policy);
+            float4 x;
+            x.x = drow != nullptr ? __uint_as_float(v[4 * u]) * w.x : __uint_as_float(v[4 * u]);
+            x.y = drow != nullptr ? __uint_as_float(v[4 * u + 1]) * w.y : __uint_as_float(v[4 * u + 1]);
+            x.z = drow != nullptr ? __uint_as_float(v[4 * u + 2]) * w.z : __uint_as_float(v[4 * u + 2]);
+            x.w = drow != nullptr ? __uint_as_float(v[4 * u + 3]) * w.w : __uint_as_float(v[4 * u + 3]);
+            if (accumulate)
+              red_add_v4(dst + 4 * u, x.x, x.y, x.z, x.w);
+            else
+              __stcs(reinterpret_cast<float4*>(dst + 4 * u), x);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < kChunkCols; ++u) {
+            if (c0 + u >= d_in) break;
+            const float x = drow != nullptr ? __uint_as_float(v[u]) * drow[u] : __uint_as_float(v[u]);
+            if (accumulate)
+              atomicAdd(dst + u, x);
+            else
+              dst[u] = x;
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        aph ^= 1;
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -433,6 +518,49 @@ SmemPlan plan_smem(int64_t k) {
   return p;
 }
 
+// TMA maps of the two operands: dLdZ [n_rows, seq_len, d_out] and
+// a [n_rows, seq_len, d_in], bf16, boxes of 64 features x kBK tokens.
+int encode_operands(const void* dLdZ, const void* a, int n_rows, int seq_len, int d_out, int d_in, CUtensorMap* tm_g,
+                    CUtensorMap* tm_a) {
+  {
+    const uint64_t dims[3] = {(uint64_t)d_out, (uint64_t)seq_len, (uint64_t)n_rows};
+    const uint64_t strides[2] = {(uint64_t)d_out * 2, (uint64_t)seq_len * d_out * 2};
+    const uint32_t box[3] = {kBoxMN, kBK, 1};
+    int rc = encode_tmap(tm_g, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dLdZ, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  const uint64_t dims[3] = {(uint64_t)d_in, (uint64_t)seq_len, (uint64_t)n_rows};
+  const uint64_t strides[2] = {(uint64_t)d_in * 2, (uint64_t)seq_len * d_in * 2};
+  const uint32_t box[3] = {kBoxMN, kBK, 1};
+  return encode_tmap(tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+struct JobPlan {
+  int groups;
+  int64_t n_jobs;
+  int grid;
+};
+
+// Split each candidate's o-blocks into `groups` jobs so that the rounds of
+// jobs over the SMs waste the least time: minimise ceil(jobs / SMs) x
+// (o-blocks per job), preferring larger jobs on ties.
+JobPlan plan_jobs(int n_rows, int n_ob) {
+  const int sms = sm_count();
+  int groups = 1;
+  int64_t best = -1;
+  for (int q = 1; q <= n_ob; ++q) {
+    const int64_t jobs = (int64_t)n_rows * q;
+    const int64_t cost = ((jobs + sms - 1) / sms) * ((n_ob + q - 1) / q);
+    if (best < 0 || cost < best) {
+      best = cost;
+      groups = q;
+    }
+  }
+  const int64_t n_jobs = (int64_t)n_rows * groups;
+  return {groups, n_jobs, static_cast<int>(n_jobs < sms ? n_jobs : sms)};
+}
+
 }  // namespace
 }  // namespace opus
 
@@ -461,22 +589,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   if (n_rows == 0 || seq_len == 0) return OPUS_OK;
 
   CUtensorMap tm_g, tm_a;
-  {
-    const uint64_t dims[3] = {(uint64_t)d_out, (uint64_t)seq_len, (uint64_t)n_rows};
-    const uint64_t strides[2] = {(uint64_t)d_out * 2, (uint64_t)seq_len * d_out * 2};
-    const uint32_t box[3] = {kBoxMN, kBK, 1};
-    int rc = encode_tmap(&tm_g, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dLdZ, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  {
-    const uint64_t dims[3] = {(uint64_t)d_in, (uint64_t)seq_len, (uint64_t)n_rows};
-    const uint64_t strides[2] = {(uint64_t)d_in * 2, (uint64_t)seq_len * d_in * 2};
-    const uint32_t box[3] = {kBoxMN, kBK, 1};
-    int rc = encode_tmap(&tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
+  if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a)) return rc;
   SmemPlan plan = plan_smem(k);
   if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small");
   // Fixed-point cap: max_bucket_load admitted updates of magnitude <= cap sum to < 2^31.
@@ -503,26 +616,47 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
-  // Split each candidate's o-blocks into `groups` jobs so that the rounds of
-  // jobs over the SMs waste the least time: minimise ceil(jobs / SMs) x
-  // (o-blocks per job), preferring larger jobs on ties.
-  const int sms = sm_count();
-  int groups = 1;
-  int64_t best = -1;
-  for (int q = 1; q <= n_ob; ++q) {
-    const int64_t jobs = (int64_t)n_rows * q;
-    const int64_t cost = ((jobs + sms - 1) / sms) * ((n_ob + q - 1) / q);
-    if (best < 0 || cost < best) {
-      best = cost;
-      groups = q;
-    }
-  }
-  const int64_t n_jobs = (int64_t)n_rows * groups;
-  const int grid = static_cast<int>(n_jobs < sms ? n_jobs : sms);
+  const JobPlan jp = plan_jobs(n_rows, n_ob);
   int* err = device_error_word();
-  sketch_gemm_kernel<<<grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows,
-                                                        seq_len, n_ob, n_cb, groups, k, rows_div, plan.stages,
-                                                        plan.k_sm, cap, cap_log2, err);
+  sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
+      tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_ob, n_cb, jp.groups, k, rows_div,
+      plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in, accumulate);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
+                                    int d_in, const float* diag, float* out, int accumulate, void* stream) {
+  if (dtype != OPUS_DTYPE_BF16)
+    return set_error(OPUS_ERR_UNSUPPORTED,
+                     "per_sample_grad: operands must be bf16 (split f32 operands into bf16 hi/lo with opus_split_bf16)");
+  if (n_rows < 0 || seq_len < 0 || d_out <= 0 || d_in <= 0)
+    return set_error(OPUS_ERR_INVALID, "per_sample_grad: bad sizes (n=%d T=%d d_out=%d d_in=%d)", n_rows, seq_len,
+                     d_out, d_in);
+  if (d_out % 8 != 0 || d_in % 8 != 0)
+    return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: d_out and d_in must be multiples of 8 (got %d, %d)",
+                     d_out, d_in);
+  if ((n_rows > 0 && !out) || (n_rows > 0 && seq_len > 0 && (!dLdZ || !a)))
+    return set_error(OPUS_ERR_INVALID, "per_sample_grad: NULL pointer");
+  if (n_rows == 0) return OPUS_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t numel = (int64_t)d_out * d_in;
+  if (seq_len == 0) {  // no tokens: every gradient is zero
+    if (!accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)n_rows * numel * sizeof(float), st));
+    return OPUS_OK;
+  }
+  CUtensorMap tm_g, tm_a;
+  if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a)) return rc;
+  const SmemPlan plan = plan_smem(0);  // no sketch: all of shared memory for pipeline stages
+  if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(plan.bytes)));
+  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
+  const JobPlan jp = plan_jobs(n_rows, n_ob);
+  int* err = device_error_word();
+  sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, nullptr, out, n_rows, seq_len, n_ob, n_cb,
+                                                            jp.groups, numel, 1, plan.stages, 0, 0.0f, 0, err,
+                                                            /*dense*/ 1, diag, d_out, d_in, accumulate);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -167,6 +167,65 @@ def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int
     return out
 
 
+def per_sample_grad(dLdZ: torch.Tensor, a: torch.Tensor, diag: torch.Tensor | None = None,
+                    out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """out[b] (+)= (diag o dLdZ_b^T a_b) flattened: exact per-sample gradients [B, d_out*d_in] in f32.
+
+    dLdZ [B, T, d_out] and a [B, T, d_in] in bf16 (tensor cores directly) or
+    f32 (split into bf16 hi/lo; hi*hi + hi*lo + lo*hi accumulated).  Widths
+    that are not multiples of 8 are zero-padded for the kernel and the result
+    is cut back to [B, d_out*d_in].
+    """
+    _cuda(dLdZ, "dLdZ")
+    _cuda(a, "a")
+    if dLdZ.dim() != 3 or a.dim() != 3 or dLdZ.shape[:2] != a.shape[:2]:
+        raise ValueError(f"Unexpected dLdZ/a shapes: {tuple(dLdZ.shape)}, {tuple(a.shape)}")
+    B, T, d_out = dLdZ.shape
+    d_in = a.shape[2]
+    if diag is not None:
+        if tuple(diag.shape) != (d_out, d_in):
+            raise ValueError(f"diag must be [{d_out}, {d_in}], got {tuple(diag.shape)}")
+        diag = _contig(_cuda(diag, "diag").to(torch.float32))
+    if out is None:
+        out = torch.empty(B, d_out * d_in, dtype=torch.float32, device=dLdZ.device)
+        accumulate = False
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < B * d_out * d_in:
+        raise ValueError("out must be a contiguous float32 tensor of at least [B, d_out * d_in]")
+    do_p, di_p = (d_out + 7) // 8 * 8, (d_in + 7) // 8 * 8
+    padded = (do_p, di_p) != (d_out, d_in)
+    if padded:
+        dLdZ = torch.nn.functional.pad(dLdZ, (0, do_p - d_out))
+        a = torch.nn.functional.pad(a, (0, di_p - d_in))
+        if diag is not None:
+            diag = torch.nn.functional.pad(diag, (0, di_p - d_in, 0, do_p - d_out))
+        target = torch.empty(B, do_p * di_p, dtype=torch.float32, device=dLdZ.device)
+    else:
+        target = out
+    lib = _lib.load()
+
+    def launch(g: torch.Tensor, x: torch.Tensor, acc: bool) -> None:
+        _lib.check(lib.opus_per_sample_grad(_ptr(g), _ptr(x), _lib.DTYPE_BF16, B, T, do_p, di_p, _ptr(diag),
+                                            _ptr(target), int(acc), _stream(g)), "opus_per_sample_grad")
+
+    first_acc = accumulate and not padded
+    if dLdZ.dtype == torch.bfloat16 and a.dtype == torch.bfloat16:
+        launch(_contig(dLdZ), _contig(a), first_acc)
+    else:
+        g_hi, g_lo = split_bf16(dLdZ)
+        a_hi, a_lo = split_bf16(a)
+        launch(g_hi, a_hi, first_acc)
+        launch(g_hi, a_lo, True)
+        launch(g_lo, a_hi, True)
+    if padded:
+        view = target.view(B, do_p, di_p)[:, :d_out, :d_in].reshape(B, d_out * d_in)
+        dst = out.view(-1)[:B * d_out * d_in].view(B, d_out * d_in)
+        if accumulate:
+            dst += view
+        else:
+            dst.copy_(view)
+    return out
+
+
 def sketch_dense(w: torch.Tensor, packed: torch.Tensor, d_out: int, d_in: int, k: int, transposed: bool = False,
                  diag: torch.Tensor | None = None, out: torch.Tensor | None = None,
                  accumulate: bool = False, rows: tuple[int, int] | None = None) -> torch.Tensor:

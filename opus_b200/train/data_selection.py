@@ -215,8 +215,8 @@ def weighted_grad_dotprod(A1, B1, A2, B2, diagonal_weight: torch.Tensor, weight_
     """<D o G1_i, G2_j> (or <D o G1_i, D o G2_j>) for all pairs (data_selection.py:255-292).
 
     A* are dL/dZ factors [B, D_out] / [B, T, D_out], B* activations.  The
-    per-sample gradients are formed once per side by the sketch kernel with an
-    identity table (bucket = flat index), then contracted with one Gram pass.
+    per-sample gradients are formed once per side by the tensor-core GEMM with
+    a dense epilogue (ops.per_sample_grad), then contracted with one Gram pass.
     """
     if diagonal_weight.ndim != 2:
         raise ValueError(f"Expected diagonal_weight with shape [D_out, D_in], got {tuple(diagonal_weight.shape)}")
@@ -228,28 +228,11 @@ def weighted_grad_dotprod(A1, B1, A2, B2, diagonal_weight: torch.Tensor, weight_
     return ops.sketch_gram(lhs, rhs)
 
 
-def _identity_projector(numel: int) -> GradientProjector:
-    return _IdentityTables(numel)
-
-
-class _IdentityTables(GradientProjector):
-    """Projector whose bucket is the flat weight index and sign +1 (exact materialisation)."""
-
-    def __init__(self, numel: int):
-        super().__init__(sketch_dim=numel, seed=0, device="cpu", enabled=True)
-
-    def _generate(self, param_numel: int, param_id: int):
-        h = torch.arange(param_numel, dtype=torch.long)
-        return h, torch.ones(param_numel, dtype=torch.float32)
-
-
 def _materialize(dLdZ, a, diag=None):
     """Per-sample gradients D o (dLdZ_b^T a_b) flattened to [B, D_out*D_in] in f32."""
     if dLdZ.dim() == 2:
         dLdZ, a = dLdZ.unsqueeze(1), a.unsqueeze(1)
-    d_out, d_in = dLdZ.shape[2], a.shape[2]
-    proj = _identity_projector(d_out * d_in)
-    return proj.sketch(dLdZ, a, 0, diag=diag)
+    return ops.per_sample_grad(dLdZ, a, diag=diag)
 
 
 def find_GClayers(model):

@@ -350,3 +350,39 @@ def test_empty_inputs():
     assert ops.boltzmann_select(sc, sim, 0, 1.0, torch.empty(0, dtype=torch.float64)).numel() == 0
     assert ops.greedy_select(sc, sim, 0).numel() == 0
     ops.check_device_error("empty inputs")
+
+
+@pytest.mark.parametrize("B,T,d_out,d_in,dtype,with_diag", [
+    (3, 64, 128, 256, torch.bfloat16, True),
+    (2, 100, 72, 48, torch.bfloat16, False),      # partial tiles in both dimensions
+    (2, 70, 136, 264, torch.bfloat16, True),
+    (3, 33, 20, 30, torch.float32, True),         # widths padded to 8, f32 split into bf16 hi/lo
+    (4, 1, 384, 768, torch.bfloat16, True),
+])
+def test_per_sample_grad_matches_oracle(B, T, d_out, d_in, dtype, with_diag):
+    """Dense epilogue of the tensor-core GEMM: exact per-sample gradients, times the diagonal."""
+    torch.manual_seed(B + T + d_out)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).to(dtype)
+    a = torch.randn(B, T, d_in, device=DEV).to(dtype)
+    diag = torch.rand(d_out, d_in, device=DEV) * 1e-3 + 1e-6 if with_diag else None
+    got = ops.per_sample_grad(g, a, diag=diag)
+    ops.check_device_error("per_sample_grad")
+    gd, ad = g.double().cpu().numpy(), a.double().cpu().numpy()
+    want = np.einsum("bto,btc->boc", gd, ad)
+    if with_diag:
+        want = want * diag.double().cpu().numpy()
+    rel_close(got.cpu().numpy(), want.reshape(B, -1), 1e-4 if dtype == torch.float32 else 1e-5, "per_sample_grad")
+    # accumulate adds onto what is there
+    acc = got.clone()
+    ops.per_sample_grad(g, a, diag=diag, out=acc, accumulate=True)
+    rel_close(acc.cpu().numpy(), 2 * want.reshape(B, -1), 1e-4 if dtype == torch.float32 else 1e-5, "accumulate")
+
+
+def test_per_sample_grad_empty_and_tokenless():
+    g = torch.zeros(0, 8, 16, device=DEV, dtype=torch.bfloat16)
+    a = torch.zeros(0, 8, 24, device=DEV, dtype=torch.bfloat16)
+    assert ops.per_sample_grad(g, a).shape == (0, 16 * 24)
+    g = torch.zeros(2, 0, 16, device=DEV, dtype=torch.bfloat16)
+    a = torch.zeros(2, 0, 24, device=DEV, dtype=torch.bfloat16)
+    out = torch.full((2, 16 * 24), 5.0, device=DEV)
+    assert not ops.per_sample_grad(g, a, out=out).any()  # no tokens: zero gradients
