@@ -21,7 +21,7 @@ import torch
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))  # tests/ for tiny_model
 
-from tiny_model import MuonLike, ProxyLoader, TinyLM, lora_factory, state_to_numpy, zipf_tokens  # noqa: E402
+from tiny_model import MuonLike, ProxyLoader, SmallGPT2, TinyLM, lora_factory, state_to_numpy, zipf_tokens  # noqa: E402
 
 
 def save(name: str, **arrays) -> None:
@@ -208,6 +208,29 @@ def gen_ppl(ds, ref_linear):
     save("ppl", cand=cand, **out, **{f"w/{k}": v for k, v in state_to_numpy(model).items()})
 
 
+def gen_gpt2_width(ds, ref_linear):
+    """compute_GradProd_GC_per_iter on two GPT-2-small-wide blocks at T = 1024, k = 8192, AdamW with
+    second moments 1e-4 (the GPT-2-small configuration's layer shapes; weights from the seed)."""
+    rng = np.random.default_rng(31)
+    torch.manual_seed(5)
+    model = SmallGPT2(ref_linear)
+    cand = zipf_tokens(rng, 4, 1024, 50257)
+    prox = zipf_tokens(rng, 2, 1024, 50257)
+    adam = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for p in model.parameters():
+        adam.state[p] = {"step": torch.tensor(1.0), "exp_avg": torch.zeros_like(p),
+                         "exp_avg_sq": torch.full_like(p, 1e-4)}
+    ds.initialize_projector(sketch_dim=8192, seed=42, device="cpu", enabled=True)
+    ct, pt = torch.from_numpy(cand), torch.from_numpy(prox)
+    batch_train = {"input_ids": ct, "attention_mask": torch.ones_like(ct), "labels": ct.clone()}
+    loader = ProxyLoader({"input_ids": pt, "attention_mask": torch.ones_like(pt), "labels": pt.clone()})
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device("cpu"), batch_train, loader, adam,
+                                                  ds.find_GClayers(model), preconditioner="adamw", score_len=1024,
+                                                  per_val=False, return_tracin_and_similarity=True)
+    save("wholepath_gpt2width", cand=cand, prox=prox, scores=scores, sim=sim, seed=np.array(5),
+         checksum=np.array(model.weight_checksum()))
+
+
 LORA_SCENARIOS = {"lora_proj": True, "lora_noproj": False}
 
 
@@ -316,6 +339,9 @@ def main() -> int:
     if args.only == "ppl":
         gen_ppl(ds, GCLinear)
         return 0
+    if args.only == "gpt2width":
+        gen_gpt2_width(ds, GCLinear)
+        return 0
     gen_tables(rp)
     gen_project(rp)
     gen_select(ds)
@@ -325,6 +351,7 @@ def main() -> int:
     gen_wholepath(ds, GCLinear)
     gen_wholepath_lora(ds, GCLoRALinear)
     gen_ppl(ds, GCLinear)
+    gen_gpt2_width(ds, GCLinear)
     return 0
 
 

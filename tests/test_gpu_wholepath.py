@@ -168,3 +168,29 @@ def test_chunked_token_loss_lowers_peak_memory(monkeypatch):
         peaks.append((torch.cuda.max_memory_allocated() - base) / size)
         del x
     assert peaks[1] < 1.6 and peaks[0] > peaks[1] + 1.0, peaks
+
+
+def test_gpt2_width_scores_match_reference():
+    """Two GPT-2-small-wide blocks at T = 1024, vocab 50257, k = 8192, AdamW (v = 1e-4): the
+    configuration's layer shapes, scores and similarity against the reference's."""
+    from opus_b200.layers import GCLinear
+    from tiny_model import ProxyLoader, SmallGPT2
+
+    g = load_golden("wholepath_gpt2width")
+    torch.manual_seed(int(g["seed"]))
+    model = SmallGPT2(GCLinear)
+    # the reference run's weights (float64 sums: the order follows the host CPU's vector width)
+    assert abs(model.weight_checksum() - float(g["checksum"])) <= 1e-12 * abs(float(g["checksum"]))
+    model.to(DEV)
+    adam = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for p in model.parameters():
+        adam.state[p] = {"step": torch.tensor(1.0), "exp_avg": torch.zeros_like(p),
+                         "exp_avg_sq": torch.full_like(p, 1e-4)}
+    ds.initialize_projector(sketch_dim=8192, seed=42, device="cpu", enabled=True)
+    cand, prox = torch.from_numpy(g["cand"]).to(DEV), torch.from_numpy(g["prox"]).to(DEV)
+    batch = {"input_ids": cand, "attention_mask": torch.ones_like(cand), "labels": cand.clone()}
+    loader = ProxyLoader({"input_ids": prox, "attention_mask": torch.ones_like(prox), "labels": prox.clone()})
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), batch, loader, adam,
+                                                  ds.find_GClayers(model), preconditioner="adamw", score_len=1024)
+    assert_close_scores(scores, g["scores"])
+    assert_close_scores(sim, g["sim"])

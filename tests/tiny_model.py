@@ -41,6 +41,55 @@ class TinyLM(nn.Module):
         return logits
 
 
+class SmallGPT2(nn.Module):
+    """GPT-2-small-wide blocks (d 768, 12 heads, MLP 3072, vocab 50257, T up to 1024).
+
+    Four capture layers per block (qkv, attention out, MLP in, MLP out), learned
+    positions, pre-LayerNorm, causal attention, tanh GELU, the head tied to the
+    token embedding.  Weights come from torch.manual_seed before construction,
+    so the reference run and the run under test build the same model.
+    """
+
+    def __init__(self, linear_cls, n_layer: int = 2, vocab: int = 50257, d: int = 768, n_head: int = 12,
+                 mlp: int = 3072, ctx: int = 1024):
+        super().__init__()
+        self.vocab, self.d, self.n_head = vocab, d, n_head
+        self.wte, self.wpe = nn.Embedding(vocab, d), nn.Embedding(ctx, d)
+        self.ln1 = nn.ModuleList([nn.LayerNorm(d) for _ in range(n_layer)])
+        self.ln2 = nn.ModuleList([nn.LayerNorm(d) for _ in range(n_layer)])
+        self.qkv = nn.ModuleList([linear_cls(d, 3 * d, bias=True) for _ in range(n_layer)])
+        self.proj = nn.ModuleList([linear_cls(d, d, bias=True) for _ in range(n_layer)])
+        self.fc = nn.ModuleList([linear_cls(d, mlp, bias=True) for _ in range(n_layer)])
+        self.fc_proj = nn.ModuleList([linear_cls(mlp, d, bias=True) for _ in range(n_layer)])
+        self.ln_f = nn.LayerNorm(d)
+        with torch.no_grad():
+            for m in [*self.qkv, *self.proj, *self.fc, *self.fc_proj]:
+                m.weight.normal_(0.0, 0.02)
+                m.bias.zero_()
+            self.wte.weight.normal_(0.0, 0.02)
+            self.wpe.weight.normal_(0.0, 0.01)
+
+    def forward(self, input_seq, target_seq=None, sliding_window_num_blocks=None):
+        if input_seq.ndim == 1:
+            input_seq = input_seq[None]
+        B, T = input_seq.shape
+        x = self.wte(input_seq) + self.wpe(torch.arange(T, device=input_seq.device))
+        for i in range(len(self.qkv)):
+            q, k, v = self.qkv[i](self.ln1[i](x)).split(self.d, dim=2)
+            q, k, v = (t.view(B, T, self.n_head, -1).transpose(1, 2) for t in (q, k, v))
+            att = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B, T, self.d)
+            x = x + self.proj[i](att)
+            x = x + self.fc_proj[i](F.gelu(self.fc[i](self.ln2[i](x)), approximate="tanh"))
+        logits = F.linear(self.ln_f(x), self.wte.weight)
+        if target_seq is not None:
+            return F.cross_entropy(logits.float().view(-1, self.vocab), target_seq.reshape(-1))
+        return logits
+
+    def weight_checksum(self) -> float:
+        return float(sum(p.detach().double().sum().item() + p.detach().double().abs().sum().item()
+                         for p in self.parameters()))
+
+
 def lora_factory(cls, r: int = 4, alpha: int = 8):
     """TinyLM capture-layer constructor for a LoRA linear of rank r (LoRALinear has no bias)."""
 
