@@ -231,6 +231,36 @@ def gen_gpt2_width(ds, ref_linear):
          checksum=np.array(model.weight_checksum()))
 
 
+def muon_state(model, ref_linear, seed: int):
+    """MuonLike optimizer over the capture layers' weights, momentum buffers N(0, 1e-3) from the seed."""
+    gc = [m for m in model.modules() if isinstance(m, ref_linear)]
+    muon = MuonLike([m.weight for m in gc], lr=0.02, momentum=0.95)
+    gen = torch.Generator().manual_seed(seed)
+    for m in gc:
+        muon.state[m.weight] = {"momentum_buffer": torch.randn(m.weight.shape, generator=gen) * 1e-3}
+    return muon
+
+
+def gen_gpt2m_muon(ds, ref_linear):
+    """compute_GradProd_GC_per_iter with Muon on one GPT-2-medium-wide block (d 1024, MLP 4096),
+    T = 1024, k = 32768 (the GPT-2-medium configuration's layer shapes and sketch size)."""
+    rng = np.random.default_rng(41)
+    torch.manual_seed(7)
+    model = SmallGPT2(ref_linear, n_layer=1, d=1024, n_head=16, mlp=4096)
+    cand = zipf_tokens(rng, 4, 1024, 50257)
+    prox = zipf_tokens(rng, 2, 1024, 50257)
+    muon = muon_state(model, ref_linear, 8)
+    ds.initialize_projector(sketch_dim=32768, seed=42, device="cpu", enabled=True)
+    ct, pt = torch.from_numpy(cand), torch.from_numpy(prox)
+    batch_train = {"input_ids": ct, "attention_mask": torch.ones_like(ct), "labels": ct.clone()}
+    loader = ProxyLoader({"input_ids": pt, "attention_mask": torch.ones_like(pt), "labels": pt.clone()})
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device("cpu"), batch_train, loader, muon,
+                                                  ds.find_GClayers(model), preconditioner="muon", score_len=1024,
+                                                  per_val=False, return_tracin_and_similarity=True)
+    save("wholepath_gpt2m_muon", cand=cand, prox=prox, scores=scores, sim=sim, seed=np.array(7),
+         momentum_seed=np.array(8), checksum=np.array(model.weight_checksum()))
+
+
 LORA_SCENARIOS = {"lora_proj": True, "lora_noproj": False}
 
 
@@ -341,6 +371,7 @@ def main() -> int:
         return 0
     if args.only == "gpt2width":
         gen_gpt2_width(ds, GCLinear)
+        gen_gpt2m_muon(ds, GCLinear)
         return 0
     gen_tables(rp)
     gen_project(rp)
@@ -352,6 +383,7 @@ def main() -> int:
     gen_wholepath_lora(ds, GCLoRALinear)
     gen_ppl(ds, GCLinear)
     gen_gpt2_width(ds, GCLinear)
+    gen_gpt2m_muon(ds, GCLinear)
     return 0
 
 

@@ -194,3 +194,30 @@ def test_gpt2_width_scores_match_reference():
                                                   ds.find_GClayers(model), preconditioner="adamw", score_len=1024)
     assert_close_scores(scores, g["scores"])
     assert_close_scores(sim, g["sim"])
+
+
+def test_gpt2m_muon_scores_match_reference():
+    """One GPT-2-medium-wide block (d 1024, MLP 4096) at T = 1024, k = 32768, Muon momentum
+    buffers from a seed: the Muon configuration's layer shapes against the reference."""
+    from opus_b200.layers import GCLinear
+    from tiny_model import MuonLike, ProxyLoader, SmallGPT2
+
+    g = load_golden("wholepath_gpt2m_muon")
+    torch.manual_seed(int(g["seed"]))
+    model = SmallGPT2(GCLinear, n_layer=1, d=1024, n_head=16, mlp=4096)
+    assert abs(model.weight_checksum() - float(g["checksum"])) <= 1e-12 * abs(float(g["checksum"]))
+    gc = [m for m in model.modules() if isinstance(m, GCLinear)]
+    muon = MuonLike([m.weight for m in gc], lr=0.02, momentum=0.95)
+    gen = torch.Generator().manual_seed(int(g["momentum_seed"]))
+    buffers = [torch.randn(m.weight.shape, generator=gen) * 1e-3 for m in gc]
+    model.to(DEV)
+    for m, buf in zip(gc, buffers):
+        muon.state[m.weight] = {"momentum_buffer": buf.to(DEV)}
+    ds.initialize_projector(sketch_dim=32768, seed=42, device="cpu", enabled=True)
+    cand, prox = torch.from_numpy(g["cand"]).to(DEV), torch.from_numpy(g["prox"]).to(DEV)
+    batch = {"input_ids": cand, "attention_mask": torch.ones_like(cand), "labels": cand.clone()}
+    loader = ProxyLoader({"input_ids": prox, "attention_mask": torch.ones_like(prox), "labels": prox.clone()})
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), batch, loader, muon,
+                                                  ds.find_GClayers(model), preconditioner="muon", score_len=1024)
+    assert_close_scores(scores, g["scores"])
+    assert_close_scores(sim, g["sim"])
