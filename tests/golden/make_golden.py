@@ -21,7 +21,8 @@ import torch
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))  # tests/ for tiny_model
 
-from tiny_model import MuonLike, ProxyLoader, SmallGPT2, TinyLM, lora_factory, state_to_numpy, zipf_tokens  # noqa: E402
+from tiny_model import (MuonLike, ProxyLoader, SmallGPT2, SmallQwen3, TinyLM, lora_factory,  # noqa: E402
+                        state_to_numpy, zipf_tokens)
 
 
 def save(name: str, **arrays) -> None:
@@ -261,6 +262,49 @@ def gen_gpt2m_muon(ds, ref_linear):
          momentum_seed=np.array(8), checksum=np.array(model.weight_checksum()))
 
 
+def gen_gpt2xl_adamw(ds, ref_linear):
+    """One GPT-2-XL-wide block (d 1600, MLP 6400), T = 1024, k = 65536, AdamW (v = 1e-4): the
+    GPT-2-XL configuration's layer shapes and sketch size."""
+    rng = np.random.default_rng(51)
+    torch.manual_seed(9)
+    model = SmallGPT2(ref_linear, n_layer=1, d=1600, n_head=25, mlp=6400)
+    cand = zipf_tokens(rng, 4, 1024, 50257)
+    prox = zipf_tokens(rng, 2, 1024, 50257)
+    adam = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for p in model.parameters():
+        adam.state[p] = {"step": torch.tensor(1.0), "exp_avg": torch.zeros_like(p),
+                         "exp_avg_sq": torch.full_like(p, 1e-4)}
+    ds.initialize_projector(sketch_dim=65536, seed=42, device="cpu", enabled=True)
+    ct, pt = torch.from_numpy(cand), torch.from_numpy(prox)
+    batch_train = {"input_ids": ct, "attention_mask": torch.ones_like(ct), "labels": ct.clone()}
+    loader = ProxyLoader({"input_ids": pt, "attention_mask": torch.ones_like(pt), "labels": pt.clone()})
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device("cpu"), batch_train, loader, adam,
+                                                  ds.find_GClayers(model), preconditioner="adamw", score_len=1024,
+                                                  per_val=False, return_tracin_and_similarity=True)
+    save("wholepath_gpt2xl_adamw", cand=cand, prox=prox, scores=scores, sim=sim, seed=np.array(9),
+         checksum=np.array(model.weight_checksum()))
+
+
+def gen_qwen3_muon(ds, ref_linear):
+    """One Qwen3-style block (d 2048, GQA 16/8 heads of 128, SwiGLU 6144), T = 4096, vocab 151936,
+    k = 131072, Muon momentum buffers from a seed: the Qwen3 configuration's shapes."""
+    rng = np.random.default_rng(61)
+    torch.manual_seed(11)
+    model = SmallQwen3(ref_linear)
+    cand = zipf_tokens(rng, 2, 4096, 151936)
+    prox = zipf_tokens(rng, 1, 4096, 151936)
+    muon = muon_state(model, ref_linear, 12)
+    ds.initialize_projector(sketch_dim=131072, seed=42, device="cpu", enabled=True)
+    ct, pt = torch.from_numpy(cand), torch.from_numpy(prox)
+    batch_train = {"input_ids": ct, "attention_mask": torch.ones_like(ct), "labels": ct.clone()}
+    loader = ProxyLoader({"input_ids": pt, "attention_mask": torch.ones_like(pt), "labels": pt.clone()})
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device("cpu"), batch_train, loader, muon,
+                                                  ds.find_GClayers(model), preconditioner="muon", score_len=4096,
+                                                  per_val=False, return_tracin_and_similarity=True)
+    save("wholepath_qwen3_muon", cand=cand, prox=prox, scores=scores, sim=sim, seed=np.array(11),
+         momentum_seed=np.array(12), checksum=np.array(model.weight_checksum()))
+
+
 LORA_SCENARIOS = {"lora_proj": True, "lora_noproj": False}
 
 
@@ -373,6 +417,12 @@ def main() -> int:
         gen_gpt2_width(ds, GCLinear)
         gen_gpt2m_muon(ds, GCLinear)
         return 0
+    if args.only == "gpt2xl":
+        gen_gpt2xl_adamw(ds, GCLinear)
+        return 0
+    if args.only == "qwen3":
+        gen_qwen3_muon(ds, GCLinear)
+        return 0
     gen_tables(rp)
     gen_project(rp)
     gen_select(ds)
@@ -384,6 +434,8 @@ def main() -> int:
     gen_ppl(ds, GCLinear)
     gen_gpt2_width(ds, GCLinear)
     gen_gpt2m_muon(ds, GCLinear)
+    gen_gpt2xl_adamw(ds, GCLinear)
+    gen_qwen3_muon(ds, GCLinear)
     return 0
 
 

@@ -221,3 +221,64 @@ def test_gpt2m_muon_scores_match_reference():
                                                   ds.find_GClayers(model), preconditioner="muon", score_len=1024)
     assert_close_scores(scores, g["scores"])
     assert_close_scores(sim, g["sim"])
+
+
+def _muon_for(model, seed):
+    from opus_b200.layers import GCLinear
+    from tiny_model import MuonLike
+
+    gc = [m for m in model.modules() if isinstance(m, GCLinear)]
+    muon = MuonLike([m.weight for m in gc], lr=0.02, momentum=0.95)
+    gen = torch.Generator().manual_seed(seed)
+    buffers = [torch.randn(m.weight.shape, generator=gen) * 1e-3 for m in gc]
+    return muon, list(zip(gc, buffers))
+
+
+def _scores_on_gpu(model, g, opt, precond, k, score_len):
+    from tiny_model import ProxyLoader
+
+    ds.initialize_projector(sketch_dim=k, seed=42, device="cpu", enabled=True)
+    cand, prox = torch.from_numpy(g["cand"]).to(DEV), torch.from_numpy(g["prox"]).to(DEV)
+    batch = {"input_ids": cand, "attention_mask": torch.ones_like(cand), "labels": cand.clone()}
+    loader = ProxyLoader({"input_ids": prox, "attention_mask": torch.ones_like(prox), "labels": prox.clone()})
+    return ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), batch, loader, opt, ds.find_GClayers(model),
+                                           preconditioner=precond, score_len=score_len)
+
+
+def test_gpt2xl_adamw_scores_match_reference():
+    """One GPT-2-XL-wide block (d 1600, MLP 6400), T = 1024, k = 65536 (a shared-memory sketch of
+    the first 32768 buckets, L2 atomics above), AdamW: against the reference."""
+    from opus_b200.layers import GCLinear
+    from tiny_model import SmallGPT2
+
+    g = load_golden("wholepath_gpt2xl_adamw")
+    torch.manual_seed(int(g["seed"]))
+    model = SmallGPT2(GCLinear, n_layer=1, d=1600, n_head=25, mlp=6400)
+    assert abs(model.weight_checksum() - float(g["checksum"])) <= 1e-12 * abs(float(g["checksum"]))
+    model.to(DEV)
+    adam = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for p in model.parameters():
+        adam.state[p] = {"step": torch.tensor(1.0), "exp_avg": torch.zeros_like(p),
+                         "exp_avg_sq": torch.full_like(p, 1e-4)}
+    scores, sim = _scores_on_gpu(model, g, adam, "adamw", 65536, 1024)
+    assert_close_scores(scores, g["scores"])
+    assert_close_scores(sim, g["sim"])
+
+
+def test_qwen3_muon_scores_match_reference():
+    """One Qwen3-style block (d 2048, GQA 16/8 x 128, SwiGLU 6144, 7 capture layers), T = 4096,
+    vocab 151936, k = 131072, Muon: the Qwen3 configuration's shapes against the reference."""
+    from opus_b200.layers import GCLinear
+    from tiny_model import SmallQwen3
+
+    g = load_golden("wholepath_qwen3_muon")
+    torch.manual_seed(int(g["seed"]))
+    model = SmallQwen3(GCLinear)
+    assert abs(model.weight_checksum() - float(g["checksum"])) <= 1e-12 * abs(float(g["checksum"]))
+    muon, buffers = _muon_for(model, int(g["momentum_seed"]))
+    model.to(DEV)
+    for m, buf in buffers:
+        muon.state[m.weight] = {"momentum_buffer": buf.to(DEV)}
+    scores, sim = _scores_on_gpu(model, g, muon, "muon", 131072, 4096)
+    assert_close_scores(scores, g["scores"])
+    assert_close_scores(sim, g["sim"])

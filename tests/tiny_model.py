@@ -90,6 +90,63 @@ class SmallGPT2(nn.Module):
                          for p in self.parameters()))
 
 
+class SmallQwen3(nn.Module):
+    """Qwen3-style blocks: RMSNorm, grouped-query attention with per-head q/k RMSNorm and
+    RoPE, SwiGLU MLP; seven capture layers per block (q, k, v, o, gate, up, down), the head
+    tied to the token embedding.  Weights come from torch.manual_seed before construction.
+    """
+
+    def __init__(self, linear_cls, n_layer: int = 1, vocab: int = 151936, d: int = 2048, n_head: int = 16,
+                 n_kv: int = 8, head_dim: int = 128, mlp: int = 6144, theta: float = 1e6):
+        super().__init__()
+        self.vocab, self.d, self.n_head, self.n_kv, self.head_dim, self.theta = vocab, d, n_head, n_kv, head_dim, theta
+        self.embed = nn.Embedding(vocab, d)
+        mk = lambda i, o: nn.ModuleList([linear_cls(i, o, bias=False) for _ in range(n_layer)])  # noqa: E731
+        self.q, self.k, self.v = mk(d, n_head * head_dim), mk(d, n_kv * head_dim), mk(d, n_kv * head_dim)
+        self.o = mk(n_head * head_dim, d)
+        self.gate, self.up, self.down = mk(d, mlp), mk(d, mlp), mk(mlp, d)
+        with torch.no_grad():
+            for m in [*self.q, *self.k, *self.v, *self.o, *self.gate, *self.up, *self.down]:
+                m.weight.normal_(0.0, 0.02)
+            self.embed.weight.normal_(0.0, 0.02)
+
+    def _rope(self, x):
+        T, hd = x.shape[1], self.head_dim
+        inv = self.theta ** (-torch.arange(0, hd, 2, device=x.device, dtype=torch.float32) / hd)
+        ang = torch.arange(T, device=x.device, dtype=torch.float32)[:, None] * inv[None, :]
+        cos, sin = torch.cos(ang).repeat(1, 2)[None, :, None, :], torch.sin(ang).repeat(1, 2)[None, :, None, :]
+        x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
+        return x * cos.to(x.dtype) + torch.cat([-x2, x1], dim=-1) * sin.to(x.dtype)
+
+    def forward(self, input_seq, target_seq=None, sliding_window_num_blocks=None):
+        if input_seq.ndim == 1:
+            input_seq = input_seq[None]
+        B, T = input_seq.shape
+        x = self.embed(input_seq)
+        hd = self.head_dim
+        for i in range(len(self.q)):
+            h = F.rms_norm(x, (self.d,))
+            q = F.rms_norm(self.q[i](h).view(B, T, self.n_head, hd), (hd,))
+            k = F.rms_norm(self.k[i](h).view(B, T, self.n_kv, hd), (hd,))
+            v = self.v[i](h).view(B, T, self.n_kv, hd)
+            q, k = self._rope(q), self._rope(k)
+            rep = self.n_head // self.n_kv
+            k, v = k.repeat_interleave(rep, dim=2), v.repeat_interleave(rep, dim=2)
+            att = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                                 is_causal=True)
+            x = x + self.o[i](att.transpose(1, 2).reshape(B, T, self.n_head * hd))
+            h = F.rms_norm(x, (self.d,))
+            x = x + self.down[i](F.silu(self.gate[i](h)) * self.up[i](h))
+        logits = F.linear(F.rms_norm(x, (self.d,)), self.embed.weight)
+        if target_seq is not None:
+            return F.cross_entropy(logits.float().view(-1, self.vocab), target_seq.reshape(-1))
+        return logits
+
+    def weight_checksum(self) -> float:
+        return float(sum(p.detach().double().sum().item() + p.detach().double().abs().sum().item()
+                         for p in self.parameters()))
+
+
 def lora_factory(cls, r: int = 4, alpha: int = 8):
     """TinyLM capture-layer constructor for a LoRA linear of rank r (LoRALinear has no bias)."""
 
