@@ -569,22 +569,25 @@ def _score_and_similarity(model, device, batch_train, validation_loader, optimiz
     return score, sim
 
 
-def _score_and_similarity_stream(model, device, batch_train, batch_val, optimizer, trainable_layers,
-                                 preconditioner, score_len, per_val, with_similarity):
-    """Streaming capture: each layer is scored from a backward hook on its Z.
+def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_layers, preconditioner, score_len,
+                   make_handler):
+    """Capture forward, then one backward whose per-layer hooks hand each (dL/dZ, A) pair to a handler.
 
     The backward pass is asked only for the gradient of the first kept
     layer's input, which every captured Z feeds, so autograd frees each dL/dZ
-    once its hook has sketched it.  Pair ids follow the forward order, as in
-    the batch capture.  Returns None, after clearing its partial sums, when a
-    layer's hook did not fire (a captured output the loss does not reach, or
-    no usable root); the caller then falls back to the batch capture.
+    once its hook has used it and no layer's gradient outlives its hook.
+    make_handler(train_bs, val_bs, n_plans) is called once after the forward
+    and returns on_plan(LayerPlan); plans arrive in backward order and carry
+    their pair id, which follows the forward order as in the batch capture.
+    Returns False when a layer's hook did not fire (a captured output the
+    loss does not reach, or no usable root): the caller then falls back to the
+    batch capture.
     """
     loss, layers_kept, z_list, train_bs, val_bs = _capture_forward(
         model, dict(batch_train), None, trainable_layers, score_len, batch_val)
     root = getattr(layers_kept[0], "layer_input", None)
     if not (isinstance(root, torch.Tensor) and root.requires_grad):
-        return None
+        return False
     params = []
     pid_base = []
     for layer in layers_kept:
@@ -592,9 +595,7 @@ def _score_and_similarity_stream(model, device, batch_train, batch_val, optimize
         names = ("lora_A", "lora_B") if _pairs_per_layer(layer) == 2 else ()
         params.extend([getattr(layer, n) for n in names] or [getattr(layer, "weight", None)])
     tables = _PrecondTables(params, optimizer, preconditioner)
-    projector = get_projector()
-    score = torch.zeros((train_bs, val_bs) if per_val else (train_bs,), device=device, dtype=torch.float32)
-    sim = torch.zeros((train_bs, train_bs), device=device, dtype=torch.float32) if with_similarity else None
+    on_plan = make_handler(train_bs, val_bs, len(params))
     fired = [False] * len(layers_kept)
     bad = []
 
@@ -606,7 +607,7 @@ def _score_and_similarity_stream(model, device, batch_train, batch_val, optimize
                     bad.append(li)
                     return None
                 for i, pr in enumerate(pairs):
-                    _score_plan(tables.plan(pid_base[li] + i, pr, device), projector, score, sim, val_bs, per_val)
+                    on_plan(tables.plan(pid_base[li] + i, pr, device))
                 fired[li] = True
             except Exception as exc:  # surfaced after backward: an exception inside autograd loses context
                 bad.append(exc)
@@ -622,9 +623,29 @@ def _score_and_similarity_stream(model, device, batch_train, batch_val, optimize
     for b in bad:
         if isinstance(b, Exception):
             raise b
-    if bad or not all(fired):
+    return not bad and all(fired)
+
+
+def _score_and_similarity_stream(model, device, batch_train, batch_val, optimizer, trainable_layers,
+                                 preconditioner, score_len, per_val, with_similarity):
+    """Streaming capture: each layer is scored from a backward hook on its Z (stream_capture).
+
+    Returns None when a hook did not fire; the caller then falls back to the
+    batch capture with fresh sums.
+    """
+    projector = get_projector()
+    out = {}
+
+    def make_handler(train_bs, val_bs, n_plans):
+        score = torch.zeros((train_bs, val_bs) if per_val else (train_bs,), device=device, dtype=torch.float32)
+        sim = torch.zeros((train_bs, train_bs), device=device, dtype=torch.float32) if with_similarity else None
+        out["score"], out["sim"] = score, sim
+        return lambda pl: _score_plan(pl, projector, score, sim, val_bs, per_val)
+
+    if not stream_capture(model, device, batch_train, batch_val, optimizer, trainable_layers, preconditioner,
+                          score_len, make_handler):
         return None
-    return score, sim
+    return out["score"], out["sim"]
 
 
 def ops_inv_rms(v: torch.Tensor, eps: float) -> torch.Tensor:

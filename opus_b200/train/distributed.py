@@ -256,39 +256,65 @@ def score_shard(model, device, batch_train, proxy_share, n_proxy_total, optimize
     [B_loc, W*B_loc] against every rank's candidates (one all-gather of the
     sketches per layer).  Needs the CountSketch projector
     (initialize_projector(enabled=True)).
+
+    With the streaming capture (the default) each layer is sketched from a
+    backward hook, as in the single-process path, so no layer's dL/dZ
+    outlives its hook; only the candidate sketches [B_loc, k] of every layer
+    are kept until the one all-reduce of the target sketches after the
+    backward.  The batch capture (one autograd call over every layer) is the
+    fallback when a hook cannot fire.
     """
     projector = ds.get_projector()
     if projector is None or not projector.enabled:
         raise ValueError("sharded selection needs the CountSketch projector (initialize_projector(enabled=True))")
-    pairs, train_bs, _ = ds.capture_pairs(model, batch_train, None, trainable_layers, score_len,
-                                          batch_val=proxy_share)
-    plans = ds.plan_layers(pairs, optimizer, preconditioner, device)
-    del pairs
+    _, world = rank_and_world(group)
 
     def shaped(pl):
         if pl.g_t.dim() == 2:
             return pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1), pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)
         return pl.g_t, pl.a_t, pl.g_v, pl.a_v
 
-    taus = torch.zeros(len(plans), projector.sketch_dim, device=device, dtype=torch.float32)
-    for li, pl in enumerate(plans):
-        _, _, g_v, a_v = shaped(pl)
-        if g_v.shape[0] > 0:
-            projector.sketch(g_v, a_v, pl.pid, rows_div=g_v.shape[0], out=taus[li:li + 1], accumulate=True)
-    allreduce_target_sketches(taus, group)
+    state = {}
 
-    _, world = rank_and_world(group)
+    def make_handler(train_bs, val_bs, n_plans):
+        taus = torch.zeros(n_plans, projector.sketch_dim, device=device, dtype=torch.float32)
+        sim = torch.zeros(train_bs, train_bs * world if exact_similarity else train_bs, device=device,
+                          dtype=torch.float32)
+        state.update(train_bs=train_bs, taus=taus, sim=sim, phis=[None] * n_plans, cs=[0.0] * n_plans)
+
+        def on_plan(pl):
+            g_t, a_t, g_v, a_v = shaped(pl)
+            if g_v.shape[0] > 0:
+                projector.sketch(g_v, a_v, pl.pid, rows_div=g_v.shape[0], out=taus[pl.pid:pl.pid + 1],
+                                 accumulate=True)
+            phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
+            state["phis"][pl.pid], state["cs"][pl.pid] = phi_t, pl.c
+            if not exact_similarity:
+                ops.sketch_gram(phi_t, alpha=pl.c * pl.c, out=sim, accumulate=True)
+        return on_plan
+
+    streamed = ds.CAPTURE_MODE == "stream" and ds.stream_capture(
+        model, device, batch_train, proxy_share, optimizer, trainable_layers, preconditioner, score_len,
+        make_handler)
+    if not streamed:
+        state.clear()
+        pairs, train_bs, _ = ds.capture_pairs(model, batch_train, None, trainable_layers, score_len,
+                                              batch_val=proxy_share)
+        plans = ds.plan_layers(pairs, optimizer, preconditioner, device)
+        del pairs
+        on_plan = make_handler(train_bs, None, len(plans))
+        for pl in plans:
+            on_plan(pl)
+        del plans
+    taus, sim, phis, cs, train_bs = state["taus"], state["sim"], state["phis"], state["cs"], state["train_bs"]
+    allreduce_target_sketches(taus, group)
     score = torch.zeros(train_bs, device=device, dtype=torch.float32)
-    cols = train_bs * world if exact_similarity else train_bs
-    sim = torch.zeros(train_bs, cols, device=device, dtype=torch.float32)
-    for li, pl in enumerate(plans):
-        g_t, a_t, _, _ = shaped(pl)
-        phi_t = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps)
+    for pid, phi_t in enumerate(phis):  # the pair ids' forward order, on every rank
         if n_proxy_total > 0:
-            ops.sketch_dot(phi_t, taus[li], alpha=pl.c / n_proxy_total, out=score, accumulate=True)
-        other = gather_sketches(phi_t, group) if exact_similarity else phi_t
-        ops.sketch_gram(phi_t, other, alpha=pl.c * pl.c, out=sim, accumulate=True)
-        del phi_t, other
+            ops.sketch_dot(phi_t, taus[pid], alpha=cs[pid] / n_proxy_total, out=score, accumulate=True)
+        if exact_similarity:
+            ops.sketch_gram(phi_t, gather_sketches(phi_t, group), alpha=cs[pid] * cs[pid], out=sim, accumulate=True)
+        phis[pid] = None
     return score, sim
 
 

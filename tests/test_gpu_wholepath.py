@@ -282,3 +282,25 @@ def test_qwen3_muon_scores_match_reference():
     scores, sim = _scores_on_gpu(model, g, muon, "muon", 131072, 4096)
     assert_close_scores(scores, g["scores"])
     assert_close_scores(sim, g["sim"])
+
+
+@pytest.mark.parametrize("name", ["adamw_proj", "muon_proj", "lora_proj"])
+@pytest.mark.parametrize("exact", [False, True])
+def test_score_shard_streams_like_batch_capture(name, exact, monkeypatch):
+    """The sharded scorer at world size 1: streaming hooks == one autograd call == the reference."""
+    from opus_b200.train import distributed as sd
+
+    g = load_golden(f"wholepath_{name}")
+    model, opt, loader, batch = (rebuild_lora if name.startswith("lora") else rebuild)(g, device=DEV)
+    ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    proxy = loader._fixed_batch
+    n = proxy["input_ids"].shape[0]
+    out = {}
+    for mode in ("stream", "batch"):
+        monkeypatch.setattr(ds, "CAPTURE_MODE", mode)
+        out[mode] = sd.score_shard(model, torch.device(DEV), dict(batch), dict(proxy), n, opt,
+                                   ds.find_GClayers(model), preconditioner=str(g["precond"]), score_len=128,
+                                   exact_similarity=exact)
+    for mode in ("stream", "batch"):
+        assert_close_scores(out[mode][0].cpu().numpy(), g["scores"])
+        assert_close_scores(out[mode][1].cpu().numpy(), g["sim"])
