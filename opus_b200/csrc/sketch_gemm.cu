@@ -141,6 +141,7 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
 
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
+                       const __grid_constant__ CUtensorMap tm_out,
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
                        int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
                        int cap_log2, int* err, int dense, const float* __restrict__ dense_diag, int d_out,
@@ -284,17 +285,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (dense) {
     // ------------------------------------------------- dense epilogue
     // Per-sample gradients: element (o, c) of G_b, times dense_diag[o, c]
-    // when given, goes to phi[b, o * d_in + c].  Every element has exactly
-    // one writer, so 16-byte streaming stores (vector reductions when
-    // accumulating) replace the scatter; each thread writes 128 contiguous
-    // bytes of its row per chunk.
+    // when given, goes to phi[b, o * d_in + c].  Each warp stages its 32 rows
+    // x 32 columns of a chunk in shared memory, in the 128-byte-swizzled
+    // layout of the output tensor map (row r's 16-byte piece u sits at
+    // u ^ (r & 7): conflict-free writes), and one lane stores the box with
+    // TMA (a reduce-add when accumulating), so every global write is a full
+    // 128-byte line.  Two staging buffers per warp: a buffer is rewritten
+    // only after the store issued from it two chunks earlier has been read.
+    // Rows past d_out and columns past d_in fall outside the tensor map and
+    // are not written.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int r = q * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint64_t diag_policy = l2_policy_evict_last();  // every candidate re-reads the diagonal
-    const int64_t numel = (int64_t)d_out * d_in;
-    const bool vec = ((reinterpret_cast<uintptr_t>(phi) | reinterpret_cast<uintptr_t>(dense_diag)) & 15) == 0;
+    float* staging = reinterpret_cast<float*>(sk) + (size_t)(warp - 2) * 2 * kChunkCols * 32;
+    int buf = 0;
     int acc = 0;
     uint32_t aph = 0;
     bool ok = true;
@@ -302,59 +307,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
     for (int cb = 0; cb < n_cb && ok; ++cb) {
       const int b = static_cast<int>(job / groups);
+      const int row0 = ob * kTileM + q * 32;  // first row of this warp's block
+      // the diagonal of a chunk is loaded one chunk ahead (the first one before the accumulator
+      // wait), so its L2 latency hides behind the previous chunk's staging and store
+      // The diagonal of the warp's 32 x 32 block of a chunk, read coalesced: load u of lane l
+      // is row 4u + l / 8, columns 4 (l % 8) .. +3, so one warp load covers four whole 128-byte
+      // rows.  It goes through the staging buffer to reach the thread that owns its row.  A
+      // chunk's block is loaded two chunks ahead (the first two before the accumulator wait).
+      float4 w_ring[3][kChunkCols / 4];
+      auto load_diag = [&](float4(&w)[kChunkCols / 4], int jj) {
+        const int c = cb * kTileN + (half * kChunksPerWarp + jj) * kChunkCols + (lane & 7) * 4;
+#pragma unroll
+        for (int u = 0; u < kChunkCols / 4; ++u) {  // d_in % 8 == 0: a piece is all in or all out
+          const int orow = row0 + 4 * u + (lane >> 3);
+          w[u] = (dense_diag != nullptr && orow < d_out && c < d_in)
+                     ? ld_f4_hint(dense_diag + (int64_t)orow * d_in + c, diag_policy)
+                     : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        }
+      };
+      load_diag(w_ring[0], 0);
+      load_diag(w_ring[1], 1);
       if (!mbar_wait(&tfull[acc], aph, abort_flag, err, kDevTimeoutEpilogue)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int o = ob * kTileM + r;
-      const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
-#pragma unroll 1
+#pragma unroll
       for (int jj = 0; jj < kChunksPerWarp; ++jj) {
         const int j = half * kChunksPerWarp + jj;
         const int c0 = cb * kTileN + j * kChunkCols;
+        if (jj + 2 < kChunksPerWarp) load_diag(w_ring[(jj + 2) % 3], jj + 2);
+        const float4* w_cur = w_ring[jj % 3];
         uint32_t v[32];
-        tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
+        tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTileN) + j * kChunkCols, v);
         tmem_ld_wait();
         if (jj == kChunksPerWarp - 1) {
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
-        if (o >= d_out || c0 >= d_in) continue;
-        float* dst = phi + (int64_t)b * numel + (int64_t)o * d_in + c0;
-        const float* drow = dense_diag != nullptr ? dense_diag + (int64_t)o * d_in + c0 : nullptr;
-        if (vec && c0 + kChunkCols <= d_in) {
+        if (row0 >= d_out || c0 >= d_in) continue;  // the whole block lies outside the output
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        float* sbuf = staging + buf * (kChunkCols * 32);
+        float4* srow = reinterpret_cast<float4*>(sbuf + lane * kChunkCols);  // this thread's row
+        if (dense_diag != nullptr) {
+          // the diagonal block into the buffer (row 4u + lane / 8 per load), then back out by row
 #pragma unroll
           for (int u = 0; u < kChunkCols / 4; ++u) {
-            float4 w = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-            if (drow != nullptr) w = ld_f4_hint(drow + 4 * u, diag_policy);
-            float4 x;
-            x.x = drow != nullptr ? __uint_as_float(v[4 * u]) * w.x : __uint_as_float(v[4 * u]);
-            x.y = drow != nullptr ? __uint_as_float(v[4 * u + 1]) * w.y : __uint_as_float(v[4 * u + 1]);
-            x.z = drow != nullptr ? __uint_as_float(v[4 * u + 2]) * w.z : __uint_as_float(v[4 * u + 2]);
-            x.w = drow != nullptr ? __uint_as_float(v[4 * u + 3]) * w.w : __uint_as_float(v[4 * u + 3]);
-            if (accumulate)
-              red_add_v4(dst + 4 * u, x.x, x.y, x.z, x.w);
-            else
-              __stcs(reinterpret_cast<float4*>(dst + 4 * u), x);
+            const int rr = 4 * u + (lane >> 3);
+            reinterpret_cast<float4*>(sbuf + rr * kChunkCols)[(lane & 7) ^ (rr & 7)] = w_cur[u];
           }
-        } else {
-#pragma unroll
-          for (int u = 0; u < kChunkCols; ++u) {
-            if (c0 + u >= d_in) break;
-            const float x = drow != nullptr ? __uint_as_float(v[u]) * drow[u] : __uint_as_float(v[u]);
-            if (accumulate)
-              atomicAdd(dst + u, x);
-            else
-              dst[u] = x;
-          }
+          __syncwarp();
         }
+#pragma unroll
+        for (int u = 0; u < kChunkCols / 4; ++u) {
+          float4 x = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                                 __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+          if (dense_diag != nullptr) {  // out-of-range pieces carry weight 1 and are clipped by the store
+            const float4 w = srow[u ^ (lane & 7)];
+            x.x *= w.x;
+            x.y *= w.y;
+            x.z *= w.z;
+            x.w *= w.w;
+          }
+          srow[u ^ (lane & 7)] = x;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (accumulate)
+            tma_reduce_add_3d(&tm_out, sbuf, c0, row0, b);
+          else
+            tma_store_3d(&tm_out, sbuf, c0, row0, b);
+          bulk_commit_group();
+        }
+        buf ^= 1;
       }
       if (++acc == 2) {
         acc = 0;
         aph ^= 1;
       }
     }
+    if (lane == 0) bulk_wait_group<0>();  // every store has landed before the CTA exits
   } else {
     // ------------------------------------------------------------ epilogue
     const int et = threadIdx.x - 64;          // 0..255
@@ -619,8 +653,9 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   const JobPlan jp = plan_jobs(n_rows, n_ob);
   int* err = device_error_word();
   sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
-      tm_g, tm_a, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_ob, n_cb, jp.groups, k, rows_div,
-      plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in, accumulate);
+      tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_ob, n_cb,
+      jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
+      accumulate);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -647,16 +682,29 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
   }
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a)) return rc;
-  const SmemPlan plan = plan_smem(0);  // no sketch: all of shared memory for pipeline stages
-  if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
+  // the output as [n_rows][d_out][d_in] f32, 32 x 32 boxes, 128-byte swizzle
+  CUtensorMap tm_out;
+  {
+    const uint64_t dims[3] = {(uint64_t)d_in, (uint64_t)d_out, (uint64_t)n_rows};
+    const uint64_t strides[2] = {(uint64_t)d_in * 4, (uint64_t)numel * 4};
+    const uint32_t box[3] = {kChunkCols, 32, 1};
+    if (int rc = encode_tmap(&tm_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  // the epilogue's staging (two 32 x 32 f32 boxes per epilogue warp) takes the place of the sketch
+  constexpr int64_t kStagingWords = (int64_t)kEpiWarps * 2 * kChunkCols * 32;
+  const SmemPlan plan = plan_smem(kStagingWords);
+  if (plan.stages == 0 || plan.k_sm < kStagingWords)
+    return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
   OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
   const JobPlan jp = plan_jobs(n_rows, n_ob);
   int* err = device_error_word();
-  sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, nullptr, out, n_rows, seq_len, n_ob, n_cb,
-                                                            jp.groups, numel, 1, plan.stages, 0, 0.0f, 0, err,
-                                                            /*dense*/ 1, diag, d_out, d_in, accumulate);
+  sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_ob,
+                                                            n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
+                                                            err, /*dense*/ 1, diag, d_out, d_in, accumulate);
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
