@@ -71,9 +71,10 @@ def parse_args():
                          "mode scores everything on one rank)")
     ap.add_argument("--model-dtype", default="f32", choices=["f32", "bf16"],
                     help="gpt2-small: parameter and activation dtype (f32 as in the GPT-2-small config)")
-    ap.add_argument("--path", default="sketch", choices=["sketch", "ghost"],
+    ap.add_argument("--path", default="sketch", choices=["sketch", "ghost", "noproj-sim"],
                     help="sketch: the selection step (default line); ghost: exact scores through the ghost "
-                         "contraction against the de-sketched AdamW target (stage 2 on its own, one GPU)")
+                         "contraction against the de-sketched AdamW target (stage 2 on its own, one GPU); "
+                         "noproj-sim: the projection-off similarity (exact per-sample gradients + Gram, one GPU)")
     args = ap.parse_args()
     return args
 
@@ -380,6 +381,71 @@ def run_ghost(args):
     return 0
 
 
+def run_noproj_sim(args):
+    """The projection-off similarity on its own, one GPU.
+
+    Per step: the exact per-sample gradients D o (dLdZ_b^T a_b) of every
+    candidate (opus_per_sample_grad: the tensor-core GEMM with a dense,
+    TMA-stored epilogue) and their Gram matrix (3xTF32 tensor cores) -- the
+    similarity of the reference's projection-off mode (data_selection.py:
+    255-292, 597-619).
+    """
+    import torch
+
+    from opus_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nb = args.batch
+    a, dz, _, diag = make_inputs(dev, 0, nb)
+    grads = torch.empty(nb, D_OUT * D_IN, device=dev)
+    sim = torch.empty(nb, nb, device=dev)
+    ev = {"s": [], "e": []}
+
+    def step(time_kernel=False):
+        if time_kernel:
+            ev["s"].append(torch.cuda.Event(enable_timing=True))
+            ev["e"].append(torch.cuda.Event(enable_timing=True))
+            ev["s"][-1].record()
+        ops.per_sample_grad(dz, a, diag=diag, out=grads)
+        if time_kernel:
+            ev["e"][-1].record()
+        ops.sketch_gram(grads, out=sim)
+        return sim
+
+    for _ in range(args.warmup):
+        step()
+    ops.check_device_error("noproj-sim warm-up")
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(time_kernel=True)
+        end.record()
+        torch.cuda.synchronize()
+    ops.check_device_error("noproj-sim timed region")
+    ms_per_step = start.elapsed_time(end) / args.steps
+    kern_ms = sum(x.elapsed_time(y) for x, y in zip(ev["s"], ev["e"])) / args.steps
+    burst, sustained, hbm, src = measured_peaks()
+    flops = 2.0 * nb * T * D_OUT * D_IN
+    achieved = flops / (kern_ms * 1e-3) / 1e12
+    line = {"metric": "candidate seqs with exact similarity/sec (projection off)",
+            "value": round(nb / (ms_per_step / 1e3), 3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD if nb == B else WORKLOAD.replace("256 seqs", f"{nb} seqs"),
+                       "path": "exact per-sample gradients (dense epilogue) -> 3xTF32 Gram"},
+            "roofline": {"bound": "tensor", "kernel": "per_sample_grad", "achieved": round(achieved, 2),
+                         "peak": sustained, "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
+                         "peak_kind": f"bf16 sustained ({src})", "kernel_ms": round(kern_ms, 4),
+                         "flops_per_launch": flops,
+                         "bytes_written_per_launch": 4.0 * nb * D_OUT * D_IN, "traffic": None},
+            "clocks": clk.summary(), "gpu_launches": 2 * args.steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def gpt2_small(linear_cls, vocab=50257, d=768, n_layer=12, n_head=12, ctx=1024):
     """A GPT-2-small-shaped causal LM (random init) whose four linears per block are capture layers.
 
@@ -631,6 +697,8 @@ def main():
         return run_reference(args)
     if args.path == "ghost":
         return run_ghost(args)
+    if args.path == "noproj-sim":
+        return run_noproj_sim(args)
     if args.workload == "gpt2-small":
         return run_gpt2(args)
     import torch
