@@ -58,6 +58,16 @@ OPUS_API const char* opus_last_error(void);
 OPUS_API int opus_device_error(int* code);
 
 /*
+ * Self-test of the bounded waits (no reference counterpart).  Every pipelined
+ * kernel waits on mbarriers with a wall-clock limit (1 s) and, when a wait
+ * runs out, records a code in the device error word, sets its CTA's abort
+ * flag and returns instead of hanging.  This launches one thread that waits
+ * on an mbarrier nothing arrives on: after the limit it records 0x106, which
+ * opus_device_error then reports, and the context stays usable.
+ */
+OPUS_API int opus_selftest_stalled_wait(void* stream);
+
+/*
  * H1 — pack the reference's CountSketch tables.
  * Replaces the tensors built by GradientProjector._get_hash_and_sign
  * (OPUS/train/random_projection.py:51-70): hash int64 in [0,k) and sign

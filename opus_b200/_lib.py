@@ -29,6 +29,7 @@ SIGNATURES: dict[str, tuple] = {
     "opus_abi_version": (_c_int, []),
     "opus_last_error": (ctypes.c_char_p, []),
     "opus_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
+    "opus_selftest_stalled_wait": (_c_int, [_c_p]),
     "opus_pack_hash_sign": (_c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p]),
     "opus_bucket_max_load": (_c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_p]),
     "opus_bucket_max_load_noalloc": (_c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_p]),

@@ -104,9 +104,34 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
   return OPUS_OK;
 }
 
+namespace {
+
+// One thread waits on an mbarrier that nothing arrives on, through the same
+// bounded wait as the pipelined kernels: after kWaitLimitNs it records
+// kDevTimeoutSelftest in the device error word and the kernel returns.
+__global__ void stalled_wait_kernel(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+    (void)mbar_wait(&bar, 0, &abort_flag, err, kDevTimeoutSelftest);
+  }
+}
+
+}  // namespace
 }  // namespace opus
 
 extern "C" {
+
+int opus_selftest_stalled_wait(void* stream) {
+  int* err = opus::device_error_word();
+  if (err == nullptr) return opus::set_error(OPUS_ERR_CUDA, "device error word unavailable");
+  opus::stalled_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(err);
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
 
 int opus_abi_version(void) { return OPUS_ABI_VERSION; }
 

@@ -43,6 +43,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 0x103,
   kDevTimeoutGroup = 0x104,
   kDevTimeoutDrain = 0x105,
+  kDevTimeoutSelftest = 0x106,  // opus_selftest_stalled_wait: a wait that nothing releases
   kDevBadBucket = 0x201,
 };
 

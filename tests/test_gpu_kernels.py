@@ -386,3 +386,22 @@ def test_per_sample_grad_empty_and_tokenless():
     a = torch.zeros(2, 0, 24, device=DEV, dtype=torch.bfloat16)
     out = torch.full((2, 16 * 24), 5.0, device=DEV)
     assert not ops.per_sample_grad(g, a, out=out).any()  # no tokens: zero gradients
+
+
+def test_bounded_wait_reports_and_the_context_survives():
+    """A wait that nothing releases ends after its limit with an error code; later kernels still run."""
+    import ctypes
+    import time
+
+    from opus_b200 import _lib
+
+    assert _lib.device_error() == 0  # nothing pending from earlier tests
+    t0 = time.monotonic()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert _lib.load().opus_selftest_stalled_wait(stream) == _lib.OPUS_OK
+    assert _lib.device_error() == 0x106  # synchronises: the kernel has returned on its own
+    assert 0.9 < time.monotonic() - t0 < 60
+    assert _lib.device_error() == 0  # reading clears the word
+    h, s, packed = cuda_tables(4096, 1, 256)  # the context is still usable
+    assert torch.equal(packed.cpu() & 0x7FFFFFFF, torch.from_numpy(h.astype(np.int32)))
+    ops.check_device_error("after the stalled wait")
