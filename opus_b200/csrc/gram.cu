@@ -97,10 +97,12 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   }
 }
 
+constexpr int64_t kTcMaxKbPerSplit = 64;  // 2048 of k per CTA: accumulation bias below ~4e-5
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     gram_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int ra, int rb,
                    int tiles_j, int n_tiles, int kb_per_split, int n_kb, float alpha, float* __restrict__ out,
-                   int vec_out, int* err) {
+                   int vec_out, int sym, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -115,7 +117,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x % n_tiles, split = blockIdx.x / n_tiles;
-  const int ti = tile / tiles_j, tj = tile % tiles_j;
+  int ti, tj;
+  if (sym) {  // upper-triangle tiles ti <= tj of the tiles_j x tiles_j grid, row by row
+    int t = tile;
+    ti = 0;
+    while (t >= tiles_j - ti) {
+      t -= tiles_j - ti;
+      ++ti;
+    }
+    tj = ti + t;
+  } else {
+    ti = tile / tiles_j;
+    tj = tile % tiles_j;
+  }
+  // a diagonal tile of a self-Gram multiplies a block by itself: one operand load and split
+  const bool self_tile = sym && ti == tj;
   const int kb0 = split * kb_per_split;
   const int kb1 = min(n_kb, kb0 + kb_per_split);
 
@@ -150,9 +166,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
         uint8_t* st = smem + (size_t)s * kTcStage;
-        mbar_arrive_expect_tx(&full[s], 2 * kTcTile);
+        mbar_arrive_expect_tx(&full[s], self_tile ? kTcTile : 2 * kTcTile);
         tma_load_2d(st, &tm_a, &full[s], kb * kTcBK, ti * kTcM);
-        tma_load_2d(st + kTcTile, &tm_b, &full[s], kb * kTcBK, tj * kTcN);
+        if (!self_tile) tma_load_2d(st + kTcTile, &tm_b, &full[s], kb * kTcBK, tj * kTcN);
         if (++s == kTcStages) {
           s = 0;
           ph ^= 1;
@@ -167,7 +183,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!mbar_wait(&conv[s], ph, abort_flag, err, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + (size_t)s * kTcStage);
-        const uint32_t sb = sa + kTcTile, sal = sa + 2 * kTcTile, sbl = sa + 3 * kTcTile;
+        const uint32_t sal = sa + 2 * kTcTile;
+        const uint32_t sb = self_tile ? sa : sa + kTcTile, sbl = self_tile ? sal : sa + 3 * kTcTile;
 #pragma unroll
         for (int kk = 0; kk < kTcBK / 8; ++kk) {
           const uint64_t dah = make_sdesc_sw128(sa + kk * 32, 16, kTcSBO);
@@ -202,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float4* src = reinterpret_cast<float4*>(smem + (size_t)s * kTcStage);
       float4* dst = reinterpret_cast<float4*>(smem + (size_t)s * kTcStage + 2 * kTcTile);
 #pragma unroll 4
-      for (int e = ct; e < 2 * kTcTile / 16; e += kTcConv) {
+      for (int e = ct; e < (self_tile ? kTcTile : 2 * kTcTile) / 16; e += kTcConv) {
         const float4 x = src[e];
         float4 h, l;
         split_tf32(x.x, h.x, l.x);
@@ -243,6 +260,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int e = 0; e < 32; ++e)
             if (j0 + e < rb) atomicAdd(o + e, alpha * __uint_as_float(v[e]));
         }
+        if (sym && ti < tj) {
+          // the mirrored block: element (i, j) also goes to (j, i); lane i writes column i, so
+          // each warp reduction covers 32 consecutive floats of row j
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (j0 + e < rb) atomicAdd(out + (int64_t)(j0 + e) * rb + i, alpha * __uint_as_float(v[e]));
+        }
       }
     }
   }
@@ -255,6 +279,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 int launch_gram_tc(const float* phi_a, int rows_a, const float* phi_b, int rows_b, int64_t k, float alpha, float* out,
                    cudaStream_t st) {
+  // phi_a phi_a^T with a long k: only the tiles on and above the diagonal are computed (the
+  // operand loads they save outweigh the mirrored block's reductions from k = 65536 up)
+  const int sym = (phi_a == phi_b && rows_a == rows_b && k >= 65536) ? 1 : 0;
   CUtensorMap tm_a, tm_b;
   {
     const uint64_t dims[2] = {(uint64_t)k, (uint64_t)rows_a};
@@ -275,13 +302,18 @@ int launch_gram_tc(const float* phi_a, int rows_a, const float* phi_b, int rows_
   if ((size_t)max_smem_optin() < kTcSmem) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gram: shared memory too small");
   OPUS_CUDA_TRY(cudaFuncSetAttribute(gram_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
   const int tiles_i = (rows_a + kTcM - 1) / kTcM, tiles_j = (rows_b + kTcN - 1) / kTcN;
-  const int64_t n_tiles64 = (int64_t)tiles_i * tiles_j;
+  const int64_t n_tiles64 = sym ? (int64_t)tiles_i * (tiles_i + 1) / 2 : (int64_t)tiles_i * tiles_j;
   if (n_tiles64 > 0x7fffffff) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gram: too many tiles");
   const int n_tiles = static_cast<int>(n_tiles64);
   const int n_kb = static_cast<int>((k + kTcBK - 1) / kTcBK);
-  // about one CTA per SM, at least 4 k-blocks (128 k) per CTA
+  // About one CTA per SM, at least 4 k-blocks (128 k) per CTA, and at most kTcMaxKbPerSplit
+  // k-blocks: the tensor cores' f32 accumulation errs by about 6e-7 of the running sum per
+  // 32-wide k-block, one way, so an all-positive sum (a self-similarity) accumulated over n
+  // k-blocks in TMEM is off by about 6e-7 n; the splits are added with rounded f32 atomics.
   int64_t splits = (sm_count() + n_tiles - 1) / n_tiles;
   if (splits > (n_kb + 3) / 4) splits = (n_kb + 3) / 4;
+  const int64_t min_splits = (n_kb + kTcMaxKbPerSplit - 1) / kTcMaxKbPerSplit;
+  if (splits < min_splits) splits = min_splits;
   if (splits < 1) splits = 1;
   const int kb_per_split = static_cast<int>((n_kb + splits - 1) / splits);
   splits = (n_kb + kb_per_split - 1) / kb_per_split;
@@ -289,7 +321,7 @@ int launch_gram_tc(const float* phi_a, int rows_a, const float* phi_b, int rows_
   if (grid > 0x7fffffff) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gram: grid too large");
   const int vec_out = (rows_b % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
   gram_tc_kernel<<<(int)grid, kTcThreads, kTcSmem, st>>>(tm_a, tm_b, rows_a, rows_b, tiles_j, n_tiles, kb_per_split,
-                                                        n_kb, alpha, out, vec_out, device_error_word());
+                                                        n_kb, alpha, out, vec_out, sym, device_error_word());
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

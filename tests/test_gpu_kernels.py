@@ -260,6 +260,25 @@ def test_sketch_gram_tensor_core_and_simt(ra, rb, k):
     ops.check_device_error("sketch_gram")
 
 
+@pytest.mark.parametrize("ra,k", [(256, 65536), (300, 65540), (129, 70000), (1000, 8192)])
+def test_sketch_gram_self_upper_tiles(ra, k):
+    """phi phi^T computes the tiles on and above the diagonal (one operand load on the diagonal)
+    and mirrors the others; partial last tiles and accumulation included.  The diagonal is a
+    sum of squares, on which the tensor cores' f32 accumulation errs one way (about 6e-7 per
+    32-wide k-block, at most 64 k-blocks per CTA), hence 1e-4 rather than 2e-5."""
+    rng = np.random.default_rng(ra + k)
+    A = (rng.standard_normal((ra, k)) * rng.uniform(0.1, 10.0, (ra, 1))).astype(np.float32)
+    tA = torch.from_numpy(A).to(DEV)
+    want = A.astype(np.float64) @ A.T.astype(np.float64)
+    got = ops.sketch_gram(tA, alpha=0.5)
+    ops.check_device_error("self gram")
+    rel_close(got.cpu().numpy(), 0.5 * want, 1e-4, f"self gram {ra}x{k}")
+    ops.sketch_gram(tA, out=got, alpha=0.5, accumulate=True)
+    rel_close(got.cpu().numpy(), want, 1e-4, f"self gram accumulate {ra}x{k}")
+    # a distinct buffer with the same values takes the general path and agrees
+    rel_close(ops.sketch_gram(tA, tA.clone()).cpu().numpy(), want, 1e-4, "general path")
+
+
 def test_sketch_gram_nonfinite():
     """Entries are non-finite exactly where the f32 product is (an inf may come out as NaN:
     the split's hi * lo term is inf * 0 when the other operand is exactly a tf32)."""
