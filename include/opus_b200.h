@@ -169,6 +169,23 @@ OPUS_API int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_
  * each element has one writer, so no scatter and no atomics (vector
  * reductions when accumulating).
  */
+/*
+ * G-ghost Gram (projection off, SGD / Muon) — the candidate similarity
+ * without per-sample gradients: S[i, j] (+)= alpha * <G_i, G_j> for every
+ * pair, G_b = dLdZ_b^T a_b, as sum over token pairs of
+ * (a_i a_j^T) o (dLdZ_i dLdZ_j^T): two tcgen05 GEMMs per 128 x 128 token block
+ * with a fused row-dot epilogue.  Equals the Gram of the per-sample gradients
+ * of grad_dotprod (OPUS/train/data_selection.py:597-619); cheaper than
+ * materialising them when 2 T^2 (d_in + d_out) (B + 1) / 2 < 2 T d_in d_out
+ * + B d_in d_out per candidate, i.e. for short windows.  a [n_rows, seq_len,
+ * d_in], dLdZ [n_rows, seq_len, d_out] bf16 (a_lo / dLdZ_lo: the lo halves of
+ * f32 operands split with opus_split_bf16, or both NULL); d_in, d_out
+ * multiples of 8; S [n_rows, n_rows] f32, zeroed first unless accumulate.
+ */
+OPUS_API int opus_ghost_gram(const void* a, const void* a_lo, const void* dLdZ, const void* dLdZ_lo, int dtype,
+                    int n_rows, int seq_len, int d_in, int d_out, float alpha, float* S, int accumulate,
+                    void* stream);
+
 OPUS_API int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
                          int d_in, const float* diag, float* out, int accumulate, void* stream);
 

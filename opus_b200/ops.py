@@ -167,6 +167,45 @@ def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int
     return out
 
 
+def ghost_gram(a: torch.Tensor, dLdZ: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None,
+               accumulate: bool = False) -> torch.Tensor:
+    """S[i, j] (+)= alpha * <G_i, G_j>, G_b = dLdZ_b^T a_b, for every candidate pair, without forming any G_b.
+
+    a [B, T, d_in], dLdZ [B, T, d_out] in bf16 (tensor cores directly) or f32
+    (split into bf16 hi/lo; hi*hi + hi*lo + lo*hi per product).  Widths that
+    are not multiples of 8 are zero-padded (zero features add nothing).
+    """
+    _cuda(a, "a")
+    _cuda(dLdZ, "dLdZ")
+    if dLdZ.dim() != 3 or a.dim() != 3 or dLdZ.shape[:2] != a.shape[:2]:
+        raise ValueError(f"Unexpected dLdZ/a shapes: {tuple(dLdZ.shape)}, {tuple(a.shape)}")
+    B, T, d_out = dLdZ.shape
+    d_in = a.shape[2]
+    if out is None:
+        out = torch.empty(B, B, dtype=torch.float32, device=a.device)
+        accumulate = False
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < B * B:
+        raise ValueError("out must be a contiguous float32 tensor of at least [B, B]")
+    a, dLdZ = _pad8(a), _pad8(dLdZ)
+    lib = _lib.load()
+    if a.dtype == torch.bfloat16 and dLdZ.dtype == torch.bfloat16:
+        parts = (_contig(a), None, _contig(dLdZ), None)
+    else:
+        a_hi, a_lo = split_bf16(a)
+        g_hi, g_lo = split_bf16(dLdZ)
+        parts = (a_hi, a_lo, g_hi, g_lo)
+    _lib.check(lib.opus_ghost_gram(_ptr(parts[0]), _ptr(parts[1]), _ptr(parts[2]), _ptr(parts[3]), _lib.DTYPE_BF16,
+                                   B, T, a.shape[2], dLdZ.shape[2], float(alpha), _ptr(out), int(accumulate),
+                                   _stream(a)), "opus_ghost_gram")
+    return out
+
+
+def _pad8(x: torch.Tensor) -> torch.Tensor:
+    d = x.shape[-1]
+    p = (d + 7) // 8 * 8
+    return x if p == d else torch.nn.functional.pad(x, (0, p - d))
+
+
 def per_sample_grad(dLdZ: torch.Tensor, a: torch.Tensor, diag: torch.Tensor | None = None,
                     out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
     """out[b] (+)= (diag o dLdZ_b^T a_b) flattened: exact per-sample gradients [B, d_out*d_in] in f32.

@@ -424,3 +424,31 @@ def test_bounded_wait_reports_and_the_context_survives():
     h, s, packed = cuda_tables(4096, 1, 256)  # the context is still usable
     assert torch.equal(packed.cpu() & 0x7FFFFFFF, torch.from_numpy(h.astype(np.int32)))
     ops.check_device_error("after the stalled wait")
+
+
+@pytest.mark.parametrize("B,T,d_in,d_out,dtype", [
+    (5, 200, 72, 136, torch.bfloat16),     # two token blocks (one partial), partial feature blocks
+    (3, 64, 256, 128, torch.float32),      # f32: bf16 hi/lo, three products per GEMM
+    (1, 130, 20, 30, torch.float32),       # widths padded to 8
+    (7, 128, 768, 3072, torch.bfloat16),   # GPT-2-small MLP widths
+])
+def test_ghost_gram_matches_materialised_gram(B, T, d_in, d_out, dtype):
+    """sum over token pairs of (a_i a_j^T) o (g_i g_j^T) == <G_i, G_j> of the per-sample gradients."""
+    torch.manual_seed(B * 100 + T)
+    a = torch.randn(B, T, d_in, device=DEV).to(dtype)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-2).to(dtype)
+    got = ops.ghost_gram(a, g, alpha=0.5)
+    ops.check_device_error("ghost_gram")
+    G = np.einsum("bto,btc->boc", g.double().cpu().numpy(), a.double().cpu().numpy()).reshape(B, -1)
+    want = 0.5 * G @ G.T
+    rel_close(got.cpu().numpy(), want, 1e-4 if dtype == torch.float32 else 2e-5, "ghost gram")
+    ops.ghost_gram(a, g, alpha=0.5, out=got, accumulate=True)
+    rel_close(got.cpu().numpy(), 2 * want, 1e-4 if dtype == torch.float32 else 2e-5, "ghost gram accumulate")
+
+
+def test_ghost_gram_empty():
+    a = torch.zeros(3, 0, 16, device=DEV, dtype=torch.bfloat16)
+    g = torch.zeros(3, 0, 24, device=DEV, dtype=torch.bfloat16)
+    out = torch.full((3, 3), 7.0, device=DEV)
+    assert not ops.ghost_gram(a, g, out=out).any()
+    assert ops.ghost_gram(a[:0], g[:0]).shape == (0, 0)

@@ -308,3 +308,13 @@ def test_ppl_strategy_matches_reference(mode, ratio):
     idx = ds.get_batch_opus(model, ct, ct.clone(), None, None, None, [], None, ratio, 128,
                             selection_strategy="ppl", selection_method=mode, score_len=128)
     assert idx.tolist() == g[f"{mode}_{ratio}"].tolist()
+
+
+@pytest.mark.parametrize("B,T,d_in,d_out,ghost", [
+    (64, 64, 768, 3072, True), (64, 128, 768, 3072, True), (64, 256, 768, 3072, False),
+    (64, 1024, 768, 3072, False), (16, 128, 768, 768, True), (8, 512, 768, 768, True),
+    (6, 128, 64, 128, True),  # the whole-path fixtures' tiny layers
+])
+def test_ghost_gram_cost_model(B, T, d_in, d_out, ghost):
+    """The projection-off similarity picks the path that measured faster on a B200."""
+    assert ds.ghost_gram_cheaper(B, T, d_in, d_out) is ghost
