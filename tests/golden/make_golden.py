@@ -122,6 +122,15 @@ SCENARIOS = {
 }
 
 
+# projection off with one score column per proxy, and Muon without projection (the ghost Gram
+# of the factors, after the candidate dL/dZ's Muon transform); own seeds, so the fixtures above
+# are unchanged when these are generated
+EXTRA_SCENARIOS = {
+    "adamw_noproj_perval": ("adamw", False, True, "adamw", "f32"),
+    "muon_noproj": ("muon", False, False, "muon", "f32"),
+}
+
+
 def build_workload(rng, ref_linear, opt_kind, B=6, n=2, T=128, vocab=256):
     torch.manual_seed(0)
     model = TinyLM(ref_linear, vocab=vocab)
@@ -150,9 +159,9 @@ def build_workload(rng, ref_linear, opt_kind, B=6, n=2, T=128, vocab=256):
     return model, cand, prox, opts, opt_arrays
 
 
-def gen_wholepath(ds, ref_linear):
-    for si, (name, (precond, proj_on, per_val, opt_kind, _dt)) in enumerate(SCENARIOS.items()):
-        rng = np.random.default_rng(100 + si)
+def gen_wholepath(ds, ref_linear, scenarios=None, seed0=100):
+    for si, (name, (precond, proj_on, per_val, opt_kind, _dt)) in enumerate((scenarios or SCENARIOS).items()):
+        rng = np.random.default_rng(seed0 + si)
         model, cand, prox, opts, opt_arrays = build_workload(rng, ref_linear, opt_kind)
         weights = state_to_numpy(model)
         if proj_on:
@@ -170,6 +179,8 @@ def gen_wholepath(ds, ref_linear):
         save(f"wholepath_{name}", cand=cand, prox=prox, scores=scores, sim=sim,
              cfg=np.array([int(proj_on), int(per_val)]), precond=np.array(precond), opt_kind=np.array(opt_kind),
              **{f"w/{k}": v for k, v in weights.items()}, **opt_arrays)
+    if scenarios is not None:
+        return
 
     # get_batch_opus end to end: stochastic and greedy selection
     for method in ("stochastic", "greedy"):
@@ -413,6 +424,9 @@ def main() -> int:
     if args.only == "ppl":
         gen_ppl(ds, GCLinear)
         return 0
+    if args.only == "noproj_extra":
+        gen_wholepath(ds, GCLinear, EXTRA_SCENARIOS, 200)
+        return 0
     if args.only == "gpt2width":
         gen_gpt2_width(ds, GCLinear)
         gen_gpt2m_muon(ds, GCLinear)
@@ -430,6 +444,7 @@ def main() -> int:
     gen_layer_bf16(rp)
     gen_muon(ds)
     gen_wholepath(ds, GCLinear)
+    gen_wholepath(ds, GCLinear, EXTRA_SCENARIOS, 200)
     gen_wholepath_lora(ds, GCLoRALinear)
     gen_ppl(ds, GCLinear)
     gen_gpt2_width(ds, GCLinear)

@@ -10,7 +10,8 @@ from opus_b200.layers import GCLinear, GCLoRALinear, LoRALinear
 from opus_b200.train import data_selection as ds
 from tiny_model import MuonLike, ProxyLoader, TinyLM, load_numpy_state, lora_factory
 
-SCENARIOS = ["adamw_proj", "adamw_proj_perval", "adamw_noproj", "sgd_proj", "sgd_noproj", "muon_proj", "auto_mixed"]
+SCENARIOS = ["adamw_proj", "adamw_proj_perval", "adamw_noproj", "adamw_noproj_perval", "sgd_proj", "sgd_noproj",
+             "muon_proj", "muon_noproj", "auto_mixed"]
 
 
 def rebuild(g, device="cpu"):
