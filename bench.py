@@ -88,17 +88,69 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples during the timed region."""
+    """SM clock and throttle-reason samples during the timed region.
+
+    Polls NVML every millisecond from a thread (the fields of
+    ``nvidia-smi --query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.*``), so a timed
+    region of a few tens of milliseconds still gets tens of samples, where an
+    ``nvidia-smi -lms`` child process would still be starting up. Falls back to that
+    child process when NVML cannot be opened. Only reads; sets nothing.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    # NVML clocks-event reason bits, in NAMES order
+    BITS = (0x8, 0x40, 0x20, 0x4)
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
+    def __init__(self, gpu_index: int, period_s: float = 0.001):
+        self.gpu, self.period = gpu_index, period_s
+        self.proc = self.thread = self.handle = None
+        self.samples, self.lines = [], []
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = self._nvml_handle(pynvml, gpu_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.handle = None
+
+    @staticmethod
+    def _nvml_handle(pynvml, gpu_index):
+        """The NVML device behind CUDA device ``gpu_index``, matched by UUID."""
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            ids = [x for x in vis.split(",") if x.strip()]
+            phys = int(ids[gpu_index]) if gpu_index < len(ids) and ids[gpu_index].strip().isdigit() else gpu_index
+            return pynvml.nvmlDeviceGetHandleByIndex(phys)
+
+    def _poll(self):
+        nv, h = self.nvml, self.handle
+        reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), int(reasons_fn(h))))
+            except Exception:
+                return
+            self.stop.wait(self.period)
 
     def __enter__(self):
+        if self.handle is not None:
+            import threading
+
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -108,7 +160,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -121,23 +175,30 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
+        if self.samples:
+            for mhz, bits in self.samples:
+                sm.append(mhz)
+                reasons.update(n for n, b in zip(self.NAMES, self.BITS) if bits & b)
+            mx = [self.max_mhz]
+            source = "nvml"
+        else:
+            for ln in self.lines:
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx.append(float(f[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(self.NAMES, f[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+            source = "nvidia-smi"
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm), "source": source}
 
 
 def make_inputs(device, rank, nb=B):

@@ -472,10 +472,6 @@ __global__ void __launch_bounds__(NT, 1)
 
 using namespace opus;
 
-extern "C" {
-
-}  // extern "C"
-
 namespace {
 
 int launch_boltzmann(const float* scores, const float* sim, int n, int block, int n_select, double temperature,
