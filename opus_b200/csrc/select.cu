@@ -1,6 +1,7 @@
 // Stage 5: Boltzmann (softmax-temperature) and greedy selection with the
-// interaction penalty on one CTA with the scores held in shared memory (128
-// to 1024 threads, chosen by the candidate count).  The float32 / float64
+// interaction penalty on one CTA (128 to 1024 threads, chosen by the candidate
+// count; the Boltzmann sampler keeps each thread's candidates in registers,
+// the greedy one keeps the scores in shared memory).  The float32 / float64
 // operation order follows numpy so the same uniforms give the same indices as
 // the host implementation:
 //   - scaled = score / T in float32, shifted by its max only if max > 700;
@@ -12,8 +13,10 @@
 // The float64 running sum is evaluated exactly with an int64 scan whenever
 // every p is a multiple of 2^-52 (then no partial sum rounds), and the
 // division by cdf[-1] with the comparison against u becomes one integer
-// threshold per draw; otherwise one thread runs the sequential float64
-// recurrence and every element is divided.
+// threshold per draw.  Otherwise the same scan of the truncated p gives the
+// pick whenever u is farther from the cdf entries on either side of it than
+// the rounding of the float64 sum can reach; only when it is not does one
+// thread run the sequential float64 recurrence and every element get divided.
 #include "opus_common.cuh"
 
 namespace opus {
@@ -21,99 +24,35 @@ namespace {
 
 constexpr int kSelMax = 8192;
 constexpr int kPwBlock = 128;
-// numpy splits a length-m sum at m/2 rounded down to a multiple of 8 until a
-// piece is <= 128 long; for m <= 8192 the pieces at depth 7 are <= 79 long,
-// so the split tree has at most 8 levels of at most 128 nodes.
-constexpr int kLevels = 8;
-constexpr int kLevelSlots = 128;
-// p and exp(x) by compacted position q live at q + 8 * (q / 128): the leaves
-// of 128 that four 8-lane groups of a warp read at once fall in distinct banks
+// numpy's split tree for m <= 8192 candidates is at most 7 levels deep
+constexpr int kMaxSlots = 128;
+// p by compacted position q lives at q + 8 * (q / 128): the leaves of 128 that
+// four 8-lane groups of a warp read at once fall in distinct banks
 constexpr int kSkewedMax = kSelMax + kSelMax / kPwBlock * 8;
 
 __device__ __forceinline__ int skew(int q) { return q + ((q >> 7) << 3); }
 
 struct SelShared {
-  // scaled scores x = score / T by original index during a draw; the float64
-  // running sum by compacted position on the rare inexact path (x is dead by then)
-  union {
-    double cdf[kSelMax];
-    float xs[kSelMax];
-  };
-  float scores[kSelMax];
-  float pc[kSkewedMax];  // exp(x), then p, at skew(compacted position)
-  int pos[kSelMax];    // compacted position of each available candidate
-  unsigned char avail[kSelMax];
-  int lvl_start[kLevels][kLevelSlots];
-  int lvl_len[kLevels][kLevelSlots];   // 0 = no node in this slot
-  float lvl_sum[kLevels][kLevelSlots];
-  int leaf_slot[kLevels * kLevelSlots];  // (level << 7) | slot of every leaf
-  int n_leaves;
-  int tree_depth;
+  double cdf[kSelMax];       // float64 running sum by compacted position (inexact fallback only)
+  float pc[kSkewedMax];      // exp(x), then p, at skew(compacted position)
+  float slot_sum[kMaxSlots]; // pairwise-sum leaves of this draw, one per slot
   long long scan_ll[32];
   int red_ne[32];
   float red_f[32];
   int red_nan[32];
-  float total;
   double cdf_total;
-  int pick;  // compacted position of this draw's pick
-  int sel;   // its original index
+  int pick;      // compacted position of this draw's pick
+  int sel;       // its original index
+  int fallback;  // set when the inexact-path pick could not be proven
 };
 
-// ---- numpy pairwise float32 sum, as a split tree built level by level
-// One warp: the node in slot j of level d has children in slots 2j, 2j+1 of
-// level d+1 (left piece first, as numpy adds left + right).
-__device__ void pw_tree_build(int m, SelShared& s, int lane) {
-  if (lane == 0) {
-    s.lvl_start[0][0] = 0;
-    s.lvl_len[0][0] = m;
-  }
-  int nl = 0, depth = kLevels - 1;
-  for (int d = 0; d < kLevels; ++d) {
-    __syncwarp();
-    const int width = 1 << d;
-    bool more = false;
-    for (int j0 = 0; j0 < width; j0 += 32) {
-      const int j = j0 + lane;
-      const int len = j < width ? s.lvl_len[d][j] : 0;
-      const bool leaf = len > 0 && len <= kPwBlock;
-      if (d + 1 < kLevels && j < width) {
-        const int start = s.lvl_start[d][j];
-        int n2 = 0;
-        if (len > kPwBlock) {
-          n2 = len / 2;
-          n2 -= n2 % 8;
-        }
-        s.lvl_start[d + 1][2 * j] = start;
-        s.lvl_len[d + 1][2 * j] = n2;
-        s.lvl_start[d + 1][2 * j + 1] = start + n2;
-        s.lvl_len[d + 1][2 * j + 1] = len > kPwBlock ? len - n2 : 0;
-      }
-      const unsigned bal = __ballot_sync(0xffffffffu, leaf);
-      if (leaf) s.leaf_slot[nl + __popc(bal & ((1u << lane) - 1u))] = (d << 7) | j;
-      nl += __popc(bal);
-      more |= __any_sync(0xffffffffu, len > kPwBlock);
-    }
-    if (!more) {
-      depth = d;  // deepest level holding a node
-      break;
-    }
-  }
-  if (lane == 0) {
-    s.n_leaves = nl;
-    s.tree_depth = depth;
-  }
-}
-
-// One warp, after every leaf sum is in lvl_sum: internal nodes bottom-up.
-__device__ float pw_tree_sum(SelShared& s, int lane) {
-  for (int d = s.tree_depth - 1; d >= 0; --d) {
-    __syncwarp();
-    const int width = 1 << d;
-    for (int j = lane; j < width; j += 32)
-      if (s.lvl_len[d][j] > kPwBlock) s.lvl_sum[d][j] = __fadd_rn(s.lvl_sum[d + 1][2 * j], s.lvl_sum[d + 1][2 * j + 1]);
-  }
-  __syncwarp();
-  return s.lvl_sum[0][0];
+// Depth of numpy's pairwise split tree for m elements: a piece longer than 128
+// splits at half its length rounded down to a multiple of 8, and the right piece
+// (the longer one) is always at least as deep as the left.
+__device__ __forceinline__ int pw_depth(int m) {
+  int d = 0;
+  for (int len = m; len > kPwBlock; ++d) len -= (len / 2) & ~7;
+  return d;
 }
 
 __device__ __forceinline__ unsigned long long shr128(unsigned long long h, unsigned long long l, int k) {
@@ -178,46 +117,70 @@ __device__ long long cdf_threshold(double u, long long L) {
   return static_cast<long long>(t);
 }
 
-// Warp 0 owns no candidates: it lays out the pairwise-sum tree of the next
-// draw while the others normalise.  Owner thread t (t >= 32) holds the
-// contiguous original indices [(t-32)*per, (t-31)*per): their scores,
-// availability, compacted positions and interaction penalties, so no barrier
-// separates one draw from the next.  The compacted (available-only) order is
-// thread order, then index order inside a thread; a pick at compacted
-// position q moves every later available candidate down by one.
-template <int NT>
+// One CTA, NT threads; thread t owns the contiguous original indices
+// [t*cnt, t*cnt + cnt) with cnt = ceil(n / NT) <= PER, and keeps their scores,
+// x = score/T, exp(x) and availability in registers.  The compacted
+// (available-only) order is thread order, then index order inside a thread, so
+// a thread's available candidates sit at consecutive positions from its base,
+// which drops by one whenever an earlier thread's candidate is picked.
+//
+// numpy's pairwise sum over the m available p is evaluated on a complete binary
+// tree of 2^D slots, D = the split tree's depth for m: slot g is the numpy
+// piece reached by descending along the bits of g, or, below a piece of <= 128
+// (a leaf), the leaf itself on the leftmost path and an empty slot (sum +0)
+// elsewhere.  Combining slots pairwise level by level then adds the numpy
+// nodes in numpy's order (x + 0 == x for the non-negative partial sums), and a
+// butterfly of shuffles gives every warp the total without another barrier.
+template <int NT, int PER>
 __global__ void __launch_bounds__(NT, 1)
     boltzmann_kernel(const float* __restrict__ scores_in, const float* __restrict__ sim, int n, int n_select,
                      int block, float temp, const double* __restrict__ uniforms, int64_t* __restrict__ out_idx,
                      int* err) {
   constexpr int W = NT / 32;
-  constexpr int kOwners = NT - 32;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   SelShared& s = *reinterpret_cast<SelShared*>(sel_smem);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int per = (n + kOwners - 1) / kOwners;
-  if (per > 2 && (per & 1) == 0) ++per;  // odd: a warp's k-th candidates fall in distinct banks
-  const int lo = tid < 32 ? n : min(n, (tid - 32) * per), hi = tid < 32 ? n : min(n, lo + per);
-  for (int i = lo; i < hi; ++i) {
-    s.scores[i] = scores_in[i];
-    s.avail[i] = 1;
-    s.pos[i] = i;
+  const int cnt = (n + NT - 1) / NT;
+  const int lo = min(n, tid * cnt), own = min(n, lo + cnt) - lo;
+  float sc[PER], xv[PER], ev[PER];
+  unsigned mask = 0;  // bit k: candidate lo + k is still available
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    sc[k] = k < own ? scores_in[lo + k] : 0.0f;
+    xv[k] = ev[k] = 0.0f;
+    if (k < own) mask |= 1u << k;
   }
-  if (warp == 0) pw_tree_build(n, s, lane);
+  int pbase = lo;  // compacted position of this thread's first available candidate
+  if (tid == 0) {
+    s.fallback = 0;
+    s.pick = 0;
+    s.sel = 0;
+  }
   __syncthreads();
 
+  // candidates whose score changed since x and exp(x) were cached: all at the
+  // first draw and after a dense penalty row, else the picked block
+  int c0 = 0, c1 = n;
   for (int r = 0; r < n_select; ++r) {
     const int m = n - r;  // available candidates
     const double u = uniforms[r];
-    // (1) x = score / T and exp(x) at the compacted positions; max and NaN flag
+    // (1) x = score / T and exp(x) (refreshed where the score changed), placed
+    //     at the compacted positions; max and NaN flag
     float lmax = -INFINITY;
     int lnan = 0;
-    for (int i = lo; i < hi; ++i) {
-      if (!s.avail[i]) continue;
-      const float x = __fdiv_rn(s.scores[i], temp);
-      s.xs[i] = x;
-      s.pc[skew(s.pos[i])] = static_cast<float>(exp(static_cast<double>(x)));
-      if (isnan(x)) lnan = 1; else lmax = fmaxf(lmax, x);
+    {
+      int q = pbase;
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        if (!((mask >> k) & 1u)) continue;
+        const int i = lo + k;
+        if (i >= c0 && i < c1) {
+          xv[k] = __fdiv_rn(sc[k], temp);
+          ev[k] = static_cast<float>(exp(static_cast<double>(xv[k])));
+        }
+        s.pc[skew(q++)] = ev[k];
+        if (isnan(xv[k])) lnan = 1; else lmax = fmaxf(lmax, xv[k]);
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -239,23 +202,35 @@ __global__ void __launch_bounds__(NT, 1)
         nn |= __shfl_xor_sync(0xffffffffu, nn, off);
       }
       if (nn == 0 && mx > 700.0f) {
-        for (int i = lo; i < hi; ++i)
-          if (s.avail[i]) s.pc[skew(s.pos[i])] = static_cast<float>(exp(static_cast<double>(__fsub_rn(s.xs[i], mx))));
+        int q = pbase;
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+          if ((mask >> k) & 1u) s.pc[skew(q++)] = static_cast<float>(exp(static_cast<double>(__fsub_rn(xv[k], mx))));
         __syncthreads();
       }
     }
-    // (2) leaf sums, 8 lanes per leaf: lane j holds numpy's accumulator r[j],
+    // (2) leaf sums, 8 lanes per slot: lane j holds numpy's accumulator r[j],
     //     combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail;
-    //     leaves shorter than 8 are a running sum from 0.  After a barrier
-    //     warp 0 combines the tree.
-    const int n_leaves = s.n_leaves;
-    for (int l0 = 0; l0 < n_leaves; l0 += NT / 8) {
-      const int leaf = l0 + (tid >> 3), j = tid & 7;
-      const bool active = leaf < n_leaves;
-      const int slot = active ? s.leaf_slot[leaf] : 0;
-      const int d = slot >> 7, sj = slot & (kLevelSlots - 1);
-      const int a0 = active ? s.lvl_start[d][sj] : 0;
-      const int ln = active ? s.lvl_len[d][sj] : 0;
+    //     leaves shorter than 8 are a running sum from 0
+    const int depth = pw_depth(m), n_slots = 1 << depth;
+    for (int g0 = 0; g0 < n_slots; g0 += NT / 8) {
+      const int g = g0 + (tid >> 3), j = tid & 7;
+      const bool active = g < n_slots;
+      int a0 = 0, ln = active ? m : 0;
+      for (int d = depth - 1; d >= 0; --d) {
+        const bool right = (g >> d) & 1;
+        if (ln > kPwBlock) {
+          const int n2 = (ln / 2) & ~7;
+          if (right) {
+            a0 += n2;
+            ln -= n2;
+          } else {
+            ln = n2;
+          }
+        } else if (right) {
+          ln = 0;
+        }
+      }
       const int full = ln >= 8 ? ln - (ln % 8) : 0;
       float v[kPwBlock / 8];
 #pragma unroll
@@ -275,31 +250,45 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int t = 0; t < 7; ++t)
           if (full + t < ln) res = __fadd_rn(res, tail[t]);
-        s.lvl_sum[d][sj] = res;
+        s.slot_sum[g] = res;
       }
     }
-    __syncthreads();
-    if (warp == 0) {
-      const float root = pw_tree_sum(s, lane);
-      if (lane == 0) s.total = __fadd_rn(0.0f, root);
+    __syncthreads();                                                   // barrier L
+    // (3) every warp combines the slots (pairs of slots first when there are
+    //     more than 32), then normalises its owned positions; p * 2^52 is an
+    //     integer for every p >= 2^-29, and then the float64 running sum is
+    //     exact and equals an int64 scan
+    float total;
+    {
+      float v;
+      if (n_slots <= 32) {
+        v = s.slot_sum[lane & (n_slots - 1)];  // every group of n_slots lanes holds the slots
+      } else if (n_slots == 64) {
+        v = __fadd_rn(s.slot_sum[2 * lane], s.slot_sum[2 * lane + 1]);
+      } else {
+        v = __fadd_rn(__fadd_rn(s.slot_sum[4 * lane], s.slot_sum[4 * lane + 1]),
+                      __fadd_rn(s.slot_sum[4 * lane + 2], s.slot_sum[4 * lane + 3]));
+      }
+      const int span = n_slots < 32 ? n_slots : 32;
+      for (int off = 1; off < span; off <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+      total = __fadd_rn(0.0f, v);
     }
-    __syncthreads();                                                   // barrier B
-    const float total = s.total;
     const bool uniform = (total == 0.0f) || !isfinite(total);
     const float inv_m = __fdiv_rn(1.0f, static_cast<float>(m));
-    // (3) normalise the owned positions; p * 2^52 is an integer for every
-    //     p >= 2^-29, and then the float64 running sum is exact and equals an
-    //     int64 scan.  Warp 0 lays out the next draw's tree meanwhile.
     int not_exact = 0;
     long long fsum = 0;
-    for (int i = lo; i < hi; ++i) {
-      if (!s.avail[i]) continue;
-      const int q = skew(s.pos[i]);
-      const float p = uniform ? inv_m : __fdiv_rn(s.pc[q], total);
-      s.pc[q] = p;
-      long long P;
-      if (!fixed52(p, P)) not_exact = 1;
-      fsum += P;
+    {
+      int q = pbase;
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        if (!((mask >> k) & 1u)) continue;
+        const int qs = skew(q++);
+        const float p = uniform ? inv_m : __fdiv_rn(s.pc[qs], total);
+        s.pc[qs] = p;
+        long long P;
+        if (!fixed52(p, P)) not_exact = 1;
+        fsum += P;
+      }
     }
     long long fx = fsum;
 #pragma unroll
@@ -311,7 +300,6 @@ __global__ void __launch_bounds__(NT, 1)
     for (int off = 16; off > 0; off >>= 1) not_exact |= __shfl_xor_sync(0xffffffffu, not_exact, off);
     if (lane == 31) s.scan_ll[warp] = fx;
     if (lane == 0) s.red_ne[warp] = not_exact;
-    if (warp == 0 && r + 1 < n_select) pw_tree_build(m - 1, s, lane);
     __syncthreads();                                                   // barrier C
     long long fbase, ftot;
     bool exact;
@@ -336,23 +324,54 @@ __global__ void __launch_bounds__(NT, 1)
     }
     // (4) searchsorted(cdf / cdf[-1], u, 'right') counts the entries <= u; the
     //     cdf is non-decreasing, so the pick is the first position whose entry
-    //     is not <= u (or the last one), and the thread holding it writes it
-    if (exact) {
-      const long long thr = cdf_threshold(u, ftot);
-      long long run = fbase;
-      for (int i = lo; i < hi; ++i) {
-        if (!s.avail[i]) continue;
-        const int q = s.pos[i];
-        const long long prev = run;
-        long long P;
-        fixed52(s.pc[skew(q)], P);
-        run += P;
-        if ((run > thr && (q == 0 || prev <= thr)) || (q == m - 1 && run <= thr)) {
-          s.pick = q;
-          s.sel = i;
+    //     is not <= u (or the last one).  With T_q the int64 scan, that is the
+    //     first T_q above thr = max{X : RN(X / T_{m-1}) <= u}; thr is within
+    //     2 of u * T_{m-1}, so only a thread whose range of T comes that close
+    //     evaluates it and searches its candidates.
+    //     When some p is not a multiple of 2^-52, T_q truncates the p and the
+    //     float64 running sum c_q rounds: |c_q * 2^52 - T_q| < q + 1 + m/2 * S_q
+    //     <= E = 2m + 2 (S_q the exact sum, <= 1 + 3.5e-4).  The pick found from
+    //     T stands when it is proven by that margin on both sides; otherwise
+    //     one thread runs the float64 recurrence below.
+    {
+      const bool u_ok = u >= 0.0 && u < 1.0;
+      const double approx = u * static_cast<double>(ftot);
+      const bool cand = own > 0 && (!u_ok || (static_cast<double>(fbase) <= approx + 4.0 &&
+                                              approx - 4.0 < static_cast<double>(fbase + fsum)));
+      if (__any_sync(0xffffffffu, cand)) {
+        const long long thr = cdf_threshold(u, ftot);
+        if (cand) {
+          long long run = fbase;
+          int q = pbase;
+#pragma unroll
+          for (int k = 0; k < PER; ++k) {
+            if (!((mask >> k) & 1u)) continue;
+            long long P;
+            fixed52(s.pc[skew(q)], P);
+            const long long prev = run;
+            run += P;
+            if ((run > thr && (q == 0 || prev <= thr)) || (q == m - 1 && run <= thr)) {
+              s.pick = q;
+              s.sel = lo + k;
+              if (!exact) {
+                const double E = 2.0 * m + 2.0;
+                bool proven = true;
+                if (q != m - 1)
+                  proven = static_cast<double>(run) - E >= (u * (static_cast<double>(ftot) + E)) * (1.0 + 0x1p-50);
+                if (q != 0)
+                  proven = proven &&
+                           static_cast<double>(prev) + E <= (u * (static_cast<double>(ftot) - E)) * (1.0 - 0x1p-50);
+                if (!proven) s.fallback = 1;
+              }
+            }
+            ++q;
+          }
         }
       }
-    } else {
+    }
+    __syncthreads();                                                   // barrier D
+    if (s.fallback) {
+      // float64 recurrence of numpy's cumsum, then RN(cdf[q] / cdf[-1]) <= u
       if (tid == 0) {
         double acc = 0.0;
         for (int q = 0; q < m; ++q) {
@@ -362,36 +381,42 @@ __global__ void __launch_bounds__(NT, 1)
         s.cdf_total = acc;
       }
       __syncthreads();
+      if (tid == 0) s.fallback = 0;  // every thread has read it
       const double last = s.cdf_total;
-      for (int i = lo; i < hi; ++i) {
-        if (!s.avail[i]) continue;
-        const int q = s.pos[i];
+      int q = pbase;
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        if (!((mask >> k) & 1u)) continue;
         const bool le = __ddiv_rn(s.cdf[q], last) <= u;
         const bool prev_le = q == 0 || __ddiv_rn(s.cdf[q - 1], last) <= u;
         if ((!le && prev_le) || (q == m - 1 && le)) {
           s.pick = q;
-          s.sel = i;
+          s.sel = lo + k;
         }
+        ++q;
       }
+      __syncthreads();
     }
-    __syncthreads();                                                   // barrier D
-    const int pick = s.pick, sel = s.sel;
+    const int sel = s.sel;
     if (tid == 0) out_idx[r] = sel;
-    // (5) interaction penalty on every owned score (float32), retire the pick,
-    //     close the gap it leaves.  Block-diagonal sim: [n/block, block,
-    //     block], and only the pick's own block has nonzero entries (x - 0 == x).
-    const float* row = sim + (int64_t)sel * n;
-    int plo = lo, phi = hi;
+    // (5) interaction penalty on every owned score (float32) and retire the
+    //     pick.  Block-diagonal sim: [n/block, block, block], and only the
+    //     pick's own block has nonzero entries (x - 0 == x).
+    const float* row = sim + static_cast<int64_t>(sel) * n;
+    c0 = 0;
+    c1 = n;
     if (block > 0) {
-      const int q0 = sel - sel % block;
-      row = sim + (int64_t)sel * block - q0;
-      plo = max(lo, q0);
-      phi = min(hi, q0 + block);
+      c0 = sel - sel % block;
+      c1 = c0 + block;
+      row = sim + static_cast<int64_t>(sel) * block - c0;
     }
-    for (int i = plo; i < phi; ++i) s.scores[i] = __fsub_rn(s.scores[i], row[i]);
-    for (int i = lo; i < hi; ++i)
-      if (s.avail[i] && s.pos[i] > pick) s.pos[i] -= 1;
-    if (sel >= lo && sel < hi) s.avail[sel] = 0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = lo + k;
+      if (k < own && i >= c0 && i < c1) sc[k] = __fsub_rn(sc[k], __ldg(row + i));
+    }
+    if (sel < lo) --pbase;
+    else if (sel < lo + own) mask &= ~(1u << (sel - lo));
   }
 }
 
@@ -487,18 +512,25 @@ int launch_boltzmann(const float* scores, const float* sim, int n, int block, in
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const float tf = static_cast<float>(temperature);
   int* err = device_error_word();
-  // one candidate per thread up to 1024 candidates, then 1024 threads
-#define OPUS_LAUNCH_BOLTZMANN(NT)                                                                              \
-  OPUS_CUDA_TRY(cudaFuncSetAttribute(boltzmann_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-  boltzmann_kernel<NT><<<1, NT, smem, st>>>(scores, sim, n, n_select, block, tf, uniforms, out_idx, err)
+  // one candidate per thread up to 1024 candidates, then 1024 threads with up to 8 each
+#define OPUS_LAUNCH_BOLTZMANN(NT, PER)                                                                          \
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(boltzmann_kernel<NT, PER>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                     (int)smem));                                                                 \
+  boltzmann_kernel<NT, PER><<<1, NT, smem, st>>>(scores, sim, n, n_select, block, tf, uniforms, out_idx, err)
   if (n <= 128) {
-    OPUS_LAUNCH_BOLTZMANN(128);
+    OPUS_LAUNCH_BOLTZMANN(128, 1);
   } else if (n <= 256) {
-    OPUS_LAUNCH_BOLTZMANN(256);
+    OPUS_LAUNCH_BOLTZMANN(256, 1);
   } else if (n <= 512) {
-    OPUS_LAUNCH_BOLTZMANN(512);
+    OPUS_LAUNCH_BOLTZMANN(512, 1);
+  } else if (n <= 1024) {
+    OPUS_LAUNCH_BOLTZMANN(1024, 1);
+  } else if (n <= 2048) {
+    OPUS_LAUNCH_BOLTZMANN(1024, 2);
+  } else if (n <= 4096) {
+    OPUS_LAUNCH_BOLTZMANN(1024, 4);
   } else {
-    OPUS_LAUNCH_BOLTZMANN(1024);
+    OPUS_LAUNCH_BOLTZMANN(1024, 8);
   }
 #undef OPUS_LAUNCH_BOLTZMANN
   OPUS_CUDA_TRY(cudaGetLastError());
