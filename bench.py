@@ -71,10 +71,14 @@ def parse_args():
                          "mode scores everything on one rank)")
     ap.add_argument("--model-dtype", default="f32", choices=["f32", "bf16"],
                     help="gpt2-small: parameter and activation dtype (f32 as in the GPT-2-small config)")
-    ap.add_argument("--path", default="sketch", choices=["sketch", "ghost", "noproj-sim"],
+    ap.add_argument("--path", default="sketch", choices=["sketch", "ghost", "noproj-sim", "select"],
                     help="sketch: the selection step (default line); ghost: exact scores through the ghost "
                          "contraction against the de-sketched AdamW target (stage 2 on its own, one GPU); "
-                         "noproj-sim: the projection-off similarity (exact per-sample gradients + Gram, one GPU)")
+                         "noproj-sim: the projection-off similarity (exact per-sample gradients + Gram, one GPU); "
+                         "select: the Boltzmann draw on its own (one GPU, --select N,K,BLOCK)")
+    ap.add_argument("--select", default="2048,512,256", metavar="N,K,BLOCK",
+                    help="--path select: candidates, draws and similarity block (0 = dense); default: the "
+                         "global draw of 8 ranks x 256 candidates")
     args = ap.parse_args()
     return args
 
@@ -507,6 +511,55 @@ def run_noproj_sim(args):
     return 0
 
 
+def run_select(args):
+    """The Boltzmann draw on its own, one GPU: K sequential draws over N candidates.
+
+    Scores N(0, 1e-3) and a symmetric similarity N(0, 1e-4) (dense [N, N], or
+    [N/BLOCK, BLOCK, BLOCK] blocks as the sharded global draw passes it), one
+    float64 uniform per draw; the same shapes as the selection step's draw.
+    """
+    import numpy as np
+    import torch
+
+    from opus_b200 import ops
+
+    n, k, block = (int(x) for x in args.select.split(","))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(SEED)
+    sc = torch.tensor(rng.standard_normal(n) * 1e-3, dtype=torch.float32, device=dev)
+    if block:
+        m = rng.standard_normal((n // block, block, block)) * 1e-4
+        sim = torch.tensor((m + m.transpose(0, 2, 1)) / 2, dtype=torch.float32, device=dev)
+    else:
+        m = rng.standard_normal((n, n)) * 1e-4
+        sim = torch.tensor((m + m.T) / 2, dtype=torch.float32, device=dev)
+    uni = torch.tensor(rng.random(k), dtype=torch.float64, device=dev)
+    for _ in range(args.warmup):
+        ops.boltzmann_select(sc, sim, k, TEMPERATURE, uni)
+    ops.check_device_error("select warm-up")
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            ops.boltzmann_select(sc, sim, k, TEMPERATURE, uni)
+        end.record()
+        torch.cuda.synchronize()
+    ops.check_device_error("select timed region")
+    ms = start.elapsed_time(end) / args.steps
+    line = {"metric": "Boltzmann draws/sec", "value": round(k / (ms / 1e3), 1), "unit": "draws/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{k} of {n} candidates, " + (f"block-diagonal similarity (block {block})"
+                                                                 if block else "dense similarity"),
+                       "temperature": TEMPERATURE},
+            "us_per_draw": round(ms * 1e3 / k, 3), "roofline": None,
+            "bound": "latency: K dependent draws in one CTA", "clocks": clk.summary(), "gpu_launches": args.steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def gpt2_small(linear_cls, vocab=50257, d=768, n_layer=12, n_head=12, ctx=1024):
     """A GPT-2-small-shaped causal LM (random init) whose four linears per block are capture layers.
 
@@ -760,6 +813,8 @@ def main():
         return run_ghost(args)
     if args.path == "noproj-sim":
         return run_noproj_sim(args)
+    if args.path == "select":
+        return run_select(args)
     if args.workload == "gpt2-small":
         return run_gpt2(args)
     import torch
