@@ -79,6 +79,8 @@ def parse_args():
     ap.add_argument("--select", default="2048,512,256", metavar="N,K,BLOCK",
                     help="--path select: candidates, draws and similarity block (0 = dense); default: the "
                          "global draw of 8 ranks x 256 candidates")
+    ap.add_argument("--select-method", default="stochastic", choices=["stochastic", "greedy"],
+                    help="--path select: the Boltzmann draw (default) or the greedy argmax selection")
     args = ap.parse_args()
     return args
 
@@ -512,7 +514,7 @@ def run_noproj_sim(args):
 
 
 def run_select(args):
-    """The Boltzmann draw on its own, one GPU: K sequential draws over N candidates.
+    """The selection draw on its own, one GPU: K sequential draws over N candidates.
 
     Scores N(0, 1e-3) and a symmetric similarity N(0, 1e-4) (dense [N, N], or
     [N/BLOCK, BLOCK, BLOCK] blocks as the sharded global draw passes it), one
@@ -535,20 +537,27 @@ def run_select(args):
         m = rng.standard_normal((n, n)) * 1e-4
         sim = torch.tensor((m + m.T) / 2, dtype=torch.float32, device=dev)
     uni = torch.tensor(rng.random(k), dtype=torch.float64, device=dev)
+    greedy = args.select_method == "greedy"
+
+    def draw():
+        if greedy:
+            return ops.greedy_select(sc, sim, k)
+        return ops.boltzmann_select(sc, sim, k, TEMPERATURE, uni)
+
     for _ in range(args.warmup):
-        ops.boltzmann_select(sc, sim, k, TEMPERATURE, uni)
+        draw()
     ops.check_device_error("select warm-up")
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clk:
         start.record()
         for _ in range(args.steps):
-            ops.boltzmann_select(sc, sim, k, TEMPERATURE, uni)
+            draw()
         end.record()
         torch.cuda.synchronize()
     ops.check_device_error("select timed region")
     ms = start.elapsed_time(end) / args.steps
-    line = {"metric": "Boltzmann draws/sec", "value": round(k / (ms / 1e3), 1), "unit": "draws/s", "n_gpus": 1,
+    line = {"metric": ("greedy" if greedy else "Boltzmann") + " draws/sec", "value": round(k / (ms / 1e3), 1), "unit": "draws/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{k} of {n} candidates, " + (f"block-diagonal similarity (block {block})"

@@ -437,6 +437,15 @@ __device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
   return a.i < b.i ? a : b;
 }
 
+// np.argmax over a warp with two redux steps: the largest order key (NaN above
+// every number, -0 folded into +0 since they compare equal), then the lowest
+// index holding it.
+__device__ __forceinline__ void warp_argmax(int& key, int& idx) {
+  const int kmax = __reduce_max_sync(0xffffffffu, key);
+  idx = __reduce_min_sync(0xffffffffu, key == kmax ? idx : 0x7fffffff);
+  key = kmax;
+}
+
 // Thread t owns the candidates i = t, t + NT, t + 2 NT, ...: it alone reads and
 // writes their scores (the penalty row is then read coalesced), so the one
 // barrier of a draw is the one that publishes the warps' maxima; they sit in
@@ -449,36 +458,25 @@ __global__ void __launch_bounds__(NT, 1)
   constexpr int W = NT / 32;
   extern __shared__ __align__(16) uint8_t sel_smem[];
   float* scores = reinterpret_cast<float*>(sel_smem);
-  __shared__ float rv[2][W];
+  __shared__ int rk[2][W];
   __shared__ int ri[2][W];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < n; i += NT) scores[i] = scores_in[i];
   for (int r = 0; r < n_select; ++r) {
     ArgMax best{-INFINITY, 0x7fffffff};
     for (int i = tid; i < n; i += NT) best = better(best, ArgMax{scores[i], i});
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      ArgMax o;
-      o.v = __shfl_xor_sync(0xffffffffu, best.v, off);
-      o.i = __shfl_xor_sync(0xffffffffu, best.i, off);
-      best = better(best, o);
-    }
+    int key = isnan(best.v) ? 0x7fffffff : f2ord(best.v == 0.0f ? 0.0f : best.v), idx = best.i;
+    warp_argmax(key, idx);
     if (lane == 0) {
-      rv[r & 1][warp] = best.v;
-      ri[r & 1][warp] = best.i;
+      rk[r & 1][warp] = key;
+      ri[r & 1][warp] = idx;
     }
     __syncthreads();
-    ArgMax b{-INFINITY, 0x7fffffff};
-    if (lane < W) b = ArgMax{rv[r & 1][lane], ri[r & 1][lane]};
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      ArgMax o;
-      o.v = __shfl_xor_sync(0xffffffffu, b.v, off);
-      o.i = __shfl_xor_sync(0xffffffffu, b.i, off);
-      b = better(b, o);
-    }
+    key = lane < W ? rk[r & 1][lane] : f2ord(-INFINITY);
+    idx = lane < W ? ri[r & 1][lane] : 0x7fffffff;
+    warp_argmax(key, idx);
     // all entries -inf: np.argmax returns 0
-    const int sel = (b.i == 0x7fffffff) ? 0 : b.i;
+    const int sel = (idx == 0x7fffffff) ? 0 : idx;
     if (tid == 0) out_idx[r] = sel;
     const float* row = sim + (int64_t)sel * n;
     int plo = 0, phi = n;
