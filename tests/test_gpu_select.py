@@ -159,3 +159,33 @@ def test_block_operand_validation():
         ops.boltzmann_select(sc, torch.zeros(5, 2, 2, device=DEV), 2, 1.0, torch.rand(2, dtype=torch.float64))
     with pytest.raises(ValueError):
         ops.greedy_select(sc, torch.zeros(3, 4, 5, device=DEV), 2)
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 7, 8, 9, 127, 128])
+def test_small_candidate_counts_select_everything(n):
+    """Tiny pools drawn to exhaustion: every draw of both samplers equals the oracle's,
+    down to one candidate (a single pairwise leaf shorter than 8)."""
+    rng = np.random.default_rng(500 + n)
+    sc = (rng.standard_normal(n) * 2.0).astype(np.float32)
+    m = (rng.standard_normal((n, n)) * 0.1).astype(np.float32)
+    sim = ((m + m.T) / 2).astype(np.float32)
+    uni = rng.random(n)
+    want = orc.stochastic_greedy_selection(sc, sim, n, temperature=0.8, uniforms=uni)
+    got = ops.boltzmann_select(dev(sc), dev(sim), n, 0.8, dev(uni)).cpu().tolist()
+    ops.check_device_error("boltzmann small n")
+    assert got == want and sorted(got) == list(range(n))
+    assert ops.greedy_select(dev(sc), dev(sim), n).cpu().tolist() == orc.greedy_selection(sc, sim, n)
+
+
+def test_block_equal_to_pool_is_the_dense_draw():
+    """One block holding every candidate: the block operand is the dense matrix."""
+    rng = np.random.default_rng(77)
+    n, K = 300, 120
+    sc = rng.standard_normal(n).astype(np.float32)
+    m = (rng.standard_normal((n, n)) * 0.05).astype(np.float32)
+    sim = ((m + m.T) / 2).astype(np.float32)
+    uni = rng.random(K)
+    dense = ops.boltzmann_select(dev(sc), dev(sim), K, 1.0, dev(uni)).cpu().tolist()
+    block = ops.boltzmann_select(dev(sc), dev(sim[None]), K, 1.0, dev(uni)).cpu().tolist()
+    assert dense == block == orc.stochastic_greedy_selection(sc, sim, K, temperature=1.0, uniforms=uni)
+    assert ops.greedy_select(dev(sc), dev(sim[None]), K).cpu().tolist() == orc.greedy_selection(sc, sim, K)
