@@ -56,6 +56,12 @@ def test_argument_validation_without_device():
     assert rc == _lib.OPUS_ERR_UNSUPPORTED
     rc = lib.opus_boltzmann_select(_null(), _null(), 10, 11, 1.0, _null(), _null(), _null())
     assert rc == _lib.OPUS_ERR_INVALID
+    rc = lib.opus_boltzmann_select(_null(), _null(), 8193, 1, 1.0, _null(), _null(), _null())
+    assert rc == _lib.OPUS_ERR_UNSUPPORTED and "8192" in _lib.last_error()  # one CTA holds at most 8192
+    rc = lib.opus_boltzmann_select_blocks(_null(), _null(), 12, 5, 2, 1.0, _null(), _null(), _null())
+    assert rc == _lib.OPUS_ERR_INVALID  # the block must divide n
+    rc = lib.opus_greedy_select(_null(), _null(), 4 * 8192 + 1, 1, _null(), _null())
+    assert rc == _lib.OPUS_ERR_UNSUPPORTED
     rc = lib.opus_ghost_score(_null(), _null(), _lib.DTYPE_BF16, 1, 1, 12, 8, _null(), 1.0, _null(), 0, _null())
     assert rc == _lib.OPUS_ERR_INVALID  # NULL pointers
     assert lib.opus_sketch_table_entries(128, 256) == 16384
