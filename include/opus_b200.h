@@ -102,7 +102,8 @@ OPUS_API int opus_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t
  *   - k <= 262144 (1 MB of counts); larger k is rejected with OPUS_ERR_INVALID.
  *   - The first call on each device looks up the array's address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address is kept per device and per
+ *     context: after cudaDeviceReset the next call looks it up again.
  *   - Every call zeroes the array on its stream before counting.  Calls that
  *     overlap on one device share the array and race: serialise them.
  *   - *out_max (one int64 on the device) is -1 when a bucket lies outside
@@ -110,6 +111,11 @@ OPUS_API int opus_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t
  */
 OPUS_API int opus_bucket_max_load_noalloc(const uint32_t* packed, int64_t numel, int64_t k, int64_t* out_max,
                                           void* stream);
+
+/* P3 — the AdamW diagonal D = 1 / (sqrt(v) + eps) of n second moments, f32,
+ * with torch's correctly rounded sqrt, add and reciprocal
+ * (_inv_rms_tensor_for_param, OPUS/train/data_selection.py:208-214). */
+OPUS_API int opus_adam_diag(const float* exp_avg_sq, float eps, int64_t n, float* out, void* stream);
 
 /* Number of 16-byte entries of the tiled epilogue table for a [d_out,d_in] layer. */
 OPUS_API int64_t opus_sketch_table_entries(int d_out, int d_in);
@@ -274,6 +280,39 @@ OPUS_API int opus_greedy_select_blocks(const float* scores, const float* sim_blo
 /* f32 -> bf16 pair: hi = bf16_rn(x), lo = bf16_rn(x - hi), n elements.
  * Used to feed f32 activations/gradients to the bf16 tensor-core kernels. */
 OPUS_API int opus_split_bf16(const float* x, int64_t n, void* hi, void* lo, void* stream);
+
+/*
+ * K2 Muon — dense bf16 GEMM on tcgen05: C[m,n] (+)= alpha * sum_k
+ * (A[m,k] + A_lo[m,k]) * B[n,k], A [M, K] and B [N, K] bf16 row-major (K
+ * contiguous), A_lo the lo half of an f32 A split with opus_split_bf16 or
+ * NULL.  c_dtype OPUS_DTYPE_BF16 rounds each f32 sum to bf16 (torch's
+ * .to(bfloat16)); OPUS_DTYPE_F32 writes f32 (accumulate adds into C).
+ * K and N multiples of 8; pointers 16-byte aligned.  With B = S^T this is the
+ * candidate transform einsum('...o,po->...p', dLdZ.float(), S.float().T)
+ * (OPUS/train/data_selection.py:495-500, :559-563;
+ * OPUS/train/random_projection.py:158).
+ */
+OPUS_API int opus_gemm_bf16(const void* a, const void* a_lo, const void* b, int M, int N, int K, float alpha,
+                            void* c, int c_dtype, int accumulate, void* stream);
+
+/*
+ * K2 Muon — the preconditioner S = a I + b A + c A^2 with A = m~ m~^T,
+ * m~ = m / ||m||_F, a, b, c = 3.4445, -4.7750, 2.0315, for one momentum
+ * buffer m [d_out, d_in] (f32 or bf16; f32 is rounded to bf16 first), written
+ * as bf16 [d_out, d_out].  Every step rounds to bf16 where torch's bf16
+ * arithmetic does; the identity when ||m|| < 1e-7.  workspace: device memory
+ * of opus_muon_S_workspace_bytes(d_out, d_in) bytes, 256-byte aligned.
+ * d_out, d_in multiples of 8.  Replaces _get_muon_S_matrix
+ * (OPUS/train/data_selection.py:228-252).
+ */
+OPUS_API int64_t opus_muon_S_workspace_bytes(int d_out, int d_in);
+OPUS_API int opus_muon_S(const void* m, int m_dtype, int d_out, int d_in, void* workspace, int64_t workspace_bytes,
+                         void* S, void* stream);
+
+/* Number of kernels this library has launched in the process so far (all
+ * devices).  Instrumentation with no counterpart in the reference: the
+ * difference over a region counts the library's launches in it. */
+OPUS_API int64_t opus_kernel_launches(void);
 
 #ifdef __cplusplus
 }

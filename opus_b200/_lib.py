@@ -52,10 +52,75 @@ SIGNATURES: dict[str, tuple] = {
     "opus_boltzmann_select_blocks": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_f64, _c_p, _c_p, _c_p]),
     "opus_greedy_select_blocks": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_p, _c_p]),
     "opus_split_bf16": (_c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p]),
+    "opus_gemm_bf16": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_f32, _c_p, _c_int, _c_int, _c_p]),
+    "opus_muon_S_workspace_bytes": (_c_i64, [_c_int, _c_int]),
+    "opus_muon_S": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p, _c_p]),
+    "opus_kernel_launches": (_c_i64, []),
+    "opus_adam_diag": (_c_int, [_c_p, _c_f32, _c_i64, _c_p, _c_p]),
 }
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
+_timer = None  # the active KernelTimer, if any
+
+# entry points that launch no kernel of their own or only query state
+_UNTIMED = {"opus_abi_version", "opus_last_error", "opus_device_error", "opus_sketch_table_entries",
+            "opus_muon_S_workspace_bytes", "opus_kernel_launches"}
+
+
+class KernelTimer:
+    """Device time of every library entry point called while it is active.
+
+    Each call is bracketed by two CUDA events recorded on the current stream
+    (the stream the front end launches on), so the figures are the calls'
+    own device durations, taken live inside whatever region is being timed.
+    summary() synchronises and returns {entry point: (calls, total ms)}.
+    """
+
+    def __init__(self):
+        self.records: list = []
+
+    def __enter__(self):
+        global _timer
+        self._prev, _timer = _timer, self
+        return self
+
+    def __exit__(self, *exc):
+        global _timer
+        _timer = self._prev
+        return False
+
+    def summary(self) -> dict:
+        import torch
+
+        torch.cuda.synchronize()
+        out: dict = {}
+        for name, s, e in self.records:
+            n, ms = out.get(name, (0, 0.0))
+            out[name] = (n + 1, ms + s.elapsed_time(e))
+        return out
+
+
+class _TimedLib:
+    """The loaded library with each entry point wrapped in a pair of CUDA events."""
+
+    def __init__(self, lib, timer):
+        self._lib, self._t = lib, timer
+
+    def __getattr__(self, name):
+        fn = getattr(self._lib, name)
+        if not name.startswith("opus_") or name in _UNTIMED:
+            return fn
+        import torch
+
+        def call(*args):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            rc = fn(*args)
+            e.record()
+            self._t.records.append((name, s, e))
+            return rc
+        return call
 
 
 def header_symbols() -> list[str]:
@@ -65,7 +130,12 @@ def header_symbols() -> list[str]:
 
 
 def load() -> ctypes.CDLL:
-    """Load (once) and return the library with argument types declared."""
+    """Load (once) and return the library with argument types declared (timed under a KernelTimer)."""
+    lib = _load()
+    return lib if _timer is None else _TimedLib(lib, _timer)
+
+
+def _load() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib

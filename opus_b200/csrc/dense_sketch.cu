@@ -206,11 +206,13 @@ int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, co
     dense_sketch_smem_kernel<<<(int)grid, kDenseSmemThreads, smem, st>>>(w, transposed, packed, diag, d_out, d_in,
                                                                         row_begin, row_end, static_cast<int>(k),
                                                                         sketch);
+    ::opus::note_launch();
   } else {
     int64_t grid = (int64_t)sm_count() * 8;
     if (grid > n_tiles) grid = n_tiles;
     dense_sketch_kernel<<<(int)grid, kDenseThreads, 0, st>>>(w, transposed, packed, diag, d_out, d_in, row_begin,
                                                              row_end, k, sketch);
+    ::opus::note_launch();
   }
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
@@ -229,6 +231,7 @@ int opus_sketch_dot(const float* phi, const float* tau, int n_rows, int64_t k, f
   const int64_t grid = (int64_t)n_rows * n_chunks;
   if (grid > 0x7fffffff) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_dot: too many rows");
   sketch_dot_kernel<<<(int)grid, 256, 0, st>>>(phi, tau, k, (int)n_chunks, alpha, score);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -241,6 +244,7 @@ int opus_split_bf16(const float* x, int64_t n, void* hi, void* lo, void* stream)
   if (grid > (int64_t)sm_count() * 16) grid = (int64_t)sm_count() * 16;
   split_bf16_kernel<<<(int)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, n, reinterpret_cast<__nv_bfloat16*>(hi), reinterpret_cast<__nv_bfloat16*>(lo));
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -278,6 +278,7 @@ extern "C" int opus_ghost_score(const void* a, const void* dLdZ, int dtype, int 
   const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
   ghost_kernel<<<grid, kThreads, kSmemBytes, st>>>(tm_a, tm_v, tm_g, n_tok, seq_len, d_in, n_nb, alpha, score,
                                                   device_error_word());
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

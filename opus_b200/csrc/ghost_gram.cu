@@ -299,6 +299,7 @@ extern "C" int opus_ghost_gram(const void* a, const void* a_lo, const void* dLdZ
   const int64_t grid = units < sm_count() ? units : sm_count();
   ghost_gram_kernel<<<(int)grid, kGgThreads, smem, st>>>(tm_a, tm_al, tm_g, tm_gl, split, n_rows, n_tb, n_kb_a,
                                                           n_kb_g, stages, units, alpha, S, device_error_word());
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

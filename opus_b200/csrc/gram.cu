@@ -322,6 +322,7 @@ int launch_gram_tc(const float* phi_a, int rows_a, const float* phi_b, int rows_
   const int vec_out = (rows_b % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
   gram_tc_kernel<<<(int)grid, kTcThreads, kTcSmem, st>>>(tm_a, tm_b, rows_a, rows_b, tiles_j, n_tiles, kb_per_split,
                                                         n_kb, alpha, out, vec_out, sym, device_error_word());
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -357,6 +358,7 @@ extern "C" int opus_sketch_gram(const float* phi_a, int rows_a, const float* phi
   if (atomic_out && !accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)rows_a * rows_b * sizeof(float), st));
   dim3 grid(tj, ti, (unsigned)splits);
   gram_kernel<<<grid, kGThreads, 0, st>>>(phi_a, rows_a, phi_b, rows_b, k, kps, alpha, out, accumulate, atomic_out);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -1,6 +1,7 @@
 // Library-wide state of libopus_b200.so: error reporting, the per-device
 // error word that bounded device waits write into, device properties and
 // TMA descriptor encoding.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -21,6 +22,8 @@ int* g_dev_err[kMaxDevices] = {nullptr};
 int g_sm_count[kMaxDevices] = {0};
 int g_smem_optin[kMaxDevices] = {0};
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+PFN_cuCtxGetCurrent_v4000 g_ctx_get_current = nullptr;
+std::atomic<int64_t> g_launches{0};
 
 int current_device() {
   int dev = 0;
@@ -40,6 +43,8 @@ int set_error(int code, const char* fmt, ...) {
 int cuda_fail(cudaError_t e, const char* what) {
   return set_error(OPUS_ERR_CUDA, "%s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int* device_error_word() {
   const int dev = current_device();
@@ -74,6 +79,22 @@ int max_smem_optin() {
     g_smem_optin[dev] = n > 0 ? n : 232448;
   }
   return g_smem_optin[dev];
+}
+
+int current_context(CUcontext* ctx) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_ctx_get_current == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
+        return set_error(OPUS_ERR_CUDA, "cannot resolve cuCtxGetCurrent");
+      g_ctx_get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    }
+  }
+  if (g_ctx_get_current(ctx) != CUDA_SUCCESS) return set_error(OPUS_ERR_CUDA, "cuCtxGetCurrent failed");
+  return OPUS_OK;
 }
 
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
@@ -129,11 +150,14 @@ int opus_selftest_stalled_wait(void* stream) {
   int* err = opus::device_error_word();
   if (err == nullptr) return opus::set_error(OPUS_ERR_CUDA, "device error word unavailable");
   opus::stalled_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(err);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
 
 int opus_abi_version(void) { return OPUS_ABI_VERSION; }
+
+int64_t opus_kernel_launches(void) { return opus::g_launches.load(std::memory_order_relaxed); }
 
 const char* opus_last_error(void) { return opus::g_last_error; }
 

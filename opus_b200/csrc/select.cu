@@ -2,10 +2,13 @@
 // interaction penalty on one CTA (128 to 1024 threads, chosen by the candidate
 // count; the Boltzmann sampler keeps each thread's candidates in registers,
 // the greedy one keeps the scores in shared memory).  The float32 / float64
-// operation order follows numpy so the same uniforms give the same indices as
-// the host implementation:
+// operation order follows numpy, so the same uniforms give the same indices as
+// the host implementation except where numpy's float32 exp and the correctly
+// rounded one differ: numpy's vectorised exp is off by one ulp for a share of
+// inputs, which moves each cdf entry by a few ulps, so a pick can differ only
+// when u falls that close to a cdf entry:
 //   - scaled = score / T in float32, shifted by its max only if max > 700;
-//   - p = exp(scaled) rounded to float32 (computed in double);
+//   - p = exp(scaled) rounded to float32 (computed in double, correctly rounded);
 //   - sum = numpy's pairwise float32 sum (0 + blocks of <=128 with 8
 //     accumulators, halves rounded down to a multiple of 8);
 //   - p /= sum in float32, or 1/m when the sum is 0 or not finite;
@@ -533,6 +536,7 @@ int launch_boltzmann(const float* scores, const float* sim, int n, int block, in
     OPUS_LAUNCH_BOLTZMANN(1024, 8);
   }
 #undef OPUS_LAUNCH_BOLTZMANN
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -561,6 +565,7 @@ int launch_greedy(const float* scores, const float* sim, int n, int block, int n
     OPUS_LAUNCH_GREEDY(1024);
   }
 #undef OPUS_LAUNCH_GREEDY
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

@@ -656,6 +656,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
       tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_ob, n_cb,
       jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
       accumulate);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -705,6 +706,7 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
   sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_ob,
                                                             n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
                                                             err, /*dense*/ 1, diag, d_out, d_in, accumulate);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

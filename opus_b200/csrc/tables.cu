@@ -130,6 +130,24 @@ __global__ void desketch_kernel(const float* __restrict__ tau, const uint32_t* _
   }
 }
 
+// D = 1 / (sqrt(v) + eps) elementwise, 16-byte loads and stores when aligned.
+__global__ void adam_diag_kernel(const float* __restrict__ v, float eps, int64_t n, float* __restrict__ out,
+                                 int vec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t start = 0;
+  if (vec) {
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const float4 q = __ldcs(reinterpret_cast<const float4*>(v) + i);
+      __stcs(reinterpret_cast<float4*>(out) + i,
+             make_float4(adam_diag(q.x, eps), adam_diag(q.y, eps), adam_diag(q.z, eps), adam_diag(q.w, eps)));
+    }
+    start = n4 * 4;
+  }
+  for (int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = adam_diag(v[i], eps);
+}
+
 int grid_for(int64_t n, int threads) {
   int64_t g = (n + threads - 1) / threads;
   const int64_t cap = (int64_t)sm_count() * 16;
@@ -220,13 +238,16 @@ int launch_bucket_max_load(const uint32_t* packed, int64_t numel, int64_t k, int
       OPUS_CUDA_TRY(cudaFuncSetAttribute(bucket_hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
       bucket_hist_kernel<true><<<(int)grid, kHistThreads, smem, st>>>(packed, numel, (uint32_t)k, counts, err);
+      ::opus::note_launch();
     } else {
       bucket_hist_kernel<false><<<grid_for(numel / 4 + 1, kHistThreads), kHistThreads, 0, st>>>(
           packed, numel, (uint32_t)k, counts, err);
+      ::opus::note_launch();
     }
     OPUS_CUDA_TRY(cudaGetLastError());
   }
   bucket_max_kernel<<<1, 1024, 0, st>>>(counts, k, out_max);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -243,6 +264,9 @@ constexpr int kNoAllocMaxDevices = 64;
 
 std::mutex g_noalloc_mu;
 int* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+// the context each cached address belongs to: after cudaDeviceReset the
+// module is loaded again into a new context and the address is looked up anew
+CUcontext g_noalloc_ctx[kNoAllocMaxDevices] = {nullptr};
 
 }  // namespace
 
@@ -251,17 +275,23 @@ static __device__ __align__(256) int g_noalloc_scratch[kNoAllocCountsOffset + kN
 namespace {
 
 // Device address of the static scratch for the current device, looked up by
-// the first call on that device and cached.
+// the first call on that device (in its current context) and cached.
 int noalloc_scratch(int** out) {
   int dev = 0;
   OPUS_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kNoAllocMaxDevices)
     return set_error(OPUS_ERR_UNSUPPORTED, "bucket_max_load_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
+  CUcontext ctx = nullptr;
+  int rc = current_context(&ctx);
+  if (rc != OPUS_OK) return rc;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
-    OPUS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    OPUS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));  // makes the primary context current if none was
+    rc = current_context(&ctx);
+    if (rc != OPUS_OK) return rc;
     g_noalloc_ptr[dev] = static_cast<int*>(p);
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return OPUS_OK;
@@ -302,13 +332,16 @@ int launch_bucket_max_load_noalloc(const uint32_t* packed, int64_t numel, int64_
       OPUS_CUDA_TRY(cudaFuncSetAttribute(bucket_hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
       bucket_hist_kernel<true><<<(int)grid, kHistThreads, smem, st>>>(packed, numel, (uint32_t)k, counts, bad);
+      ::opus::note_launch();
     } else {
       bucket_hist_kernel<false><<<grid_for(numel / 4 + 1, kHistThreads), kHistThreads, 0, st>>>(
           packed, numel, (uint32_t)k, counts, bad);
+      ::opus::note_launch();
     }
     OPUS_CUDA_TRY(cudaGetLastError());
   }
   bucket_max_flagged_kernel<<<1, 1024, 0, st>>>(counts, k, bad, out_max);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -327,6 +360,7 @@ int opus_pack_hash_sign(const int64_t* hash, const float* sign, int64_t numel, i
   if (!hash || !sign || !packed) return set_error(OPUS_ERR_INVALID, "pack: NULL pointer");
   int* err = device_error_word();
   pack_kernel<<<grid_for(numel, 256), 256, 0, (cudaStream_t)stream>>>(hash, sign, numel, k, packed, err);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -348,6 +382,7 @@ int opus_build_sketch_table(const uint32_t* packed, const float* diag, const flo
   const int blocks = n_ob * n_cb * kChunksPerTile;
   build_table_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(packed, diag, exp_avg_sq, eps, d_out, d_in, n_cb,
                                                               reinterpret_cast<uint4*>(table));
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }
@@ -364,6 +399,19 @@ int opus_desketch(const float* tau, const uint32_t* packed, const float* diag, c
   const int vec = (al & 15) == 0 && (reinterpret_cast<uintptr_t>(hi) & 7) == 0 && (reinterpret_cast<uintptr_t>(lo) & 7) == 0;
   desketch_kernel<<<grid_for(vec ? numel / 4 + 1 : numel, 256), 256, 0, (cudaStream_t)stream>>>(
       tau, packed, diag, exp_avg_sq, eps, numel, scale, hi, lo, vec);
+  ::opus::note_launch();
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+int opus_adam_diag(const float* exp_avg_sq, float eps, int64_t n, float* out, void* stream) {
+  if (n < 0) return set_error(OPUS_ERR_INVALID, "adam_diag: negative size");
+  if (n == 0) return OPUS_OK;
+  if (!exp_avg_sq || !out) return set_error(OPUS_ERR_INVALID, "adam_diag: NULL pointer");
+  const int vec = ((reinterpret_cast<uintptr_t>(exp_avg_sq) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  adam_diag_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, (cudaStream_t)stream>>>(exp_avg_sq, eps, n, out,
+                                                                                       vec);
+  ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
 }

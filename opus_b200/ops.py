@@ -107,6 +107,15 @@ def build_sketch_table(packed: torch.Tensor, d_out: int, d_in: int, diag: torch.
     return out
 
 
+def adam_diag(exp_avg_sq: torch.Tensor, eps: float = 1e-8) -> torch.Tensor:
+    """The AdamW diagonal 1 / (sqrt(v) + eps) in f32, elementwise, same shape as v."""
+    _cuda(exp_avg_sq, "exp_avg_sq")
+    v = _contig(exp_avg_sq.to(torch.float32))
+    out = torch.empty_like(v)
+    _lib.check(_lib.load().opus_adam_diag(_ptr(v), float(eps), v.numel(), _ptr(out), _stream(v)), "opus_adam_diag")
+    return out
+
+
 # --------------------------------------------------------------------- stage 3
 def split_bf16(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     _cuda(x, "x")
@@ -373,6 +382,119 @@ def sketch_gram(phi_a: torch.Tensor, phi_b: torch.Tensor | None = None, alpha: f
     _lib.check(_lib.load().opus_sketch_gram(_ptr(phi_a), ra, _ptr(phi_b), rb, k, float(alpha), _ptr(out),
                                            int(accumulate), _stream(phi_a)), "opus_sketch_gram")
     return out
+
+
+# --------------------------------------------------------------------- stage 4 (Muon)
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
+              a_lo: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              accumulate: bool = False) -> torch.Tensor:
+    """C = alpha * (a (+ a_lo)) @ b^T on the tensor cores: a [M, K], b [N, K] bf16, f32 accumulation.
+
+    out_dtype bfloat16 rounds every f32 sum once (torch's .to(bfloat16));
+    float32 keeps it (accumulate adds into out).  K and N multiples of 8.
+    """
+    _cuda(a, "a")
+    _cuda(b, "b")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError(f"gemm_bf16: a [M, K] and b [N, K] expected, got {tuple(a.shape)}, {tuple(b.shape)}")
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or (a_lo is not None and a_lo.dtype != torch.bfloat16):
+        raise ValueError("gemm_bf16: operands must be bf16")
+    if a_lo is not None and a_lo.shape != a.shape:
+        raise ValueError("gemm_bf16: a_lo must have a's shape")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("gemm_bf16: out_dtype must be bfloat16 or float32")
+    M, K = a.shape
+    N = b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+        accumulate = False
+    if out.dtype != out_dtype or not out.is_contiguous() or out.numel() < M * N:
+        raise ValueError(f"out must be a contiguous {out_dtype} tensor of at least [M, N]")
+    if M == 0:
+        return out
+    dt = _lib.DTYPE_BF16 if out_dtype == torch.bfloat16 else _lib.DTYPE_F32
+    a, b = _contig(a), _contig(b)
+    a_lo = None if a_lo is None else _contig(a_lo)
+    _lib.check(_lib.load().opus_gemm_bf16(_ptr(a), _ptr(a_lo), _ptr(b), M, N, K, float(alpha), _ptr(out), dt,
+                                         int(accumulate), _stream(a)), "opus_gemm_bf16")
+    return out
+
+
+def muon_S(m: torch.Tensor) -> torch.Tensor:
+    """Muon preconditioner S = a I + b A + c A^2, A = m~ m~^T, m~ = m / ||m||, as bf16 [d_out, d_out].
+
+    m: the momentum buffer [d_out, d_in] (f32 or bf16; other dtypes are cast
+    to bf16 first, as the reference does).  Every step rounds to bf16 where
+    the reference's bf16 torch arithmetic does; the identity when
+    ||m|| < 1e-7.  Widths that are not multiples of 8 are zero-padded (zero
+    rows and columns change neither the norm nor the valid block of S).
+    """
+    _cuda(m, "m")
+    if m.dim() != 2:
+        raise ValueError(f"muon_S: momentum buffer must be 2-D, got {tuple(m.shape)}")
+    if m.dtype not in (torch.float32, torch.bfloat16):
+        m = m.to(torch.bfloat16)
+    d_out, d_in = m.shape
+    do_p, di_p = (d_out + 7) // 8 * 8, (d_in + 7) // 8 * 8
+    if (do_p, di_p) != (d_out, d_in):
+        m = torch.nn.functional.pad(m, (0, di_p - d_in, 0, do_p - d_out))
+    m = _contig(m)
+    lib = _lib.load()
+    ws_bytes = int(lib.opus_muon_S_workspace_bytes(do_p, di_p))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=m.device)
+    S = torch.empty(do_p, do_p, dtype=torch.bfloat16, device=m.device)
+    dt = _lib.DTYPE_F32 if m.dtype == torch.float32 else _lib.DTYPE_BF16
+    _lib.check(lib.opus_muon_S(_ptr(m), dt, do_p, di_p, _ptr(ws), ws_bytes, _ptr(S), _stream(m)), "opus_muon_S")
+    return S if do_p == d_out else S[:d_out, :d_out].contiguous()
+
+
+def muon_transform(dLdZ: torch.Tensor, S: torch.Tensor, symmetric: bool = False) -> torch.Tensor:
+    """einsum('...o,po->...p', dLdZ.float(), S.float().T).to(dLdZ.dtype) on the tensor cores.
+
+    The Muon candidate transform (data_selection.py:495-500): out[..., p] =
+    sum_o dLdZ[..., o] S[o, p].  bf16 dLdZ with a bf16 S is one GEMM with a
+    bf16 output; f32 dLdZ is split into bf16 hi/lo (two products, f32
+    output); an f32 S that bf16 does not hold exactly is split as well.
+    symmetric=True skips the transpose of S (the S of muon_S is symmetric).
+    """
+    _cuda(dLdZ, "dLdZ")
+    _cuda(S, "S")
+    d_out = dLdZ.shape[-1]
+    if S.shape != (d_out, d_out):
+        raise ValueError(f"S must be [{d_out}, {d_out}], got {tuple(S.shape)}")
+    lead = dLdZ.shape[:-1]
+    g = dLdZ.reshape(-1, d_out)
+    Bm = S if symmetric else S.t()
+    p = (d_out + 7) // 8 * 8
+    if p != d_out:
+        g = torch.nn.functional.pad(g, (0, p - d_out))
+        Bm = torch.nn.functional.pad(Bm, (0, p - d_out, 0, p - d_out))
+    Bm = _contig(Bm)
+    if Bm.dtype == torch.bfloat16:
+        b_hi, b_lo = Bm, None
+    else:
+        b_hi, b_lo = split_bf16(Bm)
+        if not bool(torch.any(b_lo != 0)):
+            b_lo = None
+    if g.dtype == torch.bfloat16 and b_lo is None:
+        out = gemm_bf16(g, b_hi, out_dtype=torch.bfloat16)
+    else:
+        if g.dtype == torch.bfloat16:
+            g_hi, g_lo = _contig(g), None
+        else:
+            g_hi, g_lo = split_bf16(g)
+        out = gemm_bf16(g_hi, b_hi, out_dtype=torch.float32, a_lo=g_lo)
+        if b_lo is not None:
+            gemm_bf16(g_hi, b_lo, out_dtype=torch.float32, out=out, accumulate=True)
+        out = out.to(dLdZ.dtype)
+    if p != d_out:
+        out = out[:, :d_out]
+    return out.reshape(*lead, d_out)
+
+
+def kernel_launches() -> int:
+    """Kernels the library has launched in this process so far."""
+    return int(_lib.load().opus_kernel_launches())
 
 
 # --------------------------------------------------------------------- stage 5

@@ -187,27 +187,18 @@ def global_C_t_muon(optimizer, p):
     return torch.tensor(_C_t_muon_value(optimizer, p), dtype=torch.float32, device=p.device)
 
 
-_MUON_COEFFS = (3.4445, -4.7750, 2.0315)
-
-
 def _get_muon_S_matrix(p, optimizer):
     """S = a I + b A + c A^2 with A = m~ m~^T, m~ = m/||m|| in bf16 (data_selection.py:228-252).
 
-    Identity when the parameter has no momentum buffer or ||m|| < 1e-7.
+    Identity when the parameter has no momentum buffer or ||m|| < 1e-7.  The
+    norm, the normalisation, both GEMMs and the combination run in
+    ops.muon_S (tcgen05 GEMMs rounding to bf16 where the reference's bf16
+    torch ops round); the norm test happens on the device, so no host sync.
     """
     state = optimizer.state.get(p, None)
-    n = p.shape[0]
-    eye = torch.eye(n, dtype=torch.bfloat16, device=p.device)
     if state is None or "momentum_buffer" not in state:
-        return eye
-    m = state["momentum_buffer"].to(dtype=torch.bfloat16)
-    norm = torch.norm(m)
-    if norm < 1e-7:
-        return eye
-    mt = m / norm
-    A = mt @ mt.T
-    a, b, c = _MUON_COEFFS
-    return a * eye + b * A + c * (A @ A)
+        return torch.eye(p.shape[0], dtype=torch.bfloat16, device=p.device)
+    return ops.muon_S(state["momentum_buffer"].to(device=p.device))
 
 
 def weighted_grad_dotprod(A1, B1, A2, B2, diagonal_weight: torch.Tensor, weight_rhs: bool = False,
@@ -484,7 +475,8 @@ class _PrecondTables:
             if opt_p is not None:
                 eff = _group_kind(_find_group_for_param(opt_p, p)) if self.auto_mode else self.preconditioner
                 if eff == "muon" and p in self.S_map:
-                    g_t = (g_t.float() @ self.S_map[p].to(g_t.device).float()).to(g_t.dtype)
+                    # dLdZ_t <- einsum('...o,po->...p', dLdZ_t, S^T) (data_selection.py:495-500)
+                    g_t = ops.muon_transform(g_t, self.S_map[p].to(g_t.device), symmetric=True)
                     scale = self.muon_scale[p]
                 elif eff == "adamw" and p in self.adamw:
                     scale, group_p, state_p = self.adamw[p]
@@ -586,6 +578,18 @@ def _score_and_similarity(model, device, batch_train, validation_loader, optimiz
     """Device tensors (score [B] or [B, n], sim [B, B] or None) for one window."""
     batch_val = _sample_proxy_batch_for_step(validation_loader)  # one proxy batch per round, whichever mode
     if CAPTURE_MODE == "stream":
+        rows = batch_train["input_ids"].shape[0] + batch_val["input_ids"].shape[0]
+        seq = min(batch_train["input_ids"].shape[1], batch_val["input_ids"].shape[1], score_len or 1 << 30)
+        if _use_passes(rows, trainable_layers, seq, device):
+            score, phis, cs, _ = capture_in_passes(model, device, batch_train, batch_val, optimizer,
+                                                   trainable_layers, preconditioner, score_len, per_val=per_val,
+                                                   keep_sketches=with_similarity)
+            sim = None
+            if with_similarity:
+                sim = torch.zeros(phis.shape[1], phis.shape[1], device=device, dtype=torch.float32)
+                for pid in range(phis.shape[0]):
+                    ops.sketch_gram(phis[pid], alpha=cs[pid] * cs[pid], out=sim, accumulate=True)
+            return score, sim
         out = _score_and_similarity_stream(model, device, batch_train, batch_val, optimizer, trainable_layers,
                                            preconditioner, score_len, per_val, with_similarity)
         if out is not None:
@@ -603,7 +607,7 @@ def _score_and_similarity(model, device, batch_train, validation_loader, optimiz
 
 
 def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_layers, preconditioner, score_len,
-                   make_handler):
+                   make_handler, precond: dict | None = None):
     """Capture forward, then one backward whose per-layer hooks hand each (dL/dZ, A) pair to a handler.
 
     The backward pass is asked only for the gradient of the first kept
@@ -614,7 +618,9 @@ def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_l
     their pair id, which follows the forward order as in the batch capture.
     Returns False when a layer's hook did not fire (a captured output the
     loss does not reach, or no usable root): the caller then falls back to the
-    batch capture.
+    batch capture.  precond: a dict that keeps the preconditioner state
+    (Muon S matrices, AdamW scalars) across the passes of one round; it is
+    filled by the first pass that gets it.
     """
     loss, layers_kept, z_list, train_bs, val_bs = _capture_forward(
         model, dict(batch_train), None, trainable_layers, score_len, batch_val)
@@ -627,7 +633,11 @@ def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_l
         pid_base.append(len(params))
         names = ("lora_A", "lora_B") if _pairs_per_layer(layer) == 2 else ()
         params.extend([getattr(layer, n) for n in names] or [getattr(layer, "weight", None)])
-    tables = _PrecondTables(params, optimizer, preconditioner)
+    tables = None if precond is None else precond.get("tables")
+    if tables is None:
+        tables = _PrecondTables(params, optimizer, preconditioner)
+        if precond is not None:
+            precond["tables"] = tables
     on_plan = make_handler(train_bs, val_bs, len(params))
     fired = [False] * len(layers_kept)
     bad = []
@@ -681,16 +691,169 @@ def _score_and_similarity_stream(model, device, batch_train, batch_val, optimize
     return out["score"], out["sim"]
 
 
+# Sequences per capture pass.  None: as many as the device's free memory
+# holds (rows_per_pass); an int forces that many (tests use it to run the
+# pass-splitting path at small sizes).
+CAPTURE_ROWS: int | None = None
+# Share of the free device memory a capture pass may fill with activations.
+CAPTURE_MEMORY_FRACTION = 0.75
+# Activation bytes per token of a capture pass, in units of one (d_in + d_out)
+# row per capture layer in the model dtype (measured peaks: about 1.0 for
+# GPT-2 small in f32 and bf16, about 0.8 for GPT-2 XL in bf16; the margin
+# covers the logits and the allocator's fragmentation).
+CAPTURE_BYTES_PER_ROW = 1.25
+
+
+def rows_per_pass(trainable_layers, seq_len: int, device, reserve_bytes: int = 0) -> int:
+    """Sequences one capture forward + backward can hold on the device.
+
+    A pass keeps every layer's activations alive until its backward hook has
+    run; measured on GPT-2-shaped models the peak is about one
+    (d_in + d_out) row per token per capture layer, in the model dtype, plus
+    the logits.  The estimate takes CAPTURE_BYTES_PER_ROW times that per token
+    against CAPTURE_MEMORY_FRACTION of the free memory, after reserve_bytes
+    for what the round keeps (its candidate sketches).
+    """
+    if CAPTURE_ROWS is not None:
+        return max(1, int(CAPTURE_ROWS))
+    device = torch.device(device)
+    if device.type != "cuda":
+        return 1 << 30
+    per_tok = 0
+    for layer in trainable_layers:
+        w = getattr(layer, "weight", None)
+        if isinstance(w, torch.Tensor) and w.dim() == 2:
+            per_tok += (w.shape[0] + w.shape[1]) * w.element_size()
+    per_tok = max(1, int(CAPTURE_BYTES_PER_ROW * per_tok))
+    free, _ = torch.cuda.mem_get_info(device)
+    free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+    budget = CAPTURE_MEMORY_FRACTION * free - reserve_bytes
+    return max(1, int(budget // (per_tok * max(1, seq_len))))
+
+
+def _use_passes(rows: int, trainable_layers, seq_len: int, device) -> bool:
+    projector = get_projector()
+    if projector is None or not projector.enabled:
+        return False  # the projection-off similarity needs every candidate's factors at once
+    reserve = 4 * projector.sketch_dim * rows * 2 * len(trainable_layers)
+    return rows > rows_per_pass(trainable_layers, seq_len, device, reserve)
+
+
+def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainable_layers, preconditioner, score_len,
+                      per_val=False, keep_sketches=True, reduce_targets=None, n_proxy_total=None):
+    """Scores of a round whose candidates and proxies are captured in several forward/backward passes.
+
+    The reference runs one forward and one backward over candidates and
+    proxies together (data_selection.py:355-406); at GPT-2-XL widths that
+    holds hundreds of GB of activations.  Per-sample gradients do not depend
+    on which other samples share the batch (the batch-mean gradient is scaled
+    back by the batch size, linear.py:118-119), so the rows are split:
+
+    1. proxy passes: each layer's proxy sketches summed into one target row
+       per layer, taus [L, k] (per_val: the proxy sketches [L, n, k]);
+       reduce_targets(taus), when given, sums the ranks' partial targets;
+    2. candidate passes: each layer's candidate sketches (AdamW diagonal in
+       the table, Muon transform applied) scored against the layer's target,
+       score += c_l / n * phi_l . tau_l, and kept in phis [L, B, k] when
+       keep_sketches, for the similarity sum_l c_l^2 phi_l phi_l^T.
+
+    Rows per pass come from rows_per_pass.  The preconditioner state (Muon S)
+    is built once per round.  Returns (score [B] or [B, n], phis or None,
+    per-layer scales c_l, taus).  Needs the CountSketch projector.
+    """
+    projector = get_projector()
+    if projector is None or not projector.enabled:
+        raise ValueError("capture in passes needs the CountSketch projector (initialize_projector(enabled=True))")
+    k = projector.sketch_dim
+    B = batch_train["input_ids"].shape[0]
+    n = batch_val["input_ids"].shape[0] if batch_val is not None else 0
+    n_total = n if n_proxy_total is None else int(n_proxy_total)
+    seq = min(batch_train["input_ids"].shape[1], score_len or 1 << 30)
+    reserve = 4 * k * (B + n) * 2 * len(trainable_layers)
+    step = rows_per_pass(trainable_layers, seq, device, reserve)
+    precond: dict = {}
+    st: dict = {}
+
+    def rows_of(batch, lo, hi):
+        return {key: v[lo:hi] for key, v in batch.items()}
+
+    empty_train = rows_of(batch_train, 0, 0)
+    empty_val = rows_of(batch_train, 0, 0) if batch_val is None else rows_of(batch_val, 0, 0)
+
+    def ensure(n_plans):
+        if "taus" not in st:
+            st["taus"] = (torch.zeros(n_plans, n, k, device=device, dtype=torch.float32) if per_val else
+                          torch.zeros(n_plans, k, device=device, dtype=torch.float32))
+            st["cs"] = [0.0] * n_plans
+
+    # 1. proxy passes
+    for lo in range(0, n, step):
+        hi = min(n, lo + step)
+
+        def proxy_handler(train_bs, val_bs, n_plans, lo=lo, hi=hi):
+            ensure(n_plans)
+
+            def on_plan(pl):
+                g_v, a_v = (pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)) if pl.g_v.dim() == 2 else (pl.g_v, pl.a_v)
+                if per_val:
+                    projector.sketch(g_v, a_v, pl.pid, out=st["taus"][pl.pid, lo:hi])
+                else:
+                    projector.sketch(g_v, a_v, pl.pid, rows_div=g_v.shape[0], out=st["taus"][pl.pid:pl.pid + 1],
+                                     accumulate=True)
+            return on_plan
+
+        if not stream_capture(model, device, empty_train, rows_of(batch_val, lo, hi), optimizer, trainable_layers,
+                              preconditioner, score_len, proxy_handler, precond):
+            raise RuntimeError("capture in passes: a capture layer's backward hook did not fire")
+    if reduce_targets is not None:
+        if "taus" not in st:  # this rank holds no proxy rows: learn the layer count from the first candidate pass
+            st["defer_reduce"] = True
+        else:
+            reduce_targets(st["taus"])
+
+    # 2. candidate passes
+    score = torch.zeros((B, n) if per_val else (B,), device=device, dtype=torch.float32)
+    for lo in range(0, B, step):
+        hi = min(B, lo + step)
+
+        def cand_handler(train_bs, val_bs, n_plans, lo=lo, hi=hi):
+            ensure(n_plans)
+            if st.pop("defer_reduce", False):
+                reduce_targets(st["taus"])
+            if keep_sketches and "phis" not in st:
+                st["phis"] = torch.zeros(n_plans, B, k, device=device, dtype=torch.float32)
+
+            def on_plan(pl):
+                g_t, a_t = (pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1)) if pl.g_t.dim() == 2 else (pl.g_t, pl.a_t)
+                st["cs"][pl.pid] = pl.c
+                out = st["phis"][pl.pid, lo:hi] if keep_sketches else None
+                phi = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps, out=out)
+                if per_val:
+                    ops.sketch_gram(phi, st["taus"][pl.pid], alpha=pl.c, out=score[lo:hi], accumulate=True)
+                elif n_total > 0:
+                    ops.sketch_dot(phi, st["taus"][pl.pid], alpha=pl.c / n_total, out=score[lo:hi],
+                                   accumulate=True)
+            return on_plan
+
+        if not stream_capture(model, device, rows_of(batch_train, lo, hi), empty_val, optimizer, trainable_layers,
+                              preconditioner, score_len, cand_handler, precond):
+            raise RuntimeError("capture in passes: a capture layer's backward hook did not fire")
+    return score, st.get("phis"), st.get("cs", []), st.get("taus")
+
+
 def ops_inv_rms(v: torch.Tensor, eps: float) -> torch.Tensor:
-    """1/(sqrt(v)+eps) in float32 (the AdamW diagonal, data_selection.py:208-214)."""
-    return (v.float().sqrt() + eps).reciprocal()
+    """1/(sqrt(v)+eps) in float32 (the AdamW diagonal, data_selection.py:208-214), on the device."""
+    return ops.adam_diag(v, eps)
 
 
 def _score_dense(g_t, a_t, g_v, a_v, v_sq, eps, c, per_val, score):
     """Projection-off scores via the ghost kernel against the dense proxy target.
 
-    score_b += c * <D o G_b, mean_j G_vj> (per_val: one column per proxy j);
-    the proxy gradient sum G_v^T A_v over all proxy tokens is a plain GEMM.
+    score_b += c * <D o G_b, mean_j G_vj> = c / n * <G_b, D o sum_j G_vj>
+    (weighted_grad_dotprod / grad_dotprod, data_selection.py:255-292,
+    597-619; per_val: one column per proxy j).  The target D o sum_j G_vj is
+    the per-sample-gradient kernel run over all proxy tokens as one sample
+    (its dense epilogue applies D); D comes from ops.adam_diag.
     """
     d_out, d_in = g_t.shape[2], a_t.shape[2]
     n = g_v.shape[0]
@@ -700,20 +863,20 @@ def _score_dense(g_t, a_t, g_v, a_v, v_sq, eps, c, per_val, score):
     gt_p, at_p = _pad8(g_t), _pad8(a_t)
     do_p, di_p = gt_p.shape[2], at_p.shape[2]
 
-    def target(gv, av):
-        w = gv.float().reshape(-1, d_out).T @ av.float().reshape(-1, d_in)
-        if diag is not None:
-            w = w * diag
+    def pair(w):  # f32 target [d_out * d_in] -> bf16 (hi, lo) pair at the kernel's widths
+        w = w.view(d_out, d_in)
         if (do_p, di_p) != (d_out, d_in):
             w = torch.nn.functional.pad(w, (0, di_p - d_in, 0, do_p - d_out))
         return ops.dense_target_pair(w)
 
     if per_val:
+        targets = ops.per_sample_grad(g_v, a_v, diag=diag)
         for j in range(n):
-            col = ops.ghost_score(at_p, gt_p, target(g_v[j:j + 1], a_v[j:j + 1]), alpha=c)
-            score[:, j] += col
+            score[:, j] += ops.ghost_score(at_p, gt_p, pair(targets[j]), alpha=c)
     else:
-        ops.ghost_score(at_p, gt_p, target(g_v, a_v), alpha=c / n, out=score, accumulate=True)
+        T = g_v.shape[1]
+        w = ops.per_sample_grad(g_v.reshape(1, n * T, d_out), a_v.reshape(1, n * T, d_in), diag=diag)
+        ops.ghost_score(at_p, gt_p, pair(w[0]), alpha=c / n, out=score, accumulate=True)
 
 
 def _pad8(x):

@@ -274,6 +274,20 @@ def score_shard(model, device, batch_train, proxy_share, n_proxy_total, optimize
             return pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1), pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)
         return pl.g_t, pl.a_t, pl.g_v, pl.a_v
 
+    rows = batch_train["input_ids"].shape[0] + (proxy_share["input_ids"].shape[0] if proxy_share else 0)
+    seq = min(batch_train["input_ids"].shape[1], score_len or 1 << 30)
+    if ds.CAPTURE_MODE == "stream" and ds._use_passes(rows, trainable_layers, seq, device):
+        # the rank's rows do not fit one capture: proxy passes, one all-reduce, candidate passes
+        score, phis, cs, _ = ds.capture_in_passes(
+            model, device, batch_train, proxy_share, optimizer, trainable_layers, preconditioner, score_len,
+            reduce_targets=lambda t: allreduce_target_sketches(t, group), n_proxy_total=n_proxy_total)
+        b = phis.shape[1]
+        sim = torch.zeros(b, b * world if exact_similarity else b, device=device, dtype=torch.float32)
+        for pid in range(phis.shape[0]):
+            other = gather_sketches(phis[pid], group) if exact_similarity else phis[pid]
+            ops.sketch_gram(phis[pid], other, alpha=cs[pid] * cs[pid], out=sim, accumulate=True)
+        return score, sim
+
     state = {}
 
     def make_handler(train_bs, val_bs, n_plans):

@@ -139,8 +139,8 @@ class GradientProjector:
         """
         if not self.enabled:
             raise ValueError("Projector is disabled but project_full_gradient was called")
-        if preconditioner_S is not None:
-            dLdZ = (dLdZ.float() @ preconditioner_S.float()).to(dLdZ.dtype)
+        if preconditioner_S is not None:  # random_projection.py:155-158, on the tensor cores
+            dLdZ = ops.muon_transform(dLdZ, preconditioner_S.to(dLdZ.device))
         if dLdZ.dim() == 2:
             dLdZ, a = dLdZ.unsqueeze(1), a.unsqueeze(1)
         elif dLdZ.dim() != 3:

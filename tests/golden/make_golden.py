@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference's OPUS package, runs its own functions on seeded
 synthetic inputs on the CPU and writes the inputs and outputs next to this
@@ -408,7 +408,7 @@ def gen_muon(ds):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout (gszfwsb/OPUS)")
     ap.add_argument("--only", default=None, help="regenerate one fixture family (e.g. lora)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)

@@ -48,6 +48,11 @@ def _rank_worker(rank, world, port, scenario, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.set_num_threads(1)
+    from opus_b200 import ops
+    from oracle import reference_torch as rt
+
+    # CPU ranks: the Muon S and transform from the reference's torch recipe (the kernels need a GPU)
+    ops.muon_S, ops.muon_transform = rt.muon_S, rt.muon_transform
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
         g = load_golden(f"wholepath_{scenario}")

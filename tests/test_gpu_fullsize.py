@@ -5,6 +5,10 @@ size-independent properties, where the float64 oracle would take minutes (GPU).
 - Summing candidates into one row (rows_div) equals the column sum of their rows.
 - The ghost contraction against the de-sketched target equals phi . tau of the sketches.
 - The fixed-point shared sketch equals the f32 global-atomic path.
+
+And sampled rows of full-size launches against the float64 oracle: rows are
+independent, so a few rows check the full launch's job dealing and
+per-candidate scales at a fraction of the oracle's cost.
 """
 import numpy as np
 import pytest
@@ -68,3 +72,54 @@ def test_ghost_identity_at_full_size(operator):
     sim = ops.sketch_gram(o["phi"])
     assert rel(sim, (o["phi"].double() @ o["phi"].double().T)) < 2e-5
     assert torch.allclose(sim, sim.T, rtol=1e-5, atol=1e-5 * float(sim.abs().max()))
+
+
+def _oracle_rows(dz, a, h, s, k, diag, rows):
+    """float64 oracle sketches of the given candidates (the reference's project_full_gradient)."""
+    from oracle import opus_oracle as orc
+
+    d = None if diag is None else diag.cpu().numpy()
+    return np.stack([orc.project_full_gradient(dz[b:b + 1].float().cpu().numpy(), a[b:b + 1].float().cpu().numpy(),
+                                               h, s, k, diag=d)[0] for b in rows])
+
+
+def _check_rows(got, want, what):
+    """Each sampled row within 1e-4 of its largest bucket; the rows' Gram (a similarity block) within 1e-3."""
+    for i in range(want.shape[0]):
+        err = np.abs(got[i] - want[i]).max() / np.abs(want[i]).max()
+        assert err < 1e-4, f"{what} row {i}: {err:.3e}"
+    gram_got, gram_want = got @ got.T, want @ want.T
+    diag_err = np.abs(np.diag(gram_got) - np.diag(gram_want)) / np.diag(gram_want)
+    assert diag_err.max() < 1e-3, f"{what} squared norms: {diag_err.max():.3e}"
+
+
+def test_sampled_rows_of_the_full_launch_match_the_oracle(operator):
+    """8 rows of the full 256-candidate launch (jobs dealt over every SM, per-candidate fixed-point scales)."""
+    from oracle import opus_oracle as orc
+
+    o = operator
+    rows = [0, 1, 37, 100, 128, 129, 200, 255]
+    h, s = orc.hash_sign_tables(D_OUT * D_IN, 0, K, seed=42, device="cuda")
+    want = _oracle_rows(o["dz"], o["a"], h, s, K, o["diag"], rows)
+    _check_rows(o["phi"][rows].double().cpu().numpy(), want, "k=16384")
+
+
+def test_sampled_rows_at_the_gpt2_xl_mlp_shape():
+    """k = 65536 at 1600 -> 6400 with 128 candidates (the shared-memory prefix plus L2 atomics above it)."""
+    from oracle import opus_oracle as orc
+
+    d_in, d_out, k, nb = 1600, 6400, 65536, 128
+    g = torch.Generator(device=DEV).manual_seed(77)
+    a = torch.randn(nb, T, d_in, generator=g, device=DEV).to(torch.bfloat16)
+    dz = (torch.randn(nb, T, d_out, generator=g, device=DEV) * 1e-3).to(torch.bfloat16)
+    diag = torch.rand(d_out, d_in, generator=g, device=DEV) * (1e-3 - 1e-6) + 1e-6
+    proj = GradientProjector(sketch_dim=k, seed=42, device="cuda")
+    packed = proj.packed_table(d_out * d_in, 3, torch.device(DEV))
+    load = proj.max_bucket_load(d_out * d_in, 3, torch.device(DEV))
+    table = ops.build_sketch_table(packed, d_out, d_in, diag=diag)
+    phi = ops.sketch_gemm(dz, a, table, k, max_bucket_load=load)
+    ops.check_device_error("k=65536 sketch")
+    rows = [0, 63, 64, 127]
+    h, s = orc.hash_sign_tables(d_out * d_in, 3, k, seed=42, device="cuda")
+    want = _oracle_rows(dz, a, h, s, k, diag, rows)
+    _check_rows(phi[rows].double().cpu().numpy(), want, "k=65536")

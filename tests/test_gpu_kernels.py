@@ -452,3 +452,15 @@ def test_ghost_gram_empty():
     out = torch.full((3, 3), 7.0, device=DEV)
     assert not ops.ghost_gram(a, g, out=out).any()
     assert ops.ghost_gram(a[:0], g[:0]).shape == (0, 0)
+
+
+@pytest.mark.parametrize("n", [1, 7, 4096, 1000003])
+def test_adam_diag_bit_exact(n):
+    """1 / (sqrt(v) + eps) equals torch's CUDA result bit for bit (data_selection.py:208-214)."""
+    torch.manual_seed(n)
+    v = torch.rand(n, device=DEV) * 1e-3
+    v[: min(n, 3)] = 0.0
+    got = ops.adam_diag(v, 1e-8)
+    assert torch.equal(got, (v.sqrt() + 1e-8).reciprocal())
+    odd = v[1:]  # a 4-byte-offset view takes the scalar path
+    assert torch.equal(ops.adam_diag(odd, 1e-6), (odd.sqrt() + 1e-6).reciprocal())

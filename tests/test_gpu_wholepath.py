@@ -304,3 +304,62 @@ def test_score_shard_streams_like_batch_capture(name, exact, monkeypatch):
     for mode in ("stream", "batch"):
         assert_close_scores(out[mode][0].cpu().numpy(), g["scores"])
         assert_close_scores(out[mode][1].cpu().numpy(), g["sim"])
+
+
+@pytest.mark.parametrize("name,rows", [("adamw_proj", 2), ("adamw_proj_perval", 3), ("muon_proj", 4),
+                                       ("auto_mixed", 1), ("sgd_proj", 5)])
+def test_capture_in_passes_matches_reference(name, rows, monkeypatch):
+    """Candidates and proxies captured a few rows per forward/backward give the reference's whole-batch values."""
+    g = load_golden(f"wholepath_{name}")
+    per_val = bool(g["cfg"][1])
+    model, opt, loader, batch = rebuild(g, device=DEV)
+    ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    monkeypatch.setattr(ds, "CAPTURE_ROWS", rows)
+    assert ds._use_passes(batch["input_ids"].shape[0] + 2, ds.find_GClayers(model), 128, torch.device(DEV))
+    scores, sim = ds.compute_GradProd_GC_per_iter(model, torch.device(DEV), batch, loader, opt,
+                                                  ds.find_GClayers(model), preconditioner=str(g["precond"]),
+                                                  score_len=128, per_val=per_val)
+    assert_close_scores(scores, g["scores"])
+    assert_close_scores(sim, g["sim"])
+
+
+def test_get_batch_opus_in_passes_matches_reference(monkeypatch):
+    """The public call with the capture split into passes: the reference's scores and picks."""
+    g = load_golden("getbatch_stochastic")
+    model, opt, loader, _ = rebuild(g, device=DEV)
+    ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    monkeypatch.setattr(ds, "CAPTURE_ROWS", 3)
+    cand = torch.from_numpy(g["cand"]).to(DEV)
+    layers = ds.find_GClayers(model)
+    ds._GBG_CALL_ID = 0
+    sc, sm = ds.get_batch_opus(model, cand, cand.clone(), None, None, opt, layers, loader, 0.5, 128,
+                               selection_method="stochastic", temperature=1.0, score_len=128,
+                               preconditioner="adamw", return_scores_only=True, n_windows=2)
+    assert_close_scores(sc.cpu().numpy(), g["scores"])
+    assert_close_scores(sm.cpu().numpy(), g["sim"])
+    np.random.seed(int(g["np_seed"]))
+    ds._GBG_CALL_ID = 0
+    idx = ds.get_batch_opus(model, cand, cand.clone(), None, None, opt, layers, loader, 0.5, 128,
+                            selection_method="stochastic", temperature=1.0, score_len=128, preconditioner="adamw",
+                            n_windows=2)
+    assert idx.cpu().tolist() == list(g["idx"])
+
+
+def test_score_shard_in_passes_matches_single_pass(monkeypatch):
+    """World size 1: the sharded scorer with its capture split into passes equals the single-pass scorer."""
+    from opus_b200.train import distributed as sd
+
+    g = load_golden("wholepath_muon_proj")
+    model, opt, loader, batch = rebuild(g, device=DEV)
+    ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    proxy = loader._fixed_batch
+    layers = ds.find_GClayers(model)
+    n = proxy["input_ids"].shape[0]
+    one = sd.score_shard(model, torch.device(DEV), dict(batch), proxy, n, opt, layers, preconditioner="muon",
+                         score_len=128)
+    monkeypatch.setattr(ds, "CAPTURE_ROWS", 2)
+    split = sd.score_shard(model, torch.device(DEV), dict(batch), proxy, n, opt, layers, preconditioner="muon",
+                           score_len=128)
+    assert_close_scores(split[0].cpu().numpy(), one[0].cpu().numpy(), rtol=1e-4)
+    assert_close_scores(split[1].cpu().numpy(), one[1].cpu().numpy(), rtol=1e-4)
+    assert_close_scores(split[0].cpu().numpy(), g["scores"])

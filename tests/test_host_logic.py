@@ -64,9 +64,33 @@ def rebuild_lora(g, device="cpu"):
 
 
 def assert_close_scores(got, want, rtol=1e-3):
+    """Every score / similarity element within rtol of its own reference value.
+
+    The north star's 1e-3 relative error holds per element.  Only an element
+    whose reference value is exactly zero (relative error undefined) gets an
+    absolute bound instead: rtol * 1e-6 of the largest reference value.
+    """
     got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
-    scale = np.abs(want).max()
-    np.testing.assert_allclose(got, want, rtol=rtol, atol=rtol * 1e-2 * scale)
+    assert got.shape == want.shape, (got.shape, want.shape)
+    err = np.abs(got - want)
+    zero = want == 0
+    bound = np.where(zero, rtol * 1e-6 * np.abs(want).max(), rtol * np.abs(want))
+    bad = ~(err <= bound)
+    if bad.any():
+        i = np.unravel_index(int(np.argmax(np.where(bad, err / np.maximum(bound, 1e-300), 0))), want.shape)
+        raise AssertionError(f"{int(bad.sum())} of {want.size} elements outside rtol={rtol}; worst at {i}: "
+                             f"got {got[i]!r}, want {want[i]!r} (relative {err[i] / max(abs(want[i]), 1e-300):.3e})")
+
+
+@pytest.fixture(autouse=True)
+def _reference_muon_on_cpu(monkeypatch):
+    """plan_layers runs on the CPU here: the Muon S and transform come from the reference's own torch recipe
+    (oracle/reference_torch.py); the tcgen05 kernels that replace them need a GPU and have GPU tests."""
+    from opus_b200 import ops
+    from oracle import reference_torch as rt
+
+    monkeypatch.setattr(ops, "muon_S", rt.muon_S)
+    monkeypatch.setattr(ops, "muon_transform", rt.muon_transform)
 
 
 @pytest.mark.parametrize("name", SCENARIOS)
