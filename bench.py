@@ -67,12 +67,15 @@ def parse_args():
                     help="candidates per GPU (default 256; smaller only for profiling captures)")
     ap.add_argument("--layer", default=None, metavar="D_IN,D_OUT,K",
                     help="operator workload: another layer shape and sketch size (profiling; default 768,3072,16384)")
-    ap.add_argument("--workload", default="gpt2-xl", choices=["gpt2-xl", "gpt2-small", "operator"],
+    ap.add_argument("--workload", default="gpt2-xl",
+                    choices=["gpt2-xl", "gpt2-medium", "gpt2-small", "qwen3", "operator"],
                     help="gpt2-xl (default): one whole selection round per step on a GPT-2-XL-shaped model "
                          "(capture, 192 layers of sketches, scores, similarity, the draw), 128 candidates and 16 "
                          "proxies per GPU, k=65536, with the overhead as a share of one training step; "
-                         "gpt2-small: the same on GPT-2 small (64 + 16, k=8192); operator: the isolated "
-                         "single-layer operator")
+                         "gpt2-medium: the same on GPT-2 medium with Muon on the hidden matrices (64 + 8, "
+                         "k=32768, T=0.5); gpt2-small: the same on GPT-2 small (64 + 16, k=8192); qwen3: a "
+                         "Qwen3-style model with Muon (32 + 4 of 4096 tokens, k=131072, T=0.7); operator: the "
+                         "isolated single-layer operator")
     ap.add_argument("--candidates", type=int, default=None, help="whole path: candidates per GPU (profiling)")
     ap.add_argument("--proxies", type=int, default=None, help="whole path: proxies per GPU (profiling)")
     ap.add_argument("--selection", default="global", choices=["global", "local"],
@@ -85,11 +88,16 @@ def parse_args():
     ap.add_argument("--model-dtype", default=None, choices=["f32", "bf16"],
                     help="whole path: parameter and activation dtype (default: the workload's, bf16 for GPT-2 XL, "
                          "f32 for GPT-2 small)")
-    ap.add_argument("--path", default="sketch", choices=["sketch", "ghost", "noproj-sim", "select"],
+    ap.add_argument("--path", default="sketch",
+                    choices=["sketch", "ghost", "noproj-sim", "select", "muon", "memory"],
                     help="sketch: the selection step (default line); ghost: exact scores through the ghost "
                          "contraction against the de-sketched AdamW target (stage 2 on its own, one GPU); "
                          "noproj-sim: the projection-off similarity (exact per-sample gradients + Gram, one GPU); "
-                         "select: the Boltzmann draw on its own (one GPU, --select N,K,BLOCK)")
+                         "select: the Boltzmann draw on its own (one GPU, --select N,K,BLOCK); muon: the Muon "
+                         "candidate transform dL/dZ S^T and S itself at the Qwen3 gate/up shape (one GPU); "
+                         "memory: the memory-bound kernels at the GPT-2-XL MLP layer size (one GPU)")
+    ap.add_argument("--muon", default="4,4096,6144,2048", metavar="SEQS,T,D_OUT,D_IN",
+                    help="--path muon: sequences, tokens, the layer's d_out (the transform's width) and d_in")
     ap.add_argument("--select", default="2048,512,256", metavar="N,K,BLOCK",
                     help="--path select: candidates, draws and similarity block (0 = dense); default: the "
                          "global draw of 8 ranks x 256 candidates")
@@ -279,7 +287,7 @@ def run_gpu(args, rank, world, local_rank):
 
     def step(time_kernel=False):
         table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
-        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau, rows=rows)
+        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau, rows=rows, max_bucket_load=load)
         sd.allreduce_target_sketches(tau)
         phi.zero_()
         if time_kernel:
@@ -329,7 +337,7 @@ def run_gpu(args, rank, world, local_rank):
         evs[0].record()
         table = ops.build_sketch_table(packed, D_OUT, D_IN, diag=diag)
         evs[1].record()
-        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau, rows=rows)
+        ops.sketch_dense(V, packed, D_OUT, D_IN, K_SKETCH, transposed=True, out=tau, rows=rows, max_bucket_load=load)
         evs[2].record()
         sd.allreduce_target_sketches(tau)
         evs[3].record()
@@ -533,6 +541,167 @@ def run_noproj_sim(args):
     return 0
 
 
+def run_muon(args):
+    """The Muon preconditioner kernels on their own, one GPU.
+
+    Per step: the candidate transform dL/dZ <- dL/dZ S^T (opus_gemm_bf16,
+    bf16 in and out, f32 accumulation) over SEQS x T tokens of a layer with
+    d_out outputs, the work data_selection.py:495-500 does per Muon layer;
+    the S build (opus_muon_S: norm, normalise, A = m~ m~^T, A A^T with the
+    fused S epilogue) is timed separately on a [d_out, d_in] momentum buffer.
+    Defaults: the Qwen3-style gate/up projection (d_out 6144, d_in 2048) at
+    4 sequences of 4096 tokens.
+    """
+    import torch
+
+    from opus_b200 import ops
+
+    seqs, t, d_out, d_in = (int(x) for x in args.muon.split(","))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    dz = (torch.randn(seqs * t, d_out, generator=g, device=dev) * 1e-3).to(torch.bfloat16)
+    m = torch.randn(d_out, d_in, generator=g, device=dev) * 1e-3
+    S = ops.muon_S(m)
+    out = torch.empty_like(dz)
+    ev = {"s": [], "e": [], "ss": [], "se": []}
+
+    def step(time_kernel=False):
+        if time_kernel:
+            ev["ss"].append(torch.cuda.Event(enable_timing=True))
+            ev["se"].append(torch.cuda.Event(enable_timing=True))
+            ev["ss"][-1].record()
+        ops.muon_S(m)
+        if time_kernel:
+            ev["se"][-1].record()
+            ev["s"].append(torch.cuda.Event(enable_timing=True))
+            ev["e"].append(torch.cuda.Event(enable_timing=True))
+            ev["s"][-1].record()
+        ops.gemm_bf16(dz, S, out_dtype=torch.bfloat16, out=out)
+        if time_kernel:
+            ev["e"][-1].record()
+
+    for _ in range(args.warmup):
+        step()
+    ops.check_device_error("muon warm-up")
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.kernel_launches()
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(time_kernel=True)
+        end.record()
+        torch.cuda.synchronize()
+    launches = ops.kernel_launches() - launches0
+    ops.check_device_error("muon timed region")
+    ms = start.elapsed_time(end) / args.steps
+    t_ms = sum(x.elapsed_time(y) for x, y in zip(ev["s"], ev["e"])) / args.steps
+    s_ms = sum(x.elapsed_time(y) for x, y in zip(ev["ss"], ev["se"])) / args.steps
+    burst, sustained, hbm, src = measured_peaks()
+    flops = 2.0 * seqs * t * d_out * d_out
+    s_flops = 2.0 * d_out * d_out * d_in + 2.0 * d_out ** 3
+    achieved = flops / (t_ms * 1e-3) / 1e12
+    line = {"metric": "Muon candidate-transform tokens/sec", "value": round(seqs * t / (t_ms / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"dL/dZ [{seqs} x {t} tokens, {d_out}] x S^T [{d_out}, {d_out}] (bf16 out), S "
+                                   f"from a [{d_out}, {d_in}] momentum buffer",
+                       "l2": "dL/dZ and the output exceed the 126 MB L2, no flush"},
+            "roofline": {"bound": "tensor", "kernel": "gemm_bf16 (transform)", "achieved": round(achieved, 2),
+                         "peak": burst, "unit": "TFLOP/s", "frac": round(achieved / burst, 4),
+                         "peak_kind": f"bf16 burst ({src})", "kernel_ms": round(t_ms, 4),
+                         "flops_per_launch": flops, "traffic": None},
+            "muon_S": {"ms": round(s_ms, 4), "tflops": round(s_flops / (s_ms * 1e-3) / 1e12, 2),
+                       "flops": s_flops},
+            "clocks": clk.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_memory(args):
+    """The memory-bound kernels at the GPT-2-XL MLP layer size (6400 x 1600, k = 65536), one GPU.
+
+    Each kernel's algorithmic bytes (every input read once, every output
+    written once) over its CUDA-event time, against the measured HBM peak:
+      sketch_dense (flat)    w f32 + packed table u32: 8 B per element
+      sketch_dense (w^T)     the same, the weight stored transposed
+      build_sketch_table     packed u32 + v f32 read, 8 B table written: 16 B per element
+      adam_diag              v f32 read, D f32 written: 8 B per element
+      sketch_dot             phi [128, 65536] f32 read once (tau stays in L2): 4 B per element
+    Before every timed launch a 256 MB buffer is read (summed), which leaves L2 full of clean
+    lines of other data: the inputs come from HBM and no dirty line's write-back lands inside
+    the timed kernel.
+    """
+    import torch
+
+    from opus_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    d_out, d_in, k, rows = 6400, 1600, 65536, 128
+    n = d_out * d_in
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    w = torch.randn(d_out, d_in, generator=g, device=dev)
+    wt = w.T.contiguous()
+    v = torch.rand(d_out, d_in, generator=g, device=dev) * 1e-4
+    h = torch.randint(0, k, (n,), generator=g, device=dev)
+    sgn = torch.randint(0, 2, (n,), generator=g, device=dev).float() * 2 - 1
+    packed = ops.pack_hash_sign(h, sgn, k)
+    load = ops.bucket_max_load(packed, k)
+    phi = torch.randn(rows, k, generator=g, device=dev)
+    tau = torch.randn(k, generator=g, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+    sk = torch.empty(k, device=dev)
+    table = torch.empty(ops.sketch_table_entries(d_out, d_in) * 4, dtype=torch.int32, device=dev)
+    score = torch.empty(rows, device=dev)
+    cases = {
+        "sketch_dense_flat": (8.0 * n, lambda: ops.sketch_dense(w, packed, d_out, d_in, k, out=sk,
+                                                                max_bucket_load=load)),
+        "sketch_dense_transposed": (8.0 * n, lambda: ops.sketch_dense(wt, packed, d_out, d_in, k, transposed=True,
+                                                                      out=sk, max_bucket_load=load)),
+        "build_sketch_table": (16.0 * n, lambda: ops.build_sketch_table(packed, d_out, d_in, exp_avg_sq=v,
+                                                                        out=table)),
+        "adam_diag": (8.0 * n, lambda: ops.adam_diag(v)),
+        "sketch_dot": (4.0 * rows * k, lambda: ops.sketch_dot(phi, tau, out=score)),
+    }
+    burst, sustained, hbm, src = measured_peaks()
+    out = {}
+    launches0 = ops.kernel_launches()
+    with ClockSampler(0) as clk:
+        for name, (nbytes, fn) in cases.items():
+            for _ in range(args.warmup):
+                fn()
+            times = []
+            for _ in range(args.steps):
+                flush.sum()  # evict the inputs from L2 with clean lines
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                fn()
+                s1.record()
+                torch.cuda.synchronize()
+                times.append(s0.elapsed_time(s1))
+            ms = statistics.median(times)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                         "bytes": nbytes}
+    launches = ops.kernel_launches() - launches0
+    ops.check_device_error("memory kernels")
+    line = {"metric": "memory-bound kernels, achieved GB/s", "value": out["sketch_dense_flat"]["GB/s"],
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": out["sketch_dense_flat"]["us"] / 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"GPT-2-XL MLP layer {d_out} x {d_in} (82 MB f32 + 41 MB table), k={k}, "
+                                   f"sketch_dot over [{rows}, {k}]",
+                       "l2": "a 256 MB buffer read before every timed launch"},
+            "roofline": {"bound": "hbm", "peak": hbm, "unit": "GB/s", "peak_kind": f"HBM copy ({src})",
+                         "kernels": out, "traffic": None},
+            "clocks": clk.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_select(args):
     """The selection draw on its own, one GPU: K sequential draws over N candidates.
 
@@ -642,9 +811,94 @@ def gpt2_model(linear_cls, vocab=50257, d=768, n_layer=12, n_head=12, ctx=1024, 
     return GPT()
 
 
+def qwen3_model(linear_cls, vocab=151936, d=2048, n_layer=28, n_head=16, n_kv=8, head_dim=128, ffn=6144,
+                ctx=4096, rope_theta=1e6):
+    """A Qwen3-style causal LM (random init) whose seven linears per block are capture layers.
+
+    The selection path's workload only: pre-RMSNorm blocks with grouped-query
+    attention (n_head query heads, n_kv key/value heads of head_dim, RMSNorm
+    on q and k per head, rotary position embedding) and a SwiGLU MLP of
+    width ffn, no biases, tied output embedding.  At the defaults: 28 blocks,
+    196 capture layers holding 1,409,286,144 weights.
+    """
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    class RMSNorm(nn.Module):
+        def __init__(self, n):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(n))
+
+        def forward(self, x):
+            return F.rms_norm(x, (x.shape[-1],), self.weight, eps=1e-6)
+
+    inv = 1.0 / (rope_theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+
+    def rope(x, cos, sin):  # x [b, h, t, hd]
+        x1, x2 = x[..., : head_dim // 2], x[..., head_dim // 2:]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.n1, self.n2 = RMSNorm(d), RMSNorm(d)
+            self.q, self.k = linear_cls(d, n_head * head_dim, bias=False), linear_cls(d, n_kv * head_dim, bias=False)
+            self.v, self.o = linear_cls(d, n_kv * head_dim, bias=False), linear_cls(n_head * head_dim, d, bias=False)
+            self.qn, self.kn = RMSNorm(head_dim), RMSNorm(head_dim)
+            self.gate, self.up = linear_cls(d, ffn, bias=False), linear_cls(d, ffn, bias=False)
+            self.down = linear_cls(ffn, d, bias=False)
+
+        def forward(self, x, cos, sin):
+            b, t, _ = x.shape
+            h = self.n1(x)
+            q = self.qn(self.q(h).view(b, t, n_head, head_dim)).transpose(1, 2)
+            k = self.kn(self.k(h).view(b, t, n_kv, head_dim)).transpose(1, 2)
+            v = self.v(h).view(b, t, n_kv, head_dim).transpose(1, 2)
+            q, k = rope(q, cos, sin), rope(k, cos, sin)
+            y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            x = x + self.o(y.transpose(1, 2).reshape(b, t, n_head * head_dim))
+            h = self.n2(x)
+            return x + self.down(F.silu(self.gate(h)) * self.up(h))
+
+    class LM(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = nn.Embedding(vocab, d)
+            self.blocks = nn.ModuleList(Block() for _ in range(n_layer))
+            self.norm = RMSNorm(d)
+            self.register_buffer("inv_freq", inv, persistent=False)
+
+        def forward(self, input_seq, target_seq=None, sliding_window_num_blocks=None):
+            if input_seq.ndim == 1:
+                input_seq = input_seq[None]
+            t = input_seq.shape[1]
+            ang = torch.outer(torch.arange(t, device=input_seq.device, dtype=torch.float32), self.inv_freq)
+            x = self.embed(input_seq)
+            cos, sin = ang.cos().to(x.dtype), ang.sin().to(x.dtype)
+            for blk in self.blocks:
+                x = blk(x, cos, sin)
+            logits = F.linear(self.norm(x), self.embed.weight)
+            if target_seq is not None:
+                return F.cross_entropy(logits.float().view(-1, logits.size(-1)), target_seq.reshape(-1))
+            return logits
+
+    return LM()
+
+
+def build_model(cfg, linear_cls, n_layer=None):
+    """The workload model of a whole-path configuration (n_layer blocks: the configuration's by default)."""
+    n_layer = cfg["layers"] if n_layer is None else n_layer
+    if cfg.get("arch") == "qwen3":
+        return qwen3_model(linear_cls, vocab=cfg["vocab"], d=cfg["d"], n_layer=n_layer, n_head=cfg["heads"],
+                           n_kv=cfg["kv_heads"], head_dim=cfg["head_dim"], ffn=cfg["ffn"], ctx=cfg["seq"])
+    return gpt2_model(linear_cls, vocab=cfg["vocab"], d=cfg["d"], n_layer=n_layer, n_head=cfg["heads"],
+                      ctx=cfg["seq"])
+
+
 # The training step the overhead is measured against: the kept sequences in micro-batches of this many
-# (gradient accumulation), then one AdamW step.
-TRAIN_MICRO_BATCH = 8
+# tokens (gradient accumulation; 8 sequences of 1024, 2 of 4096), then one AdamW step.
+TRAIN_MICRO_TOKENS = 8192
 
 # Whole selection rounds on a model (SURVEY-style configurations: per GPU
 # candidates and proxies, the sketch size, the kept share, the temperature).
@@ -653,6 +907,13 @@ WHOLE = {
                 "cand": 128, "proxy": 16, "k": 65536, "keep": 0.25, "temp": 1.0, "dtype": "bf16"},
     "gpt2-small": {"label": "GPT-2 small", "d": 768, "layers": 12, "heads": 12, "vocab": 50257, "seq": 1024,
                    "cand": 64, "proxy": 16, "k": 8192, "keep": 0.25, "temp": 1.0, "dtype": "f32"},
+    # Muon (momentum SGD state) on the blocks' matrices, AdamW on the embeddings; "auto" picks per group
+    "gpt2-medium": {"label": "GPT-2 medium", "d": 1024, "layers": 24, "heads": 16, "vocab": 50257, "seq": 1024,
+                    "cand": 64, "proxy": 8, "k": 32768, "keep": 0.25, "temp": 0.5, "dtype": "bf16",
+                    "muon": True},
+    "qwen3": {"label": "Qwen3-style", "arch": "qwen3", "d": 2048, "layers": 28, "heads": 16, "kv_heads": 8,
+              "head_dim": 128, "ffn": 6144, "vocab": 151936, "seq": 4096, "cand": 32, "proxy": 4, "k": 131072,
+              "keep": 0.25, "temp": 0.7, "dtype": "bf16", "muon": True},
 }
 
 
@@ -679,13 +940,17 @@ def zipf_tokens(rng, n, seq, vocab):
 def capture_layer_weights(cfg) -> int:
     """Weights held by the capture layers of the workload model (P_lin)."""
     d = cfg["d"]
+    if cfg.get("arch") == "qwen3":
+        q, kv = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+        return cfg["layers"] * (2 * d * q + 2 * d * kv + 3 * d * cfg["ffn"])
     return cfg["layers"] * (d * 3 * d + d * d + d * 4 * d + 4 * d * d)
 
 
 def wholepath_label(cfg, world) -> str:
+    opt = "Muon on the blocks' matrices, AdamW on the embeddings" if cfg.get("muon") else "AdamW"
     return (f"{cfg['label']} whole selection round: {cfg['cand']} candidates + {cfg['proxy']} proxies of "
             f"{cfg['seq']} tokens per GPU ({cfg['cand'] * world} + {cfg['proxy'] * world} in all), capture of "
-            f"{cfg['layers'] * 4} layers by streaming backward hooks, k={cfg['k']} CountSketch, AdamW, keep "
+            f"{cfg['layers'] * 4} layers by streaming backward hooks, k={cfg['k']} CountSketch, {opt}, keep "
             f"{cfg['kept'] * world} by Boltzmann T={cfg['temp']}")
 
 
@@ -715,12 +980,28 @@ def run_wholepath(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     torch.manual_seed(0)  # the same weights on every rank
     mdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
-    model = gpt2_model(GCLinear, vocab=cfg["vocab"], d=cfg["d"], n_layer=cfg["layers"], n_head=cfg["heads"],
-                       ctx=cfg["seq"]).to(device=dev, dtype=mdt)
+    model = build_model(cfg, GCLinear).to(device=dev, dtype=mdt)
     layers = ds.find_GClayers(model)
-    opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
-    for prm in model.parameters():
-        opt.state[prm] = {"step": torch.tensor(1.0), "exp_avg_sq": torch.full_like(prm, 1e-4, dtype=torch.float32)}
+    precond = "adamw"
+    if cfg.get("muon"):
+        # the blocks' matrices under Muon (a momentum group: momentum buffers N(0, 1e-3)), the rest under AdamW
+        hidden = [prm for blk in model.blocks for prm in blk.parameters() if prm.dim() == 2]
+        ids = {id(prm) for prm in hidden}
+        rest = [prm for prm in model.parameters() if id(prm) not in ids]
+        muon = torch.optim.SGD(hidden, lr=0.02, momentum=0.95)
+        adam = torch.optim.AdamW(rest, lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+        gm = torch.Generator(device=dev).manual_seed(5)
+        for prm in hidden:
+            muon.state[prm] = {"momentum_buffer": torch.randn(prm.shape, generator=gm, device=dev).mul_(1e-3)}
+        for prm in rest:
+            adam.state[prm] = {"step": torch.tensor(1.0), "exp_avg_sq": torch.full_like(prm, 1e-4,
+                                                                                         dtype=torch.float32)}
+        opt, precond = [muon, adam], "auto"
+    else:
+        opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+        for prm in model.parameters():
+            opt.state[prm] = {"step": torch.tensor(1.0), "exp_avg_sq": torch.full_like(prm, 1e-4,
+                                                                                       dtype=torch.float32)}
     seq, nc, npx = cfg["seq"], cfg["cand"], cfg["proxy"]
     buf_np = zipf_tokens(np.random.default_rng(1000 + rank), nc, seq, cfg["vocab"])
     prox_np = zipf_tokens(np.random.default_rng(999), npx * world, seq, cfg["vocab"])
@@ -738,10 +1019,10 @@ def run_wholepath(args, rank, world, local_rank):
         if world == 1:
             return ds.get_batch_opus(model, tokens, tokens, None, None, opt, layers, loader, cfg["keep"], seq,
                                      selection_method="stochastic", temperature=cfg["temp"], score_len=seq,
-                                     preconditioner="adamw")
+                                     preconditioner=precond)
         _, mine = sd.get_batch_opus_global(model, tokens, tokens, opt, layers, loader, cfg["keep"], seq,
                                            selection_method="stochastic", temperature=cfg["temp"], score_len=seq,
-                                           preconditioner="adamw")
+                                           preconditioner=precond)
         return mine
 
     def ev():
@@ -767,7 +1048,9 @@ def run_wholepath(args, rank, world, local_rank):
     with ClockSampler(local_rank) as clk, _lib.KernelTimer() as timer:
         s0.record()
         for _ in range(args.steps):
+            torch.cuda.nvtx.range_push("timed_round")  # ncu --nvtx --nvtx-include timed_round/ selects it
             idx = select(buf)
+            torch.cuda.nvtx.range_pop()
         s1.record()
         torch.cuda.synchronize()
     launches = ops.kernel_launches() - launches0
@@ -782,7 +1065,8 @@ def run_wholepath(args, rank, world, local_rank):
 
     # stage 1 alone: the same forward/backward passes with hooks that do nothing
     rows = nc + npx
-    step = ds.rows_per_pass(layers, seq, dev, 4 * cfg["k"] * rows * 2 * len(layers))
+    step = ds.rows_per_pass(layers, seq, dev, 4 * cfg["k"] * rows * ds._pairs(layers), model,
+                            ds._has_muon(opt, precond))
     mine = prox[rank * npx:(rank + 1) * npx] if world > 1 else prox
 
     def part(x):
@@ -797,7 +1081,7 @@ def run_wholepath(args, rank, world, local_rank):
     def capture_only():
         pc = {}
         for bt, bv in passes:
-            ds.stream_capture(model, dev, bt, bv, opt, layers, "adamw", seq, lambda *a: (lambda pl: None), pc)
+            ds.stream_capture(model, dev, bt, bv, opt, layers, precond, seq, lambda *a: (lambda pl: None), pc)
 
     capture_only()
     c0, c1 = ev(), ev()
@@ -836,12 +1120,12 @@ def run_wholepath(args, rank, world, local_rank):
     # multi-GPU parity: the N-rank global draw equals one process's draw over the gathered scores and blocks
     parity = None
     if world > 1:
-        parity = wholepath_parity(model, dev, buf, opt, layers, loader, cfg, world)
+        parity = wholepath_parity(model, dev, buf, opt, layers, loader, cfg, world, precond)
 
     # the training step the selection feeds: forward, backward and AdamW on this rank's kept sequences
     kept = buf[:cfg["kept"]]  # the per-GPU share of the kept sequences (their content does not change the time)
     train_opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
-    micro = min(TRAIN_MICRO_BATCH, kept.shape[0])
+    micro = max(1, min(TRAIN_MICRO_TOKENS // seq, kept.shape[0]))
 
     def train_step():
         train_opt.zero_grad(set_to_none=True)
@@ -872,7 +1156,7 @@ def run_wholepath(args, rank, world, local_rank):
             "rows_per_pass": step, "kept": int(kept.shape[0])}
 
 
-def wholepath_parity(model, dev, buf, opt, layers, loader, cfg, world):
+def wholepath_parity(model, dev, buf, opt, layers, loader, cfg, world, precond="adamw"):
     """Recompute one global round step by step and check its picks.
 
     Every rank scores its shard (score_shard), the global draw runs over
@@ -896,7 +1180,7 @@ def wholepath_parity(model, dev, buf, opt, layers, loader, cfg, world):
     share = {key: v[lo:hi] for key, v in proxy.items()}
     batch = {"input_ids": buf, "attention_mask": torch.ones_like(buf), "labels": buf}
     score, sim = sd.score_shard(model, dev, batch, share, proxy["input_ids"].shape[0], opt, layers,
-                                preconditioner="adamw", score_len=seq)
+                                preconditioner=precond, score_len=seq)
     n_sel = max(1, int(buf.shape[0] * world * cfg["keep"]))
     u = sd.shared_uniforms(n_sel, dev)
     gidx, _ = sd.select_global(score, sim, n_sel, method="stochastic", temperature=cfg["temp"], uniforms=u)
@@ -944,21 +1228,24 @@ def cpu_wholepath_sample(cfg, models=None):
 
     if models is None:
         torch.manual_seed(0)
-        models = [gpt2_model(GCLinear, vocab=cfg["vocab"], d=d, n_layer=nb, n_head=cfg["heads"], ctx=seq).float()
-                  for nb in (1, 2)]
+        models = [build_model(cfg, GCLinear, nb).float() for nb in (1, 2)]
         for m in models:  # the first call of each model pays one-time allocations
             capture(m)
     t1, pairs = capture(models[0])
     t2, _ = capture(models[1])
     t_block = max(0.0, t2 - t1)
-    shapes = [(3 * d, d), (d, d), (4 * d, d), (d, 4 * d)]
+    shapes = [tuple(layer.weight.shape) for layer in ds.find_GClayers(models[0])]
     t_cand = t_prox = 0.0
     for pid, ((g_t, a_t), (g_v, a_v)) in enumerate(pairs):
         d_out, d_in = shapes[pid]
         h, s = orc.hash_sign_tables(d_out * d_in, pid, k, seed=SEED)
-        diag = torch.full((d_out, d_in), 1.0 / (1e-2 + 1e-8))
+        diag = S = None
+        if cfg.get("muon"):  # the candidate transform by S (built once per round, as the reference caches it)
+            S = rt.muon_S(torch.randn(d_out, d_in, generator=g) * 1e-3)
+        else:
+            diag = torch.full((d_out, d_in), 1.0 / (1e-2 + 1e-8))
         t = time.perf_counter()
-        phi = rt.project_full_gradient(g_t, a_t, h, s, k, diag=diag)
+        phi = rt.project_full_gradient(g_t, a_t, h, s, k, diag=diag, S=S)
         t_cand += time.perf_counter() - t
         t = time.perf_counter()
         rt.project_full_gradient(g_v, a_v, h, s, k)
@@ -969,8 +1256,9 @@ def cpu_wholepath_sample(cfg, models=None):
     per_cand = t_model_2rows / 2 * (1 + ratio) + cfg["layers"] * (2 * t_cand + ratio * t_prox)
     desc = (f"reference op sequence (oracle/reference_torch.py) in f32 on the host cores: capture of a 1- and a "
             f"2-block model of the {cfg['label']} width with 1 candidate + 1 proxy row of {seq} tokens "
-            f"({t1:.2f} s, {t2:.2f} s), one block's 4 layers sketched for the candidate ({t_cand:.2f} s, twice per "
-            f"round as the reference does) and the proxy ({t_prox:.2f} s); extrapolated to {cfg['layers']} blocks "
+            f"({t1:.2f} s, {t2:.2f} s), one block's {len(shapes)} layers sketched for the candidate "
+            f"({t_cand:.2f} s, twice per round as the reference does) and the proxy ({t_prox:.2f} s); "
+            f"extrapolated to {cfg['layers']} blocks "
             f"and {cfg['proxy']} proxies per {cfg['cand']} candidates: {per_cand:.1f} s per candidate")
     return 1.0 / per_cand, per_cand, desc, models
 
@@ -1051,9 +1339,9 @@ def emit_wholepath(args, res, world):
                        "capture_rows_per_pass": res["rows_per_pass"],
                        "l2": "weights and activations (GBs) exceed the 126 MB L2, no flush",
                        "overhead_denominator": (f"one training step: forward and backward over the {res['kept']} "
-                                                f"sequences this GPU keeps (micro-batches of {TRAIN_MICRO_BATCH}, "
-                                                "gradients accumulated), then AdamW; same model, no gradient "
-                                                "all-reduce")},
+                                                f"sequences this GPU keeps (micro-batches of {TRAIN_MICRO_TOKENS} "
+                                                "tokens, gradients accumulated), then AdamW; same model, no "
+                                                "gradient all-reduce")},
             "overhead_pct_of_step": round(100.0 * res["ms"] / res["train_ms"], 1),
             "capture_ms": round(res["capture_ms"], 2), "train_step_ms": round(res["train_ms"], 2),
             "stage_ms": res["stage_ms"], "stage_calls_per_step": res["stage_calls"],
@@ -1180,6 +1468,10 @@ def main():
         return run_noproj_sim(args)
     if args.path == "select":
         return run_select(args)
+    if args.path == "muon":
+        return run_muon(args)
+    if args.path == "memory":
+        return run_memory(args)
     import torch.distributed as dist
 
     rank, world, local_rank = init_ranks()

@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define OPUS_ABI_VERSION 1
+#define OPUS_ABI_VERSION 2
 
 #define OPUS_OK 0
 #define OPUS_ERR_INVALID 1     /* bad argument (maps to ValueError) */
@@ -201,12 +201,25 @@ OPUS_API int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, in
  * w[o*d_in+c] (transposed = 0) or w[c*d_out+o] (transposed = 1); diag may be
  * NULL.  Only rows row_begin <= o < row_end are added (0, d_out for the whole
  * matrix): ranks that share the target each sketch their rows and sum the
- * partial sketches.  Replaces GradientProjector.project_vector
+ * partial sketches.  max_bucket_load: the table's largest bucket load
+ * (opus_bucket_max_load), or 0 when unknown; it bounds the int32 fixed-point
+ * shared-memory sketch, and the element count bounds it otherwise, at about
+ * 100 times coarser rounding (still below 1e-4 of the largest bucket).
+ * Replaces GradientProjector.project_vector
  * (OPUS/train/random_projection.py:72-99).
  */
 OPUS_API int opus_sketch_dense(const float* w, int transposed, const uint32_t* packed, const float* diag,
-                      int d_out, int d_in, int row_begin, int row_end, int64_t k, float* sketch, int accumulate,
-                      void* stream);
+                               int d_out, int d_in, int row_begin, int row_end, int64_t k, int max_bucket_load,
+                               float* sketch, int accumulate, void* stream);
+
+/*
+ * K1 batched — the CountSketch of each of n_vec vectors of numel f32 values
+ * (w[v * numel + i], table element i), into sketches[v * k + h]; one launch
+ * for GradientProjector.project_batch (OPUS/train/random_projection.py:
+ * 101-132), which sketches a [B, d] batch row by row.  n_vec <= 65535.
+ */
+OPUS_API int opus_sketch_dense_rows(const float* w, int n_vec, int64_t numel, const uint32_t* packed, int64_t k,
+                                    int max_bucket_load, float* sketches, int accumulate, void* stream);
 
 /*
  * K2 — de-sketched target for the ghost contraction:

@@ -40,8 +40,8 @@ SIGNATURES: dict[str, tuple] = {
     "opus_ghost_gram": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f32, _c_p, _c_int,
                                  _c_p]),
     "opus_per_sample_grad": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_int, _c_p]),
-    "opus_sketch_dense": (_c_int, [_c_p, _c_int, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_p, _c_int,
-                                   _c_p]),
+    "opus_sketch_dense": (_c_int, [_c_p, _c_int, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int, _c_p,
+                                   _c_int, _c_p]),
     "opus_desketch": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_i64, _c_f32, _c_p, _c_p]),
     "opus_ghost_score": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_f32, _c_p, _c_int,
                                   _c_p]),
@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "opus_muon_S": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p, _c_p]),
     "opus_kernel_launches": (_c_i64, []),
     "opus_adam_diag": (_c_int, [_c_p, _c_f32, _c_i64, _c_p, _c_p]),
+    "opus_sketch_dense_rows": (_c_int, [_c_p, _c_int, _c_i64, _c_p, _c_i64, _c_int, _c_p, _c_int, _c_p]),
 }
 
 _lock = threading.Lock()

@@ -36,6 +36,7 @@
 // round-robin, so at any time the CTAs work on neighbouring candidates whose
 // operands stay resident in L2, and each job ends with one sketch flush.
 #include <cstdio>
+#include <cstdlib>
 
 #include "opus_common.cuh"
 #include "sketch_layout.cuh"
@@ -49,18 +50,25 @@ constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kChunksPerWarp = kChunksPerTile / (kEpiWarps / 4);  // 4
 constexpr int kHeadroomLog2 = 4;                     // first-tile max maps to cap / 16
 constexpr int kBoxMN = 64;                           // bf16 elements per 128-byte swizzle row
-constexpr int kBK = 64;                              // tokens per pipeline stage
 constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
-constexpr int kKSteps = kBK / kUmmaK;                // 4 MMAs per stage
 constexpr int kGBoxes = kTileM / kBoxMN;             // 2 boxes for the 128 weight rows
 constexpr int kABoxes = kTileN / kBoxMN;             // 4 boxes for the 256 weight columns
-constexpr int kBoxBytes = kBoxMN * 2 * kBK;          // 8 KB
-constexpr int kGTileBytes = kGBoxes * kBoxBytes;     // 16 KB
-constexpr int kATileBytes = kABoxes * kBoxBytes;     // 32 KB
-constexpr int kStageBytes = kGTileBytes + kATileBytes;  // 48 KB
+// Pipeline stage geometry for BK tokens per stage (64: 48 KB stages; 32: 24 KB
+// stages, which leave room for more of a large sketch in shared memory).
+template <int BK>
+struct Stage {
+  static constexpr int kBK = BK;
+  static constexpr int kKSteps = BK / kUmmaK;                     // MMAs per stage
+  static constexpr int kBoxBytes = kBoxMN * 2 * BK;               // one 64-feature box
+  static constexpr int kGTileBytes = kGBoxes * kBoxBytes;
+  static constexpr int kATileBytes = kABoxes * kBoxBytes;
+  static constexpr int kStageBytes = kGTileBytes + kATileBytes;   // 48 KB at BK = 64, 24 KB at 32
+  static constexpr uint32_t kLBO = kBoxBytes;
+};
+constexpr int kStageBytes64 = Stage<64>::kStageBytes;
+constexpr int kStageBytes32 = Stage<32>::kStageBytes;
 // MN-major SW128 canonical layout: 64 contiguous MN elements x 8 K rows per
 // 1024-B atom; atoms along K at SBO = 1024 B, along MN (next box) at LBO.
-constexpr uint32_t kLBO = kBoxBytes;
 constexpr uint32_t kSBO = 1024;
 constexpr uint32_t kKStepBytes = (kUmmaK / 8) * 1024;  // 2 atoms per MMA
 constexpr uint32_t kIdesc = make_idesc(/*bf16*/ 1, /*a MN-major*/ 1, /*b MN-major*/ 1, kTileM, kTileN);
@@ -139,6 +147,7 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
   return epi_sync(bar, phase, abort_flag, err);
 }
 
+template <int BK>
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_out,
@@ -146,13 +155,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                        int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
                        int cap_log2, int* err, int dense, const float* __restrict__ dense_diag, int d_out,
                        int d_in, int accumulate) {
+  using G = Stage<BK>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* stage_mem = smem;
-  int* sk = reinterpret_cast<int*>(smem + (size_t)stages * kStageBytes);
+  int* sk = reinterpret_cast<int*>(smem + (size_t)stages * G::kStageBytes);
   const bool smem_sketch = k_sm > 0;
-  uint8_t* tail = smem + (size_t)stages * kStageBytes + (size_t)k_sm * 4;
+  uint8_t* tail = smem + (size_t)stages * G::kStageBytes + (size_t)k_sm * 4;
   tail = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tail) + 15) & ~uintptr_t(15));
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
@@ -170,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // so the CTAs work on neighbouring candidates at any time and each
   // candidate's operands stay L2-resident while they are read.
   const int64_t n_jobs = (int64_t)n_rows * groups;
-  const int n_kb = (seq_len + kBK - 1) / kBK;
+  const int n_kb = (seq_len + G::kBK - 1) / G::kBK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -217,19 +227,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          uint8_t* sg = stage_mem + (size_t)s * kStageBytes;
-          uint8_t* sa = sg + kGTileBytes;
-          const int t0 = kb * kBK;
+          mbar_arrive_expect_tx(&full[s], G::kStageBytes);
+          uint8_t* sg = stage_mem + (size_t)s * G::kStageBytes;
+          uint8_t* sa = sg + G::kGTileBytes;
+          const int t0 = kb * G::kBK;
           // L2 policy: the dLdZ rows of this o-block are not read again after
           // its last column block; the activations serve every o-block
           const uint64_t gpol = cb == n_cb - 1 ? pol_first : pol_last;
 #pragma unroll
           for (int i = 0; i < kGBoxes; ++i)
-            tma_load_3d_hint(sg + i * kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b, gpol);
+            tma_load_3d_hint(sg + i * G::kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b, gpol);
 #pragma unroll
           for (int i = 0; i < kABoxes; ++i)
-            tma_load_3d_hint(sa + i * kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, pol_last);
+            tma_load_3d_hint(sa + i * G::kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, pol_last);
           if (++s == stages) {
             s = 0;
             ph ^= 1;
@@ -257,12 +267,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t ag = smem_u32(stage_mem + (size_t)s * kStageBytes);
-          const uint32_t aa = ag + kGTileBytes;
+          const uint32_t ag = smem_u32(stage_mem + (size_t)s * G::kStageBytes);
+          const uint32_t aa = ag + G::kGTileBytes;
 #pragma unroll
-          for (int kk = 0; kk < kKSteps; ++kk) {
-            const uint64_t da = make_sdesc_sw128(ag + kk * kKStepBytes, kLBO, kSBO);
-            const uint64_t db = make_sdesc_sw128(aa + kk * kKStepBytes, kLBO, kSBO);
+          for (int kk = 0; kk < G::kKSteps; ++kk) {
+            const uint64_t da = make_sdesc_sw128(ag + kk * kKStepBytes, G::kLBO, kSBO);
+            const uint64_t db = make_sdesc_sw128(aa + kk * kKStepBytes, G::kLBO, kSBO);
             umma_bf16(d_tmem, da, db, kIdesc, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
@@ -525,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
 }
 
-SmemPlan plan_smem(int64_t k) {
+SmemPlan plan_smem(int64_t k, int kStageBytes = kStageBytes64) {
   const size_t limit = static_cast<size_t>(max_smem_optin());
   const size_t fixed = 1024 /*alignment slack*/ + 16 + 8 * (2 * 8 + 6) + 32;
   SmemPlan p{0, 0, 0};
@@ -553,20 +563,20 @@ SmemPlan plan_smem(int64_t k) {
 }
 
 // TMA maps of the two operands: dLdZ [n_rows, seq_len, d_out] and
-// a [n_rows, seq_len, d_in], bf16, boxes of 64 features x kBK tokens.
+// a [n_rows, seq_len, d_in], bf16, boxes of 64 features x bk tokens.
 int encode_operands(const void* dLdZ, const void* a, int n_rows, int seq_len, int d_out, int d_in, CUtensorMap* tm_g,
-                    CUtensorMap* tm_a) {
+                    CUtensorMap* tm_a, int bk = 64) {
   {
     const uint64_t dims[3] = {(uint64_t)d_out, (uint64_t)seq_len, (uint64_t)n_rows};
     const uint64_t strides[2] = {(uint64_t)d_out * 2, (uint64_t)seq_len * d_out * 2};
-    const uint32_t box[3] = {kBoxMN, kBK, 1};
+    const uint32_t box[3] = {kBoxMN, (uint32_t)bk, 1};
     int rc = encode_tmap(tm_g, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dLdZ, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   const uint64_t dims[3] = {(uint64_t)d_in, (uint64_t)seq_len, (uint64_t)n_rows};
   const uint64_t strides[2] = {(uint64_t)d_in * 2, (uint64_t)seq_len * d_in * 2};
-  const uint32_t box[3] = {kBoxMN, kBK, 1};
+  const uint32_t box[3] = {kBoxMN, (uint32_t)bk, 1};
   return encode_tmap(tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -622,8 +632,6 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   if (!accumulate && out_rows > 0) OPUS_CUDA_TRY(cudaMemsetAsync(phi, 0, (size_t)out_rows * k * sizeof(float), st));
   if (n_rows == 0 || seq_len == 0) return OPUS_OK;
 
-  CUtensorMap tm_g, tm_a;
-  if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a)) return rc;
   SmemPlan plan = plan_smem(k);
   if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small");
   // Fixed-point cap: max_bucket_load admitted updates of magnitude <= cap sum to < 2^31.
@@ -636,23 +644,51 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
     while ((int64_t(1) << (cap_log2 + 1)) <= cap_int) ++cap_log2;
     if (cap_log2 < 2 * kHeadroomLog2) max_bucket_load = 0;  // too little range left for fixed point
   }
+  // A sketch larger than shared memory sends the updates of the buckets outside the shared
+  // prefix to L2 reductions.  32-token stages (24 KB) leave room for 45056 buckets instead of
+  // 32768 but feed the MMAs from a shorter pipeline: measured at 128 candidates, they lose at
+  // k = 65536 (445 against 462 TFLOP/s at 1600 -> 6400) and win at k = 131072 (469 against
+  // 391 at 2048 -> 6144), so they are taken when less than half of the sketch fits with
+  // 64-token stages.  OPUS_SKETCH_STAGE_TOKENS=64 or 32 forces one depth.
+  int bk = 64;
+  if (max_bucket_load > 0 && plan.k_sm * 2 < k) {
+    const SmemPlan p32 = plan_smem(k, kStageBytes32);
+    if (p32.stages > 0 && p32.k_sm > plan.k_sm) {
+      plan = p32;
+      bk = 32;
+    }
+  }
+  if (const char* env = getenv("OPUS_SKETCH_STAGE_TOKENS")) {
+    const int want = atoi(env);
+    if ((want == 32 || want == 64) && want != bk) {
+      const SmemPlan pf = plan_smem(k, want == 32 ? kStageBytes32 : kStageBytes64);
+      if (pf.stages > 0) {
+        plan = pf;
+        bk = want;
+      }
+    }
+  }
+  const int stage_bytes = bk == 32 ? kStageBytes32 : kStageBytes64;
   if (max_bucket_load <= 0 && plan.k_sm > 0) {
     // No usable bound: every update goes to global f32 atomics; use the smem for stages.
     for (int stg = 4; stg >= 2; --stg) {
       const size_t need =
-          plan.bytes - (size_t)plan.stages * kStageBytes - (size_t)plan.k_sm * 4 + (size_t)stg * kStageBytes;
+          plan.bytes - (size_t)plan.stages * stage_bytes - (size_t)plan.k_sm * 4 + (size_t)stg * stage_bytes;
       if (need <= static_cast<size_t>(max_smem_optin())) {
         plan = {stg, 0, need};
         break;
       }
     }
   }
-  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  CUtensorMap tm_g, tm_a;
+  if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
+  auto kernel = bk == 32 ? sketch_gemm_kernel<32> : sketch_gemm_kernel<64>;
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
   const JobPlan jp = plan_jobs(n_rows, n_ob);
   int* err = device_error_word();
-  sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
+  kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
       tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_ob, n_cb,
       jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
       accumulate);
@@ -698,12 +734,12 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
   const SmemPlan plan = plan_smem(kStagingWords);
   if (plan.stages == 0 || plan.k_sm < kStagingWords)
     return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
-  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
   const JobPlan jp = plan_jobs(n_rows, n_ob);
   int* err = device_error_word();
-  sketch_gemm_kernel<<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_ob,
+  sketch_gemm_kernel<64><<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_ob,
                                                             n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
                                                             err, /*dense*/ 1, diag, d_out, d_in, accumulate);
   ::opus::note_launch();

@@ -130,17 +130,32 @@ __global__ void desketch_kernel(const float* __restrict__ tau, const uint32_t* _
   }
 }
 
-// D = 1 / (sqrt(v) + eps) elementwise, 16-byte loads and stores when aligned.
+// D = 1 / (sqrt(v) + eps) elementwise: 16-byte loads and stores when aligned,
+// four loads in flight per thread.
+constexpr int kDiagUnroll = 4;
+
 __global__ void adam_diag_kernel(const float* __restrict__ v, float eps, int64_t n, float* __restrict__ out,
                                  int vec) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t start = 0;
   if (vec) {
     const int64_t n4 = n / 4;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-      const float4 q = __ldcs(reinterpret_cast<const float4*>(v) + i);
-      __stcs(reinterpret_cast<float4*>(out) + i,
-             make_float4(adam_diag(q.x, eps), adam_diag(q.y, eps), adam_diag(q.z, eps), adam_diag(q.w, eps)));
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    float4* o4 = reinterpret_cast<float4*>(out);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride * kDiagUnroll) {
+      float4 q[kDiagUnroll];
+#pragma unroll
+      for (int u = 0; u < kDiagUnroll; ++u) {
+        const int64_t iu = i + u * stride;
+        q[u] = iu < n4 ? __ldcs(v4 + iu) : make_float4(1.f, 1.f, 1.f, 1.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kDiagUnroll; ++u) {
+        const int64_t iu = i + u * stride;
+        if (iu < n4)
+          __stcs(o4 + iu, make_float4(adam_diag(q[u].x, eps), adam_diag(q[u].y, eps), adam_diag(q[u].z, eps),
+                                      adam_diag(q[u].w, eps)));
+      }
     }
     start = n4 * 4;
   }
@@ -409,8 +424,9 @@ int opus_adam_diag(const float* exp_avg_sq, float eps, int64_t n, float* out, vo
   if (n == 0) return OPUS_OK;
   if (!exp_avg_sq || !out) return set_error(OPUS_ERR_INVALID, "adam_diag: NULL pointer");
   const int vec = ((reinterpret_cast<uintptr_t>(exp_avg_sq) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
-  adam_diag_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, (cudaStream_t)stream>>>(exp_avg_sq, eps, n, out,
-                                                                                       vec);
+  const int64_t per_thread = vec ? 4 * kDiagUnroll : 1;
+  adam_diag_kernel<<<grid_for(n / per_thread + 1, 256), 256, 0, (cudaStream_t)stream>>>(exp_avg_sq, eps, n, out,
+                                                                                         vec);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;

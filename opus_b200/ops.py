@@ -276,10 +276,13 @@ def per_sample_grad(dLdZ: torch.Tensor, a: torch.Tensor, diag: torch.Tensor | No
 
 def sketch_dense(w: torch.Tensor, packed: torch.Tensor, d_out: int, d_in: int, k: int, transposed: bool = False,
                  diag: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                 accumulate: bool = False, rows: tuple[int, int] | None = None) -> torch.Tensor:
+                 accumulate: bool = False, rows: tuple[int, int] | None = None,
+                 max_bucket_load: int = 0) -> torch.Tensor:
     """sketch[h] += s * diag * W for a dense [d_out, d_in] (or [d_in, d_out] if transposed) matrix.
 
     rows=(lo, hi) adds only the rows lo <= o < hi of the [d_out, d_in] layout.
+    max_bucket_load (bucket_max_load of the table) tightens the fixed-point
+    scale of the shared-memory sketch; 0 falls back to the element count.
     """
     _cuda(w, "w")
     _cuda(packed, "packed")
@@ -292,8 +295,28 @@ def sketch_dense(w: torch.Tensor, packed: torch.Tensor, d_out: int, d_in: int, k
         out = torch.empty(k, dtype=torch.float32, device=w.device)
         accumulate = False
     _lib.check(_lib.load().opus_sketch_dense(_ptr(w), int(bool(transposed)), _ptr(packed), _ptr(diag), int(d_out),
-                                            int(d_in), lo, hi, int(k), _ptr(out), int(accumulate), _stream(w)),
-               "opus_sketch_dense")
+                                            int(d_in), lo, hi, int(k), int(max_bucket_load), _ptr(out),
+                                            int(accumulate), _stream(w)), "opus_sketch_dense")
+    return out
+
+
+def sketch_dense_rows(w: torch.Tensor, packed: torch.Tensor, k: int, out: torch.Tensor | None = None,
+                      accumulate: bool = False, max_bucket_load: int = 0) -> torch.Tensor:
+    """CountSketch of every row of a [n, numel] matrix with one table of numel elements, [n, k] f32."""
+    _cuda(w, "w")
+    _cuda(packed, "packed")
+    if w.dim() != 2 or w.shape[1] != packed.numel():
+        raise ValueError(f"w must be [n, {packed.numel()}], got {tuple(w.shape)}")
+    w = _contig(w.to(torch.float32))
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(n, k, dtype=torch.float32, device=w.device)
+        accumulate = False
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < n * k:
+        raise ValueError("out must be a contiguous float32 tensor of at least [n, k]")
+    _lib.check(_lib.load().opus_sketch_dense_rows(_ptr(w), n, w.shape[1], _ptr(_contig(packed)), int(k),
+                                                 int(max_bucket_load), _ptr(out), int(accumulate), _stream(w)),
+               "opus_sketch_dense_rows")
     return out
 
 

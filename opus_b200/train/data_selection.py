@@ -580,7 +580,7 @@ def _score_and_similarity(model, device, batch_train, validation_loader, optimiz
     if CAPTURE_MODE == "stream":
         rows = batch_train["input_ids"].shape[0] + batch_val["input_ids"].shape[0]
         seq = min(batch_train["input_ids"].shape[1], batch_val["input_ids"].shape[1], score_len or 1 << 30)
-        if _use_passes(rows, trainable_layers, seq, device):
+        if _use_passes(rows, trainable_layers, seq, device, model, _has_muon(optimizer, preconditioner)):
             score, phis, cs, _ = capture_in_passes(model, device, batch_train, batch_val, optimizer,
                                                    trainable_layers, preconditioner, score_len, per_val=per_val,
                                                    keep_sketches=with_similarity)
@@ -696,47 +696,70 @@ def _score_and_similarity_stream(model, device, batch_train, batch_val, optimize
 # pass-splitting path at small sizes).
 CAPTURE_ROWS: int | None = None
 # Share of the free device memory a capture pass may fill with activations.
-CAPTURE_MEMORY_FRACTION = 0.75
+CAPTURE_MEMORY_FRACTION = 0.8
 # Activation bytes per token of a capture pass, in units of one (d_in + d_out)
 # row per capture layer in the model dtype (measured peaks: about 1.0 for
-# GPT-2 small in f32 and bf16, about 0.8 for GPT-2 XL in bf16; the margin
-# covers the logits and the allocator's fragmentation).
-CAPTURE_BYTES_PER_ROW = 1.25
+# GPT-2 small in f32 and bf16, 0.8 for GPT-2 XL in bf16, about 1.3 for a
+# Qwen3-style block with its SwiGLU MLP and q/k norms); the logits and their
+# gradient are counted apart, from the model's embedding width.
+CAPTURE_BYTES_PER_ROW = 1.5
 
 
-def rows_per_pass(trainable_layers, seq_len: int, device, reserve_bytes: int = 0) -> int:
+def rows_per_pass(trainable_layers, seq_len: int, device, reserve_bytes: int = 0, model=None,
+                  muon: bool = True) -> int:
     """Sequences one capture forward + backward can hold on the device.
 
     A pass keeps every layer's activations alive until its backward hook has
     run; measured on GPT-2-shaped models the peak is about one
     (d_in + d_out) row per token per capture layer, in the model dtype, plus
-    the logits.  The estimate takes CAPTURE_BYTES_PER_ROW times that per token
+    the logits.  The estimate takes CAPTURE_BYTES_PER_ROW times that per token,
+    plus the logits and their gradient (the model's largest embedding width),
     against CAPTURE_MEMORY_FRACTION of the free memory, after reserve_bytes
-    for what the round keeps (its candidate sketches).
+    for what the round keeps (its candidate sketches) and, when muon, room for
+    one d_out x d_out bf16 matrix per layer (the Muon S the first pass builds).
     """
     if CAPTURE_ROWS is not None:
         return max(1, int(CAPTURE_ROWS))
     device = torch.device(device)
     if device.type != "cuda":
         return 1 << 30
-    per_tok = 0
+    per_tok, elt = 0, 2
     for layer in trainable_layers:
         w = getattr(layer, "weight", None)
         if isinstance(w, torch.Tensor) and w.dim() == 2:
             per_tok += (w.shape[0] + w.shape[1]) * w.element_size()
-    per_tok = max(1, int(CAPTURE_BYTES_PER_ROW * per_tok))
+            reserve_bytes += 2 * w.shape[0] * w.shape[0] if muon else 0
+            elt = w.element_size()
+    per_tok = int(CAPTURE_BYTES_PER_ROW * per_tok)
+    if model is not None:
+        vocab = max((m.num_embeddings for m in model.modules() if isinstance(m, torch.nn.Embedding)), default=0)
+        per_tok += 2 * vocab * elt
+    per_tok = max(1, per_tok)
     free, _ = torch.cuda.mem_get_info(device)
     free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
     budget = CAPTURE_MEMORY_FRACTION * free - reserve_bytes
     return max(1, int(budget // (per_tok * max(1, seq_len))))
 
 
-def _use_passes(rows: int, trainable_layers, seq_len: int, device) -> bool:
+def _pairs(trainable_layers) -> int:
+    return sum(_pairs_per_layer(layer) for layer in trainable_layers)
+
+
+def _has_muon(optimizer, preconditioner) -> bool:
+    """Whether any capture layer may take the Muon preconditioner (and so an S matrix)."""
+    if preconditioner == "muon":
+        return True
+    if preconditioner != "auto":
+        return False
+    return any(_group_kind(g) == "muon" for opt in _as_opt_list(optimizer) for g in opt.param_groups)
+
+
+def _use_passes(rows: int, trainable_layers, seq_len: int, device, model=None, muon: bool = True) -> bool:
     projector = get_projector()
     if projector is None or not projector.enabled:
         return False  # the projection-off similarity needs every candidate's factors at once
-    reserve = 4 * projector.sketch_dim * rows * 2 * len(trainable_layers)
-    return rows > rows_per_pass(trainable_layers, seq_len, device, reserve)
+    reserve = 4 * projector.sketch_dim * rows * _pairs(trainable_layers)
+    return rows > rows_per_pass(trainable_layers, seq_len, device, reserve, model, muon)
 
 
 def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainable_layers, preconditioner, score_len,
@@ -769,8 +792,8 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
     n = batch_val["input_ids"].shape[0] if batch_val is not None else 0
     n_total = n if n_proxy_total is None else int(n_proxy_total)
     seq = min(batch_train["input_ids"].shape[1], score_len or 1 << 30)
-    reserve = 4 * k * (B + n) * 2 * len(trainable_layers)
-    step = rows_per_pass(trainable_layers, seq, device, reserve)
+    reserve = 4 * k * (B + n) * _pairs(trainable_layers)
+    step = rows_per_pass(trainable_layers, seq, device, reserve, model, _has_muon(optimizer, preconditioner))
     precond: dict = {}
     st: dict = {}
 

@@ -276,7 +276,8 @@ def score_shard(model, device, batch_train, proxy_share, n_proxy_total, optimize
 
     rows = batch_train["input_ids"].shape[0] + (proxy_share["input_ids"].shape[0] if proxy_share else 0)
     seq = min(batch_train["input_ids"].shape[1], score_len or 1 << 30)
-    if ds.CAPTURE_MODE == "stream" and ds._use_passes(rows, trainable_layers, seq, device):
+    if ds.CAPTURE_MODE == "stream" and ds._use_passes(rows, trainable_layers, seq, device, model,
+                                                      ds._has_muon(optimizer, preconditioner)):
         # the rank's rows do not fit one capture: proxy passes, one all-reduce, candidate passes
         score, phis, cs, _ = ds.capture_in_passes(
             model, device, batch_train, proxy_share, optimizer, trainable_layers, preconditioner, score_len,

@@ -113,7 +113,8 @@ class GradientProjector:
         flat = vector.flatten()
         numel = flat.numel()
         packed = self.packed_table(numel, param_id, flat.device)
-        return ops.sketch_dense(flat, packed, 1, numel, self.sketch_dim)
+        return ops.sketch_dense(flat, packed, 1, numel, self.sketch_dim,
+                                max_bucket_load=self.max_bucket_load(numel, param_id, flat.device))
 
     def project_batch(self, vectors: torch.Tensor, param_id: int) -> torch.Tensor:
         """CountSketch of each row of a [B, d] batch (random_projection.py:101-132)."""
@@ -121,10 +122,8 @@ class GradientProjector:
             return vectors
         B, d = vectors.shape
         packed = self.packed_table(d, param_id, vectors.device)
-        out = torch.empty(B, self.sketch_dim, dtype=torch.float32, device=vectors.device)
-        for b in range(B):
-            ops.sketch_dense(vectors[b], packed, 1, d, self.sketch_dim, out=out[b])
-        return out
+        return ops.sketch_dense_rows(vectors, packed, self.sketch_dim,  # every row in one launch
+                                     max_bucket_load=self.max_bucket_load(d, param_id, vectors.device))
 
     def project_full_gradient(self, dLdZ: torch.Tensor, a: torch.Tensor, param_id: int,
                               preconditioner_S: torch.Tensor | None = None,

@@ -9,7 +9,7 @@ from opus_b200 import _lib
 
 def test_library_loads_and_reports_version():
     lib = _lib.load()
-    assert lib.opus_abi_version() == 1
+    assert lib.opus_abi_version() == 2
     assert _lib.last_error() == "" or isinstance(_lib.last_error(), str)
 
 

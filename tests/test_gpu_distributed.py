@@ -35,13 +35,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, scenario, out_q):
+def _worker(rank, world, port, scenario, out_q, capture_rows=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    ds.CAPTURE_ROWS = capture_rows  # a small count splits each rank's capture into passes
     try:
         g = load_golden(f"wholepath_{scenario}")
         model, opt, loader, batch = rebuild(g, device=dev)
@@ -82,15 +83,16 @@ def _worker(rank, world, port, scenario, out_q):
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("scenario", ["adamw_proj", "muon_proj"])
-def test_sharded_selection_on_gpus(scenario):
+@pytest.mark.parametrize("scenario,capture_rows", [("adamw_proj", None), ("muon_proj", None), ("muon_proj", 1)])
+def test_sharded_selection_on_gpus(scenario, capture_rows):
     world = min(torch.cuda.device_count(), 3)
     if world < 2:
         pytest.skip("needs two or more GPUs")
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, scenario, out_q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, scenario, out_q, capture_rows))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}

@@ -117,6 +117,7 @@ SKETCH_SHAPES = [
     (3, 40, 136, 264, 40001),     # odd k: rows of phi start off 16-byte boundaries
     (2, 64, 128, 512, 131072),
     (5, 33, 136, 520, 8192),
+    (3, 200, 272, 520, 50000),    # 32-token stages: 45056 buckets in shared memory, the rest in L2
 ]
 
 
@@ -209,9 +210,14 @@ def test_sketch_dense(transposed, d_out, d_in, k):
     W = torch.randn(d_out, d_in, device=DEV)
     diag = torch.rand(d_out, d_in, device=DEV)
     src = W.T.contiguous() if transposed else W
-    out = ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, diag=diag)
+    load = ops.bucket_max_load(packed, k)
+    out = ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, diag=diag, max_bucket_load=load)
     want = orc.dense_sketch(W.cpu().numpy(), h, s, k, diag=diag.cpu().numpy())
     rel_close(out.cpu().numpy(), want, 1e-5, "dense sketch")
+    # without the load bound the share's element count bounds the fixed point: rounding about 100 times
+    # coarser (at most count / 2^31 of the share's largest value per element), still far inside 1e-3
+    coarse = ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, diag=diag)
+    rel_close(coarse.cpu().numpy(), want, 3e-4, "dense sketch, count bound")
 
 
 @pytest.mark.parametrize("transposed", [False, True])
@@ -222,12 +228,13 @@ def test_sketch_dense_row_shards_sum_to_whole(transposed):
     W = torch.randn(d_out, d_in, device=DEV)
     src = W.T.contiguous() if transposed else W
     whole = orc.dense_sketch(W.cpu().numpy(), h, s, k)
+    load = ops.bucket_max_load(packed, k)
     for world in (3, 8):
         acc = torch.zeros(k, device=DEV)
         for r in range(world):
             lo, hi = r * d_out // world, (r + 1) * d_out // world
             ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, out=acc, accumulate=True,
-                             rows=(lo, hi))
+                             rows=(lo, hi), max_bucket_load=load)
         rel_close(acc.cpu().numpy(), whole, 1e-5, f"row shards x{world}")
     empty = ops.sketch_dense(src, packed, d_out, d_in, k, transposed=transposed, rows=(5, 5))
     assert not empty.any()
@@ -464,3 +471,34 @@ def test_adam_diag_bit_exact(n):
     assert torch.equal(got, (v.sqrt() + 1e-8).reciprocal())
     odd = v[1:]  # a 4-byte-offset view takes the scalar path
     assert torch.equal(ops.adam_diag(odd, 1e-6), (odd.sqrt() + 1e-6).reciprocal())
+
+
+@pytest.mark.parametrize("n,d,k", [(5, 3000, 1024), (17, 4099, 4096), (1, 2_359_296, 16384)])
+def test_sketch_dense_rows_match_oracle(n, d, k):
+    """project_batch: every row of a [n, d] batch in one launch (odd d takes the scalar path)."""
+    h, s, packed = cuda_tables(d, 2, k)
+    X = torch.randn(n, d, device=DEV)
+    proj = GradientProjector(sketch_dim=k, seed=42, device="cuda")
+    got = proj.project_batch(X, 2)
+    ops.check_device_error("sketch_dense_rows")
+    assert got.shape == (n, k)
+    for i in range(n):
+        rel_close(got[i].cpu().numpy(), orc.dense_sketch(X[i].cpu().numpy()[None], h, s, k), 1e-5, f"row {i}")
+    one = proj.project_vector(X[0], 2)
+    rel_close(one.cpu().numpy(), got[0].cpu().numpy(), 1e-5, "project_vector == row 0")
+
+
+@pytest.mark.parametrize("stage_tokens", ["64", "32"])
+def test_sketch_gemm_stage_depths_match_oracle(stage_tokens, monkeypatch):
+    """A large sketch with either pipeline depth forced: 32768 or 45056 buckets in shared memory."""
+    monkeypatch.setenv("OPUS_SKETCH_STAGE_TOKENS", stage_tokens)
+    B, T, d_out, d_in, k = 3, 150, 256, 768, 65536
+    torch.manual_seed(11)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 4, k)
+    table = ops.build_sketch_table(packed, d_out, d_in)
+    phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=ops.bucket_max_load(packed, k))
+    ops.check_device_error("sketch_gemm stage depth")
+    want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
+    rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, {stage_tokens}-token stages")
