@@ -52,7 +52,11 @@ SKETCH_GEMM_DRAM_BYTES = 3.20e9
 SKETCH_GEMM_TRAFFIC_SOURCE = "profiles/kernels_c2.md: ncu capture of the operator bench, mean of two launches"
 # The same for the whole-path workloads: DRAM bytes of the sketch_gemm launches of one step, from an ncu
 # capture of a smaller case scaled by rows (the file named in each entry); recorded values, not measured here
-WHOLE_SKETCH_TRAFFIC: dict = {}
+WHOLE_SKETCH_TRAFFIC: dict = {
+    "gpt2-xl": {"bytes_per_step": 109.65e9 * 144 / 18,
+                "source": "profiles/sketch_gemm_wholepath_traffic.md: dram__bytes_read.sum + write of the 384 "
+                          "sketch_gemm launches of a 16 + 2 row round, scaled to 144 rows (an upper bound)"},
+}
 
 
 def parse_args():
@@ -656,6 +660,7 @@ def run_memory(args):
     sk = torch.empty(k, device=dev)
     table = torch.empty(ops.sketch_table_entries(d_out, d_in) * 4, dtype=torch.int32, device=dev)
     score = torch.empty(rows, device=dev)
+    copy_dst = torch.empty_like(v)
     cases = {
         "sketch_dense_flat": (8.0 * n, lambda: ops.sketch_dense(w, packed, d_out, d_in, k, out=sk,
                                                                 max_bucket_load=load)),
@@ -665,6 +670,8 @@ def run_memory(args):
                                                                         out=table)),
         "adam_diag": (8.0 * n, lambda: ops.adam_diag(v)),
         "sketch_dot": (4.0 * rows * k, lambda: ops.sketch_dot(phi, tau, out=score)),
+        # not a library kernel: torch's device copy of the same 41 MB, what a plain stream of this size reaches
+        "reference_torch_copy": (8.0 * n, lambda: copy_dst.copy_(v)),
     }
     burst, sustained, hbm, src = measured_peaks()
     out = {}
