@@ -343,3 +343,24 @@ def test_ppl_strategy_matches_reference(mode, ratio):
 def test_ghost_gram_cost_model(B, T, d_in, d_out, ghost):
     """The projection-off similarity picks the path that measured faster on a B200."""
     assert ds.ghost_gram_cheaper(B, T, d_in, d_out) is ghost
+
+
+def test_capture_pass_planning(monkeypatch):
+    """rows_per_pass: a forced count wins, a CPU device never splits; Muon detection by group or name."""
+    model = TinyLM(GCLinear)
+    layers = ds.find_GClayers(model)
+    assert ds.rows_per_pass(layers, 128, "cpu") >= 1 << 20
+    monkeypatch.setattr(ds, "CAPTURE_ROWS", 3)
+    assert ds.rows_per_pass(layers, 128, "cuda") == 3
+    assert ds._pairs(layers) == len(layers)
+    adam = torch.optim.AdamW(model.parameters())
+    muon = MuonLike(list(model.parameters())[:1])
+    assert not ds._has_muon(adam, "adamw") and ds._has_muon(adam, "muon")
+    assert ds._has_muon([adam, muon], "auto") and not ds._has_muon(adam, "auto")
+    assert not ds._has_muon([adam, muon], "sgd")
+
+
+def test_capture_in_passes_needs_the_projector():
+    ds.initialize_projector(enabled=False)
+    with pytest.raises(ValueError, match="projector"):
+        ds.capture_in_passes(None, "cpu", {"input_ids": torch.zeros(1, 4)}, None, None, [], "adamw", 4)
