@@ -1051,6 +1051,7 @@ def run_wholepath(args, rank, world, local_rank):
     torch.cuda.reset_peak_memory_stats(dev)
     held = torch.cuda.memory_allocated(dev)
     launches0 = ops.kernel_launches()
+    mem0 = torch.cuda.memory_stats(dev)
     s0, s1 = ev(), ev()
     with ClockSampler(local_rank) as clk, _lib.KernelTimer() as timer:
         s0.record()
@@ -1061,6 +1062,11 @@ def run_wholepath(args, rank, world, local_rank):
         s1.record()
         torch.cuda.synchronize()
     launches = ops.kernel_launches() - launches0
+    mem1 = torch.cuda.memory_stats(dev)
+    # cudaMalloc / cudaFree calls of torch's caching allocator inside the timed region (a free
+    # synchronises the device), and its out-of-memory retries (free the cache, allocate again)
+    allocator = {key: int(mem1.get(key, 0) - mem0.get(key, 0))
+                 for key in ("num_alloc_retries", "num_device_alloc", "num_device_free")}
     ops.check_device_error("whole-path timed region")
     peak = torch.cuda.max_memory_allocated(dev) - held
     kern = timer.summary()
@@ -1082,8 +1088,8 @@ def run_wholepath(args, rank, world, local_rank):
     if rows <= step:
         passes = [(part(buf), part(mine))]
     else:
-        passes = ([(part(buf[:0]), part(mine[lo:lo + step])) for lo in range(0, npx, step)]
-                  + [(part(buf[lo:lo + step]), part(mine[:0])) for lo in range(0, nc, step)])
+        passes = ([(part(buf[:0]), part(mine[lo:hi])) for lo, hi in ds.pass_ranges(npx, step)]
+                  + [(part(buf[lo:hi]), part(mine[:0])) for lo, hi in ds.pass_ranges(nc, step)])
 
     def capture_only():
         pc = {}
@@ -1160,6 +1166,7 @@ def run_wholepath(args, rank, world, local_rank):
     return {"cfg": cfg, "ms": sel_ms, "gemm_ms": gemm_ms_max, "flops": flops, "stage_ms": stage_ms,
             "stage_calls": stage_calls, "capture_ms": cap_ms, "train_ms": train_ms, "e2e": e2e,
             "clocks": clk.summary(), "launches": launches, "parity": parity, "peak_gb": peak / 1e9,
+            "allocator": allocator,
             "rows_per_pass": step, "kept": int(kept.shape[0])}
 
 
@@ -1352,7 +1359,7 @@ def emit_wholepath(args, res, world):
             "overhead_pct_of_step": round(100.0 * res["ms"] / res["train_ms"], 1),
             "capture_ms": round(res["capture_ms"], 2), "train_step_ms": round(res["train_ms"], 2),
             "stage_ms": res["stage_ms"], "stage_calls_per_step": res["stage_calls"],
-            "selection_peak_gb_above_model": round(res["peak_gb"], 2),
+            "selection_peak_gb_above_model": round(res["peak_gb"], 2), "allocator_in_timed_region": res["allocator"],
             "roofline": roofline, "cpu_baseline": cpu, "e2e": res["e2e"], "clocks": res["clocks"],
             "gpu_launches": res["launches"], "parity": res["parity"]}
     print(json.dumps(line), flush=True)

@@ -31,12 +31,13 @@
 // largest prefix of them that does (32768 buckets) and the updates of the
 // other buckets are f32 global atomic adds.
 //
-// Work: a job is one candidate's tiles for a contiguous range of o-blocks
-// (every column block); jobs are numbered candidate-major and dealt to CTAs
-// round-robin, so at any time the CTAs work on neighbouring candidates whose
-// operands stay resident in L2, and each job ends with one sketch flush.
+// Work: a job is a contiguous range of one candidate's tiles (o-block major);
+// jobs are numbered candidate-major and dealt to CTAs round-robin, so at any
+// time the CTAs work on neighbouring candidates whose operands stay resident
+// in L2, and each job ends with one sketch flush.
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 
 #include "opus_common.cuh"
 #include "sketch_layout.cuh"
@@ -102,14 +103,27 @@ __device__ __forceinline__ float4 ld_f4_hint(const float* p, uint64_t l2_policy)
   return v;
 }
 
-// O-block range [begin, end) of job j: each candidate's o-blocks are split
-// into `groups` contiguous ranges.
-__device__ __forceinline__ int job_ob_begin(int64_t job, int groups, int n_ob) {
-  return static_cast<int>((job % groups) * n_ob / groups);
+// Tile range [begin, end) of job j: each candidate's n_tiles tiles (o-block
+// major) are cut into units of `unit` tiles (a whole o-block, or one tile),
+// and the units into `groups` contiguous ranges.
+__device__ __forceinline__ int job_tile_begin(int64_t job, int groups, int n_tiles, int unit) {
+  return static_cast<int>((job % groups) * (n_tiles / unit) / groups) * unit;
 }
-__device__ __forceinline__ int job_ob_end(int64_t job, int groups, int n_ob) {
-  return static_cast<int>((job % groups + 1) * n_ob / groups);
+__device__ __forceinline__ int job_tile_end(int64_t job, int groups, int n_tiles, int unit) {
+  return static_cast<int>((job % groups + 1) * (n_tiles / unit) / groups) * unit;
 }
+
+// Tile `t` of a candidate's walk: o-block major (t = ob * n_cb + cb) or
+// column-block major (t = cb * n_ob + ob); plan_jobs picks the walk.
+struct TileWalk {
+  int n_ob, n_cb, cb_major;
+  __device__ __forceinline__ int ob(int t) const { return cb_major ? t % n_ob : t / n_cb; }
+  __device__ __forceinline__ int cb(int t) const { return cb_major ? t / n_ob : t % n_cb; }
+  // the last tile of a run that shares the outer operand
+  __device__ __forceinline__ bool last_inner(int t) const {
+    return cb_major ? t % n_ob == n_ob - 1 : t % n_cb == n_cb - 1;
+  }
+};
 
 // Bounded barrier over the epilogue threads (an mbarrier, so that a thread
 // that gave up cannot leave the others blocked forever).
@@ -151,7 +165,7 @@ template <int BK>
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_out,
-                       const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_ob,
+                       const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_tiles, int unit, int cb_major, int prefetch,
                        int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
                        int cap_log2, int* err, int dense, const float* __restrict__ dense_diag, int d_out,
                        int d_in, int accumulate) {
@@ -175,11 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* tile_max_bits = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Job j = (candidate j / groups, o-block group j % groups) covers that
-  // group's o-blocks x all column blocks; CTA i takes jobs i, i + grid, ...,
-  // so the CTAs work on neighbouring candidates at any time and each
-  // candidate's operands stay L2-resident while they are read.
+  // Job j = (candidate j / groups, tile range j % groups); CTA i takes jobs
+  // i, i + grid, ..., so the CTAs work on neighbouring candidates at any time
+  // and each candidate's operands stay L2-resident while they are read.
   const int64_t n_jobs = (int64_t)n_rows * groups;
+  const TileWalk walk{n_tiles / n_cb, n_cb, cb_major};
   const int n_kb = (seq_len + G::kBK - 1) / G::kBK;
 
   if (threadIdx.x == 0) {
@@ -219,10 +233,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       const uint64_t pol_last = l2_policy_evict_last(), pol_first = l2_policy_evict_first();
       for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
-      for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
-      for (int cb = 0; cb < n_cb && ok; ++cb) {
+      for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok;
+           ++tile) {
+        const int ob = walk.ob(tile), cb = walk.cb(tile);
         const int b = static_cast<int>(job / groups);
+        const bool next_in_job = tile + 1 < job_tile_end(job, groups, n_tiles, unit);
         for (int kb = 0; kb < n_kb; ++kb) {
+          if (prefetch > 0) {
+            // pull the operands `prefetch` k-blocks ahead (into the job's next tile) into L2,
+            // so that the stage loads, which only start when a stage frees up, hit L2
+            int pk = kb + prefetch, pt = tile;
+            if (pk >= n_kb && next_in_job) {
+              pk -= n_kb;
+              pt = tile + 1;
+            }
+            if (pk < n_kb) {
+#pragma unroll
+              for (int i = 0; i < kGBoxes; ++i)
+                tma_prefetch_l2_3d(&tm_g, walk.ob(pt) * kTileM + i * kBoxMN, pk * G::kBK, b);
+#pragma unroll
+              for (int i = 0; i < kABoxes; ++i)
+                tma_prefetch_l2_3d(&tm_a, walk.cb(pt) * kTileN + i * kBoxMN, pk * G::kBK, b);
+            }
+          }
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err, kDevTimeoutProducer)) {
             ok = false;
             break;
@@ -231,15 +264,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sg = stage_mem + (size_t)s * G::kStageBytes;
           uint8_t* sa = sg + G::kGTileBytes;
           const int t0 = kb * G::kBK;
-          // L2 policy: the dLdZ rows of this o-block are not read again after
-          // its last column block; the activations serve every o-block
-          const uint64_t gpol = cb == n_cb - 1 ? pol_first : pol_last;
+          // L2 policy: the outer operand of the walk (dLdZ rows of an o-block, or
+          // activation columns of a column block) is not read again after the
+          // last tile of its run; the inner operand serves every run
+          const bool drop = walk.last_inner(tile);
+          const uint64_t gpol = drop && !walk.cb_major ? pol_first : pol_last;
+          const uint64_t apol = drop && walk.cb_major ? pol_first : pol_last;
 #pragma unroll
           for (int i = 0; i < kGBoxes; ++i)
             tma_load_3d_hint(sg + i * G::kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b, gpol);
 #pragma unroll
           for (int i = 0; i < kABoxes; ++i)
-            tma_load_3d_hint(sa + i * G::kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, pol_last);
+            tma_load_3d_hint(sa + i * G::kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, apol);
           if (++s == stages) {
             s = 0;
             ph ^= 1;
@@ -256,8 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t aph = 0;
       bool ok = true;
       for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
-      for (int64_t u = 0; u < (int64_t)(job_ob_end(job, groups, n_ob) - job_ob_begin(job, groups, n_ob)) * n_cb && ok;
-           ++u) {
+      for (int u = job_tile_begin(job, groups, n_tiles, unit); u < job_tile_end(job, groups, n_tiles, unit) && ok; ++u) {
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, err, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
@@ -314,8 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t aph = 0;
     bool ok = true;
     for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
-    for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
-    for (int cb = 0; cb < n_cb && ok; ++cb) {
+    for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok; ++tile) {
+      const int ob = walk.ob(tile), cb = walk.cb(tile);
       const int b = static_cast<int>(job / groups);
       const int row0 = ob * kTileM + q * 32;  // first row of this warp's block
       // the diagonal of a chunk is loaded one chunk ahead (the first one before the accumulator
@@ -418,10 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool bad = false;
     bool ok = true;
     for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
-    for (int ob = job_ob_begin(job, groups, n_ob); ob < job_ob_end(job, groups, n_ob) && ok; ++ob)
-    for (int cb = 0; cb < n_cb && ok; ++cb) {
+    for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok; ++tile) {
       const int b = static_cast<int>(job / groups);
-      const int64_t tile = (int64_t)ob * n_cb + cb;
       float* out_row = phi + (int64_t)(b / rows_div) * k;
       if (smem_sketch && job != cur_job) {
         if (cur_job >= 0 && !flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, epi_bar,
@@ -437,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint4* tp = table + tile * kEntriesPerTile + r;
+      const uint4* tp = table + ((int64_t)walk.ob(tile) * n_cb + walk.cb(tile)) * kEntriesPerTile + r;
       const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
       if (smem_sketch && !scaled) {
         // First tile of this candidate in this CTA: scale from max |w G| over the tile.
@@ -582,27 +615,62 @@ int encode_operands(const void* dLdZ, const void* a, int n_rows, int seq_len, in
 
 struct JobPlan {
   int groups;
+  int unit;      // tiles per unit of a job range: 1, or a whole run of the outer index
+  int cb_major;  // tile walk (TileWalk)
   int64_t n_jobs;
   int grid;
 };
 
-// Split each candidate's o-blocks into `groups` jobs so that the rounds of
-// jobs over the SMs waste the least time: minimise ceil(jobs / SMs) x
-// (o-blocks per job), preferring larger jobs on ties.
-JobPlan plan_jobs(int n_rows, int n_ob) {
+// K-blocks of operands the producer pulls into L2 ahead of its stage loads
+// (OPUS_SKETCH_L2_PREFETCH, default 0: off).
+int l2_prefetch_blocks() {
+  if (const char* env = getenv("OPUS_SKETCH_L2_PREFETCH")) return atoi(env) > 0 ? atoi(env) : 0;
+  return 0;
+}
+
+// Walk and job cut, from measurements on the GPT-2-XL and Qwen3 layer shapes
+// (k = 65536 / 131072):
+//  - d_in <= d_out, or many rows: o-block major, jobs of single tiles, so a
+//    launch with few rows (a pass of the whole path, proxies merged into long
+//    rows) still fills every SM;
+//  - d_in > d_out with up to 64 rows (the passes of the whole path): column
+//    block major, jobs cut at whole columns.  Each job then loads each of its
+//    wide activation tiles once and re-reads only the narrow dLdZ tiles, which
+//    every candidate in flight keeps in L2 (6400 -> 1600 at 24 rows: 418
+//    against 348 TFLOP/s).
+// Each candidate's walk is split into `groups` jobs so that the rounds of jobs
+// over the SMs waste the least time: minimise ceil(jobs / SMs) x (tiles per
+// job + 1), the 1 standing for a job's fixed cost (its sketch flush and the
+// scale pass over its first tile), preferring larger jobs on ties.
+// OPUS_SKETCH_ORDER=ob|cb and OPUS_SKETCH_JOBS=tiles|lines force either choice.
+JobPlan plan_jobs(int n_rows, int d_out, int d_in) {
   const int sms = sm_count();
+  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
+  const int64_t n_tiles = (int64_t)n_ob * n_cb;
+  int cb_major = d_in > d_out && n_rows <= 64 ? 1 : 0;
+  if (const char* env = getenv("OPUS_SKETCH_ORDER")) {
+    if (strcmp(env, "cb") == 0) cb_major = 1;
+    if (strcmp(env, "ob") == 0) cb_major = 0;
+  }
+  bool lines = cb_major != 0;
+  if (const char* env = getenv("OPUS_SKETCH_JOBS")) {
+    if (strcmp(env, "lines") == 0) lines = true;
+    if (strcmp(env, "tiles") == 0) lines = false;
+  }
+  const int unit = lines ? (cb_major ? n_ob : n_cb) : 1;
+  const int64_t n_units = n_tiles / unit;
   int groups = 1;
   int64_t best = -1;
-  for (int q = 1; q <= n_ob; ++q) {
+  for (int64_t q = 1; q <= n_units; ++q) {
     const int64_t jobs = (int64_t)n_rows * q;
-    const int64_t cost = ((jobs + sms - 1) / sms) * ((n_ob + q - 1) / q);
+    const int64_t cost = ((jobs + sms - 1) / sms) * (((n_units + q - 1) / q) * unit + 1);
     if (best < 0 || cost < best) {
       best = cost;
-      groups = q;
+      groups = static_cast<int>(q);
     }
   }
   const int64_t n_jobs = (int64_t)n_rows * groups;
-  return {groups, n_jobs, static_cast<int>(n_jobs < sms ? n_jobs : sms)};
+  return {groups, unit, cb_major, n_jobs, static_cast<int>(n_jobs < sms ? n_jobs : sms)};
 }
 
 }  // namespace
@@ -685,12 +753,12 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   auto kernel = bk == 32 ? sketch_gemm_kernel<32> : sketch_gemm_kernel<64>;
   OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
-  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
-  const JobPlan jp = plan_jobs(n_rows, n_ob);
+  const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
+  const JobPlan jp = plan_jobs(n_rows, d_out, d_in);
   int* err = device_error_word();
   kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
-      tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_ob, n_cb,
-      jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
+      tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_tiles,
+      jp.unit, jp.cb_major, l2_prefetch_blocks(), n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
       accumulate);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
@@ -736,11 +804,11 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
     return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
   OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
-  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
-  const JobPlan jp = plan_jobs(n_rows, n_ob);
+  const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
+  const JobPlan jp = plan_jobs(n_rows, d_out, d_in);
   int* err = device_error_word();
-  sketch_gemm_kernel<64><<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_ob,
-                                                            n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
+  sketch_gemm_kernel<64><<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len,
+                                                            n_tiles, jp.unit, jp.cb_major, 0, n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
                                                             err, /*dense*/ 1, diag, d_out, d_in, accumulate);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());

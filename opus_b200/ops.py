@@ -7,6 +7,7 @@ tensor or a missing libopus_b200.so raises.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -134,6 +135,10 @@ def _as3d(t: torch.Tensor, name: str) -> torch.Tensor:
     return t
 
 
+# Longest row (in tokens) that sketch_gemm forms by merging samples that share an output row.
+MERGE_TOKENS = 16384
+
+
 def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int, rows_div: int = 1,
                 out: torch.Tensor | None = None, accumulate: bool = False,
                 max_bucket_load: int = 0) -> torch.Tensor:
@@ -151,6 +156,17 @@ def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int
     B, T, d_out = dLdZ.shape
     d_in = a.shape[2]
     rows = 0 if B == 0 else (B + rows_div - 1) // rows_div
+    # The sketch is linear, and the G of a row of r*T tokens is the sum of its
+    # r rows' G: samples that share an output row are merged into one long row
+    # (a view), which scatters into the sketch once instead of r times.  The
+    # merged row is kept to MERGE_TOKENS tokens: its G is one f32 accumulation
+    # over all of them, whose rounding error grows with the length.
+    g = math.gcd(rows_div, B)
+    r = max([d for d in range(1, g + 1) if g % d == 0 and d * T <= MERGE_TOKENS] or [1])
+    if r > 1:
+        dLdZ = _contig(dLdZ).view(B // r, r * T, d_out)
+        a = _contig(a).view(B // r, r * T, d_in)
+        B, T, rows_div = B // r, r * T, rows_div // r
     if out is None:
         out = torch.empty(rows, k, dtype=torch.float32, device=dLdZ.device)
         accumulate = False

@@ -741,6 +741,13 @@ def rows_per_pass(trainable_layers, seq_len: int, device, reserve_bytes: int = 0
     return max(1, int(budget // (per_tok * max(1, seq_len))))
 
 
+def pass_ranges(rows: int, step: int) -> list[tuple[int, int]]:
+    """Row ranges [lo, hi) of a capture in passes of at most `step` rows: as few passes as
+    that allows, of balanced sizes (no short last pass)."""
+    n_pass = -(-rows // max(1, step))
+    return [(rows * i // n_pass, rows * (i + 1) // n_pass) for i in range(n_pass)]
+
+
 def _pairs(trainable_layers) -> int:
     return sum(_pairs_per_layer(layer) for layer in trainable_layers)
 
@@ -810,8 +817,7 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
             st["cs"] = [0.0] * n_plans
 
     # 1. proxy passes
-    for lo in range(0, n, step):
-        hi = min(n, lo + step)
+    for lo, hi in pass_ranges(n, step):
 
         def proxy_handler(train_bs, val_bs, n_plans, lo=lo, hi=hi):
             ensure(n_plans)
@@ -836,8 +842,7 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
 
     # 2. candidate passes
     score = torch.zeros((B, n) if per_val else (B,), device=device, dtype=torch.float32)
-    for lo in range(0, B, step):
-        hi = min(B, lo + step)
+    for lo, hi in pass_ranges(B, step):
 
         def cand_handler(train_bs, val_bs, n_plans, lo=lo, hi=hi):
             ensure(n_plans)

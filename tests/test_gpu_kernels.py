@@ -177,6 +177,22 @@ def test_sketch_gemm_rows_div_and_accumulate():
     rel_close(out.cpu().numpy(), 2 * per, 1e-4, "accumulate")
 
 
+@pytest.mark.parametrize("B,T,d_out,d_in,k", [(8, 96, 384, 1024, 65536), (5, 64, 256, 512, 4096)])
+def test_sketch_gemm_merged_rows_match_sum_of_samples(B, T, d_out, d_in, k):
+    """rows_div = B: the whole batch becomes one row of B*T tokens whose tiles are dealt over the SMs."""
+    torch.manual_seed(B * k)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-2).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 3, k)
+    table = ops.build_sketch_table(packed, d_out, d_in)
+    load = ops.bucket_max_load(packed, k)
+    per = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
+    got = ops.sketch_gemm(g, a, table, k, rows_div=B, max_bucket_load=load)
+    ops.check_device_error("sketch_gemm merged rows")
+    assert got.shape == (1, k)
+    rel_close(got.cpu().numpy(), per.sum(0, keepdims=True), 1e-4, "merged rows")
+
+
 def test_sketch_gemm_f32_inputs_split():
     B, T, d_out, d_in, k = 3, 50, 96, 64, 1024
     g = torch.randn(B, T, d_out, device=DEV)
@@ -502,3 +518,27 @@ def test_sketch_gemm_stage_depths_match_oracle(stage_tokens, monkeypatch):
     ops.check_device_error("sketch_gemm stage depth")
     want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
     rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, {stage_tokens}-token stages")
+
+
+@pytest.mark.parametrize("order,jobs", [("ob", "tiles"), ("cb", "tiles"), ("ob", "lines"), ("cb", "lines")])
+@pytest.mark.parametrize("d_out,d_in", [(384, 768), (768, 256)])
+def test_sketch_gemm_tile_walks_match_oracle(order, jobs, d_out, d_in, monkeypatch):
+    """Either tile walk and either job cut (OPUS_SKETCH_ORDER / OPUS_SKETCH_JOBS forced), with and
+    without the diagonal: the same sketches, the per-sample gradients too."""
+    monkeypatch.setenv("OPUS_SKETCH_ORDER", order)
+    monkeypatch.setenv("OPUS_SKETCH_JOBS", jobs)
+    B, T, k = 5, 70, 8192
+    torch.manual_seed(d_out + d_in)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    diag = torch.rand(d_out, d_in, device=DEV) + 0.5
+    h, s, packed = cuda_tables(d_out * d_in, 5, k)
+    table = ops.build_sketch_table(packed, d_out, d_in, diag=diag)
+    phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=ops.bucket_max_load(packed, k))
+    dense = ops.per_sample_grad(g, a, diag=diag)
+    ops.check_device_error(f"sketch_gemm walk {order}/{jobs}")
+    gn, an = g.float().cpu().numpy(), a.float().cpu().numpy()
+    want = orc.project_full_gradient(gn, an, h, s, k, diag=diag.cpu().numpy())
+    rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, walk {order}/{jobs}")
+    want_dense = orc.per_sample_grads(gn, an) * diag.cpu().numpy()[None]
+    rel_close(dense.cpu().numpy().reshape(want_dense.shape), want_dense, 1e-5, f"dense, walk {order}/{jobs}")

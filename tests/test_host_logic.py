@@ -360,6 +360,17 @@ def test_capture_pass_planning(monkeypatch):
     assert not ds._has_muon([adam, muon], "sgd")
 
 
+@pytest.mark.parametrize("rows,step", [(128, 29), (16, 29), (0, 8), (7, 1), (144, 24), (5, 100)])
+def test_pass_ranges_cover_rows_in_balanced_passes(rows, step):
+    """As few passes as the step allows, contiguous, covering every row once, sizes within one."""
+    ranges = ds.pass_ranges(rows, step)
+    assert len(ranges) == -(-rows // step)
+    assert [lo for lo, _ in ranges[1:]] == [hi for _, hi in ranges[:-1]]
+    assert (ranges[0][0] if ranges else 0) == 0 and (ranges[-1][1] if ranges else 0) == rows
+    sizes = [hi - lo for lo, hi in ranges]
+    assert all(0 < n <= step for n in sizes) and (not sizes or max(sizes) - min(sizes) <= 1)
+
+
 def test_capture_in_passes_needs_the_projector():
     ds.initialize_projector(enabled=False)
     with pytest.raises(ValueError, match="projector"):
