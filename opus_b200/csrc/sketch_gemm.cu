@@ -7,7 +7,8 @@
 // w(o,c) = s(o,c) * D(o,c) from the precomputed table and adds it into bucket
 // h(o,c) of candidate b's sketch.  G_b is never written to HBM.
 //
-// Warp roles (320 threads, persistent, one CTA per SM):
+// Warp roles (320 threads, persistent, one CTA per SM; in a pair the MMA warp
+// of the second CTA stays idle):
 //   warp 0      TMA producer: 3-D tile loads of dLdZ and a into a ring of
 //               shared-memory stages (128-byte swizzle, MN-major operands);
 //   warp 1      TMEM allocation + single-thread UMMA issue into one of two
@@ -31,10 +32,17 @@
 // largest prefix of them that does (32768 buckets) and the updates of the
 // other buckets are f32 global atomic adds.
 //
-// Work: a job is a contiguous range of one candidate's tiles (o-block major);
-// jobs are numbered candidate-major and dealt to CTAs round-robin, so at any
-// time the CTAs work on neighbouring candidates whose operands stay resident
-// in L2, and each job ends with one sketch flush.
+// CTA pairs (sketches larger than one CTA's shared memory): a cluster of two
+// CTAs computes 256 x 256 tiles with tcgen05.mma.cta_group::2.  Each CTA
+// stages its own o-block's dLdZ rows and half of the activation columns (32 KB
+// per 64-token stage instead of 48 KB), so the shared memory it saves holds
+// more of the sketch; the leader issues the MMAs and each CTA's epilogue
+// scatters the accumulator rows of its own o-block.
+//
+// Work: a job is a contiguous range of one candidate's tiles (in the walk
+// that plan_jobs picks); jobs are numbered candidate-major and dealt to CTAs
+// (or pairs) round-robin, so at any time they work on neighbouring candidates
+// whose operands stay resident in L2, and each job ends with one sketch flush.
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -55,24 +63,30 @@ constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
 constexpr int kGBoxes = kTileM / kBoxMN;             // 2 boxes for the 128 weight rows
 constexpr int kABoxes = kTileN / kBoxMN;             // 4 boxes for the 256 weight columns
 // Pipeline stage geometry for BK tokens per stage (64: 48 KB stages; 32: 24 KB
-// stages, which leave room for more of a large sketch in shared memory).
-template <int BK>
+// stages, which leave room for more of a large sketch in shared memory).  A CTA
+// of a pair (PAIR) stages its own o-block's dLdZ rows and half of the tile's
+// activation columns: 32 KB at BK = 64.
+template <int BK, bool PAIR = false>
 struct Stage {
   static constexpr int kBK = BK;
   static constexpr int kKSteps = BK / kUmmaK;                     // MMAs per stage
   static constexpr int kBoxBytes = kBoxMN * 2 * BK;               // one 64-feature box
   static constexpr int kGTileBytes = kGBoxes * kBoxBytes;
-  static constexpr int kATileBytes = kABoxes * kBoxBytes;
+  static constexpr int kABoxesCta = PAIR ? kABoxes / 2 : kABoxes;  // activation boxes this CTA loads
+  static constexpr int kATileBytes = kABoxesCta * kBoxBytes;
   static constexpr int kStageBytes = kGTileBytes + kATileBytes;   // 48 KB at BK = 64, 24 KB at 32
   static constexpr uint32_t kLBO = kBoxBytes;
 };
 constexpr int kStageBytes64 = Stage<64>::kStageBytes;
 constexpr int kStageBytes32 = Stage<32>::kStageBytes;
+constexpr int kStageBytesPair64 = Stage<64, true>::kStageBytes;
+constexpr int kStageBytesPair32 = Stage<32, true>::kStageBytes;
 // MN-major SW128 canonical layout: 64 contiguous MN elements x 8 K rows per
 // 1024-B atom; atoms along K at SBO = 1024 B, along MN (next box) at LBO.
 constexpr uint32_t kSBO = 1024;
 constexpr uint32_t kKStepBytes = (kUmmaK / 8) * 1024;  // 2 atoms per MMA
 constexpr uint32_t kIdesc = make_idesc(/*bf16*/ 1, /*a MN-major*/ 1, /*b MN-major*/ 1, kTileM, kTileN);
+constexpr uint32_t kIdescPair = make_idesc(/*bf16*/ 1, /*a MN-major*/ 1, /*b MN-major*/ 1, 2 * kTileM, kTileN);
 constexpr int kTmemCols = 2 * kTileN;  // two accumulators
 
 struct SmemPlan {
@@ -161,15 +175,15 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
   return epi_sync(bar, phase, abort_flag, err);
 }
 
-template <int BK>
+template <int BK, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_out,
-                       const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_tiles, int unit, int cb_major, int prefetch,
+                       const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_tiles, int unit, int cb_major,
                        int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
                        int cap_log2, int* err, int dense, const float* __restrict__ dense_diag, int d_out,
                        int d_in, int accumulate) {
-  using G = Stage<BK>;
+  using G = Stage<BK, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -189,8 +203,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* tile_max_bits = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Job j = (candidate j / groups, tile range j % groups); CTA i takes jobs
-  // i, i + grid, ..., so the CTAs work on neighbouring candidates at any time
+  // PAIR: a cluster of two CTAs computes 256 x 256 tiles (an o-block pair by a
+  // column block) with tcgen05.mma.cta_group::2.  Each CTA stages its own
+  // o-block's 128 dLdZ rows and its half of the activation columns, the leader
+  // (rank 0) issues the MMAs for both, and each CTA's TMEM holds the accumulator
+  // rows of its own o-block, which its epilogue scatters into its own sketch.
+  // The walk then runs over o-block pairs; the CTA's o-block is 2 * pair + rank.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int64_t worker = PAIR ? blockIdx.x / 2 : blockIdx.x;  // the CTA, or the pair, that takes jobs
+  const int64_t n_workers = PAIR ? gridDim.x / 2 : gridDim.x;
+  const int n_ob_real = (d_out + kTileM - 1) / kTileM;
+  // Job j = (candidate j / groups, tile range j % groups); worker i takes jobs
+  // i, i + workers, ..., so the CTAs work on neighbouring candidates at any time
   // and each candidate's operands stay L2-resident while they are read.
   const int64_t n_jobs = (int64_t)n_rows * groups;
   const TileWalk walk{n_tiles / n_cb, n_cb, cb_major};
@@ -203,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiThreads);
+      mbar_init(&tempty[a], PAIR ? 2 * kEpiThreads : kEpiThreads);  // both epilogues release the leader's
     }
     mbar_init(epi_bar, kEpiThreads);
     mbar_init(drain_bar, 1);
@@ -216,12 +240,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_a);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   for (int64_t i = threadIdx.x; i < k_sm; i += kThreads) sk[i] = 0;
   tc_fence_before();
   __syncthreads();
+  // both CTAs' barriers are initialised before any load, commit or arrival crosses the pair
+  if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -232,35 +263,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       const uint64_t pol_last = l2_policy_evict_last(), pol_first = l2_policy_evict_first();
-      for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+      const uint32_t full_lead = PAIR ? mapa_shared(smem_u32(full), 0) : 0u;  // the leader's full barriers
+      for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
       for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok;
            ++tile) {
         const int ob = walk.ob(tile), cb = walk.cb(tile);
         const int b = static_cast<int>(job / groups);
-        const bool next_in_job = tile + 1 < job_tile_end(job, groups, n_tiles, unit);
         for (int kb = 0; kb < n_kb; ++kb) {
-          if (prefetch > 0) {
-            // pull the operands `prefetch` k-blocks ahead (into the job's next tile) into L2,
-            // so that the stage loads, which only start when a stage frees up, hit L2
-            int pk = kb + prefetch, pt = tile;
-            if (pk >= n_kb && next_in_job) {
-              pk -= n_kb;
-              pt = tile + 1;
-            }
-            if (pk < n_kb) {
-#pragma unroll
-              for (int i = 0; i < kGBoxes; ++i)
-                tma_prefetch_l2_3d(&tm_g, walk.ob(pt) * kTileM + i * kBoxMN, pk * G::kBK, b);
-#pragma unroll
-              for (int i = 0; i < kABoxes; ++i)
-                tma_prefetch_l2_3d(&tm_a, walk.cb(pt) * kTileN + i * kBoxMN, pk * G::kBK, b);
-            }
-          }
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], G::kStageBytes);
+          // a pair's stage is complete on the leader's barrier when both CTAs' bytes have landed
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], (PAIR ? 2 : 1) * G::kStageBytes);
           uint8_t* sg = stage_mem + (size_t)s * G::kStageBytes;
           uint8_t* sa = sg + G::kGTileBytes;
           const int t0 = kb * G::kBK;
@@ -270,12 +285,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool drop = walk.last_inner(tile);
           const uint64_t gpol = drop && !walk.cb_major ? pol_first : pol_last;
           const uint64_t apol = drop && walk.cb_major ? pol_first : pol_last;
+          if constexpr (PAIR) {
+            // this CTA's o-block (zero-filled past d_out) and its half of the columns
+            const uint32_t bar = full_lead + static_cast<uint32_t>(s) * 8u;
 #pragma unroll
-          for (int i = 0; i < kGBoxes; ++i)
-            tma_load_3d_hint(sg + i * G::kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b, gpol);
+            for (int i = 0; i < kGBoxes; ++i)
+              tma_load_3d_pair(sg + i * G::kBoxBytes, &tm_g, bar, (2 * ob + (int)rank) * kTileM + i * kBoxMN, t0, b,
+                               gpol);
 #pragma unroll
-          for (int i = 0; i < kABoxes; ++i)
-            tma_load_3d_hint(sa + i * G::kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, apol);
+            for (int i = 0; i < G::kABoxesCta; ++i)
+              tma_load_3d_pair(sa + i * G::kBoxBytes, &tm_a, bar,
+                               cb * kTileN + (int)rank * (kTileN / 2) + i * kBoxMN, t0, b, apol);
+          } else {
+#pragma unroll
+            for (int i = 0; i < kGBoxes; ++i)
+              tma_load_3d_hint(sg + i * G::kBoxBytes, &tm_g, &full[s], ob * kTileM + i * kBoxMN, t0, b, gpol);
+#pragma unroll
+            for (int i = 0; i < kABoxes; ++i)
+              tma_load_3d_hint(sa + i * G::kBoxBytes, &tm_a, &full[s], cb * kTileN + i * kBoxMN, t0, b, apol);
+          }
           if (++s == stages) {
             s = 0;
             ph ^= 1;
@@ -285,13 +313,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // (a pair's MMAs are issued by its leader alone)
+    if (lane == 0 && rank == 0) {
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+      // a commit arrives on this barrier in both CTAs of a pair (each at its own address)
+      auto commit_both = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(smem_u32(bar), 0));
+          umma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
+      for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
       for (int u = job_tile_begin(job, groups, n_tiles, unit); u < job_tile_end(job, groups, n_tiles, unit) && ok; ++u) {
         if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, err, kDevTimeoutMma)) break;
         tc_fence_after();
@@ -308,26 +346,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < G::kKSteps; ++kk) {
             const uint64_t da = make_sdesc_sw128(ag + kk * kKStepBytes, G::kLBO, kSBO);
             const uint64_t db = make_sdesc_sw128(aa + kk * kKStepBytes, G::kLBO, kSBO);
-            umma_bf16(d_tmem, da, db, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_bf16_pair(d_tmem, da, db, kIdescPair, (kb | kk) != 0 ? 1u : 0u);
+            else
+              umma_bf16(d_tmem, da, db, kIdesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          commit_both(&empty[s]);
           if (++s == stages) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        commit_both(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           aph ^= 1;
         }
       }
       // Drain: every MMA issued above must be complete before TMEM is freed.
-      umma_commit(drain_bar);
+      if constexpr (PAIR)
+        umma_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
+      else
+        umma_commit(drain_bar);
       mbar_wait(drain_bar, 0, nullptr, err, kDevTimeoutDrain);
     }
-  } else if (dense) {
+  } else if (!PAIR && dense) {
     // ------------------------------------------------- dense epilogue
     // Per-sample gradients: element (o, c) of G_b, times dense_diag[o, c]
     // when given, goes to phi[b, o * d_in + c].  Each warp stages its 32 rows
@@ -348,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t aph = 0;
     bool ok = true;
-    for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+    for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
     for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok; ++tile) {
       const int ob = walk.ob(tile), cb = walk.cb(tile);
       const int b = static_cast<int>(job / groups);
@@ -452,7 +496,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool scaled = false;    // a scale has been chosen for the current candidate
     bool bad = false;
     bool ok = true;
-    for (int64_t job = blockIdx.x; job < n_jobs && ok; job += gridDim.x)
+    // release an accumulator to the MMA issuer (a pair's is the leader's barrier)
+    const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
+    auto release = [&](int a) {
+      if constexpr (PAIR)
+        mbar_arrive_cluster(tempty_lead + static_cast<uint32_t>(a) * 8u);
+      else
+        mbar_arrive(&tempty[a]);
+    };
+    for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
     for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok; ++tile) {
       const int b = static_cast<int>(job / groups);
       float* out_row = phi + (int64_t)(b / rows_div) * k;
@@ -470,7 +522,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint4* tp = table + ((int64_t)walk.ob(tile) * n_cb + walk.cb(tile)) * kEntriesPerTile + r;
+      // this CTA's o-block; past d_out (the second o-block of a pair when their count is odd)
+      // the accumulator rows are zeros and there is no table tile: release the accumulator only
+      const int ob = PAIR ? 2 * walk.ob(tile) + (int)rank : walk.ob(tile);
+      if (PAIR && ob >= n_ob_real) {
+        tc_fence_before();
+        release(acc);
+        if (++acc == 2) {
+          acc = 0;
+          aph ^= 1;
+        }
+        continue;
+      }
+      const uint4* tp = table + ((int64_t)ob * n_cb + walk.cb(tile)) * kEntriesPerTile + r;
       const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
       if (smem_sketch && !scaled) {
         // First tile of this candidate in this CTA: scale from max |w G| over the tile.
@@ -529,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (jj == kChunksPerWarp - 1) {
           // all of this thread's accumulator reads are done: release the buffer
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);
+          release(acc);
         }
 #pragma unroll
         for (int p = 0; p < kPairsPerChunk; ++p) {
@@ -564,8 +628,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // a pair: the leader's MMAs are drained, both epilogues are done with TMEM and every
+  // arrival that crosses the pair has landed before either CTA frees TMEM or exits
+  if constexpr (PAIR) cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
+  }
 }
 
 SmemPlan plan_smem(int64_t k, int kStageBytes = kStageBytes64) {
@@ -621,13 +693,6 @@ struct JobPlan {
   int grid;
 };
 
-// K-blocks of operands the producer pulls into L2 ahead of its stage loads
-// (OPUS_SKETCH_L2_PREFETCH, default 0: off).
-int l2_prefetch_blocks() {
-  if (const char* env = getenv("OPUS_SKETCH_L2_PREFETCH")) return atoi(env) > 0 ? atoi(env) : 0;
-  return 0;
-}
-
 // Walk and job cut, from measurements on the GPT-2-XL and Qwen3 layer shapes
 // (k = 65536 / 131072):
 //  - d_in <= d_out, or many rows: o-block major, jobs of single tiles, so a
@@ -643,9 +708,9 @@ int l2_prefetch_blocks() {
 // job + 1), the 1 standing for a job's fixed cost (its sketch flush and the
 // scale pass over its first tile), preferring larger jobs on ties.
 // OPUS_SKETCH_ORDER=ob|cb and OPUS_SKETCH_JOBS=tiles|lines force either choice.
-JobPlan plan_jobs(int n_rows, int d_out, int d_in) {
-  const int sms = sm_count();
-  const int n_ob = ceil_div(d_out, kTileM), n_cb = ceil_div(d_in, kTileN);
+JobPlan plan_jobs(int n_rows, int d_out, int d_in, int n_ob, int workers) {
+  const int sms = workers;  // CTAs, or CTA pairs, that take jobs
+  const int n_cb = ceil_div(d_in, kTileN);
   const int64_t n_tiles = (int64_t)n_ob * n_cb;
   int cb_major = d_in > d_out && n_rows <= 64 ? 1 : 0;
   if (const char* env = getenv("OPUS_SKETCH_ORDER")) {
@@ -677,6 +742,90 @@ JobPlan plan_jobs(int n_rows, int d_out, int d_in) {
 }  // namespace opus
 
 using namespace opus;
+
+// Shared memory of one CTA of a pair: stages of `stage` bytes (32 KB at 64
+// tokens, 16 KB at 32).  The whole sketch with as many stages (3 to 6) as fit;
+// otherwise `pref_stages` stages and the largest prefix of the buckets next to them.
+SmemPlan plan_smem_pair(int64_t k, bool sketch_on_chip, size_t stage, int pref_stages) {
+  const size_t limit = static_cast<size_t>(max_smem_optin());
+  const size_t fixed = 1024 /*alignment slack*/ + 16 + 8 * (2 * 8 + 6) + 32;
+  if (!sketch_on_chip) {
+    for (int st = 6; st >= 2; --st)
+      if (fixed + st * stage <= limit) return {st, 0, fixed + st * stage};
+    return {0, 0, 0};
+  }
+  for (int st = 6; st >= 3; --st)
+    if (fixed + st * stage + (size_t)k * 4 <= limit) return {st, k, fixed + st * stage + (size_t)k * 4};
+  const int st = pref_stages;
+  if (fixed + st * stage >= limit) return {0, 0, 0};
+  int64_t k_sm = static_cast<int64_t>((limit - fixed - st * stage) / 4) & ~int64_t(1023);
+  if (k_sm > k) k_sm = k;
+  if (k_sm < 4096) k_sm = 0;
+  return {st, k_sm, fixed + st * stage + (size_t)k_sm * 4};
+}
+
+// The CTA-pair launch of opus_sketch_gemm (OPUS_SKETCH_PAIR=1): clusters of two
+// CTAs, as many as the device keeps resident, each pair taking jobs over
+// o-block pairs x column blocks.
+int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, int n_rows, int seq_len,
+                int d_out, int d_in, int64_t k, int max_bucket_load, int rows_div, float cap, int cap_log2,
+                int accumulate, cudaStream_t st) {
+  // Pipeline, measured with interleaved launches at 24 and 128 rows: up to k = 65536 two
+  // 64-token stages (32 KB) next to 40960 buckets beat three stages next to 32768 (1600 -> 6400:
+  // 491 against 470 TFLOP/s at 24 rows); at k = 131072 three 32-token stages (16 KB) next to
+  // 45056 buckets win (2048 -> 6144: 459 against 426).  OPUS_SKETCH_PAIR_STAGE_TOKENS (64 or
+  // 32) and OPUS_SKETCH_PAIR_STAGES force either.
+  int bk = k > 65536 ? 32 : 64;
+  if (const char* env = getenv("OPUS_SKETCH_PAIR_STAGE_TOKENS")) bk = atoi(env) == 32 ? 32 : 64;
+  int pref = bk == 32 ? 3 : 2;
+  if (const char* env = getenv("OPUS_SKETCH_PAIR_STAGES")) pref = atoi(env) >= 2 && atoi(env) <= 6 ? atoi(env) : pref;
+  const SmemPlan plan = plan_smem_pair(k, max_bucket_load > 0, bk == 32 ? kStageBytesPair32 : kStageBytesPair64,
+                                       pref);
+  if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small for CTA pairs");
+  CUtensorMap tm_g, tm_a;
+  if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
+  auto kernel = bk == 32 ? sketch_gemm_kernel<32, true> : sketch_gemm_kernel<64, true>;
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(plan.bytes)));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = plan.bytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int pairs = 0;
+  OPUS_CUDA_TRY(cudaOccupancyMaxActiveClusters(&pairs, kernel, &cfg));
+  if (pairs <= 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: no CTA pair fits on the device");
+  const int n_op = ceil_div(ceil_div(d_out, kTileM), 2), n_cb = ceil_div(d_in, kTileN);
+  const JobPlan jp = plan_jobs(n_rows, d_out, d_in, n_op, pairs);
+  cfg.gridDim = dim3(2 * jp.grid, 1, 1);
+  int* err = device_error_word();
+  OPUS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, tm_g, tm_a, tm_g /*no dense output*/,
+                                   reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_op * n_cb, jp.unit,
+                                   jp.cb_major, n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2,
+                                   err, /*dense*/ 0, static_cast<const float*>(nullptr), d_out, d_in, accumulate));
+  ::opus::note_launch();
+  return OPUS_OK;
+}
+
+// CTA pairs serve sketches that do not fit one CTA's shared memory next to its
+// stages (k > 32768) with a fixed-point bound, on layers of two o-blocks or
+// more: each CTA then stages half of a tile's activation columns, and the
+// shared memory saved holds more of the sketch (40960 or 45056 buckets against
+// 32768), so fewer updates go to L2.  Below that the one-CTA kernel is faster
+// (768 -> 3072 at k = 16384: 702 against 663 TFLOP/s at 24 rows).
+// OPUS_SKETCH_PAIR=1 or 0 forces either.
+bool use_pairs(int d_out, int64_t k, int max_bucket_load) {
+  if (ceil_div(d_out, kTileM) < 2) return false;
+  if (const char* env = getenv("OPUS_SKETCH_PAIR")) return strcmp(env, "1") == 0;
+  return max_bucket_load > 0 && k > 32768;
+}
 
 extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
                                 int d_in, const void* table, int64_t table_entries_given, int64_t k,
@@ -736,6 +885,9 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
       }
     }
   }
+  if (use_pairs(d_out, k, max_bucket_load))
+    return launch_pair(dLdZ, a, table, phi, n_rows, seq_len, d_out, d_in, k, max_bucket_load, rows_div, cap,
+                       cap_log2, accumulate, st);
   const int stage_bytes = bk == 32 ? kStageBytes32 : kStageBytes64;
   if (max_bucket_load <= 0 && plan.k_sm > 0) {
     // No usable bound: every update goes to global f32 atomics; use the smem for stages.
@@ -750,15 +902,15 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   }
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  auto kernel = bk == 32 ? sketch_gemm_kernel<32> : sketch_gemm_kernel<64>;
+  auto kernel = bk == 32 ? sketch_gemm_kernel<32, false> : sketch_gemm_kernel<64, false>;
   OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
-  const JobPlan jp = plan_jobs(n_rows, d_out, d_in);
+  const JobPlan jp = plan_jobs(n_rows, d_out, d_in, ceil_div(d_out, kTileM), sm_count());
   int* err = device_error_word();
   kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
       tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_tiles,
-      jp.unit, jp.cb_major, l2_prefetch_blocks(), n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
+      jp.unit, jp.cb_major, n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
       accumulate);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
@@ -802,13 +954,13 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
   const SmemPlan plan = plan_smem(kStagingWords);
   if (plan.stages == 0 || plan.k_sm < kStagingWords)
     return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
-  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
-  const JobPlan jp = plan_jobs(n_rows, d_out, d_in);
+  const JobPlan jp = plan_jobs(n_rows, d_out, d_in, ceil_div(d_out, kTileM), sm_count());
   int* err = device_error_word();
-  sketch_gemm_kernel<64><<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len,
-                                                            n_tiles, jp.unit, jp.cb_major, 0, n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
+  sketch_gemm_kernel<64, false><<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len,
+                                                            n_tiles, jp.unit, jp.cb_major, n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
                                                             err, /*dense*/ 1, diag, d_out, d_in, accumulate);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());

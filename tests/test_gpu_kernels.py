@@ -139,6 +139,21 @@ def test_sketch_gemm_matches_oracle(B, T, d_out, d_in, k, fixed_point):
     rel_close(phi.cpu().numpy(), want, 1e-4, "phi")
 
 
+@pytest.mark.parametrize("B,T,d_out,d_in,k", [sh for sh in SKETCH_SHAPES if sh[4] > 32768 and sh[2] > 128])
+def test_sketch_gemm_one_cta_large_sketch_matches_oracle(B, T, d_out, d_in, k, monkeypatch):
+    """The one-CTA kernel at the sketch sizes where CTA pairs are the default."""
+    monkeypatch.setenv("OPUS_SKETCH_PAIR", "0")
+    torch.manual_seed(B * 1000 + T)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 3, k)
+    table = ops.build_sketch_table(packed, d_out, d_in)
+    phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=ops.bucket_max_load(packed, k))
+    ops.check_device_error("sketch_gemm one CTA")
+    want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k)
+    rel_close(phi.cpu().numpy(), want, 1e-4, "phi, one CTA")
+
+
 def test_sketch_gemm_outliers_and_nonfinite():
     """Updates far above the first tile's scale, and NaN, take the exact f32 path.
 
@@ -506,7 +521,9 @@ def test_sketch_dense_rows_match_oracle(n, d, k):
 
 @pytest.mark.parametrize("stage_tokens", ["64", "32"])
 def test_sketch_gemm_stage_depths_match_oracle(stage_tokens, monkeypatch):
-    """A large sketch with either pipeline depth forced: 32768 or 45056 buckets in shared memory."""
+    """A large sketch on the one-CTA kernel with either pipeline depth forced: 32768 or 45056
+    buckets in shared memory (CTA pairs, the default at this size, are off)."""
+    monkeypatch.setenv("OPUS_SKETCH_PAIR", "0")
     monkeypatch.setenv("OPUS_SKETCH_STAGE_TOKENS", stage_tokens)
     B, T, d_out, d_in, k = 3, 150, 256, 768, 65536
     torch.manual_seed(11)
