@@ -53,7 +53,7 @@ SKETCH_GEMM_TRAFFIC_SOURCE = "profiles/kernels_c2.md: ncu capture of the operato
 # The same for the whole-path workloads: DRAM bytes of the sketch_gemm launches of one step, from an ncu
 # capture of a smaller case scaled by rows (the file named in each entry); recorded values, not measured here
 WHOLE_SKETCH_TRAFFIC: dict = {
-    "gpt2-xl": {"bytes_per_step": 109.65e9 * 144 / 18,
+    "gpt2-xl": {"bytes_per_step": 113.41e9 * 144 / 18,
                 "source": "profiles/sketch_gemm_wholepath_traffic.md: dram__bytes_read.sum + write of the 384 "
                           "sketch_gemm launches of a 16 + 2 row round, scaled to 144 rows (an upper bound)"},
 }
