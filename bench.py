@@ -1078,8 +1078,8 @@ def run_wholepath(args, rank, world, local_rank):
 
     # stage 1 alone: the same forward/backward passes with hooks that do nothing
     rows = nc + npx
-    step = ds.rows_per_pass(layers, seq, dev, 4 * cfg["k"] * rows * ds._pairs(layers), model,
-                            ds._has_muon(opt, precond))
+    step = ds.rows_per_pass(layers, seq, dev, 4 * cfg["k"] * rows * ds._pairs(layers)
+                            + ds._adamw_table_bytes(layers, opt, precond), model, ds._has_muon(opt, precond))
     mine = prox[rank * npx:(rank + 1) * npx] if world > 1 else prox
 
     def part(x):
@@ -1094,7 +1094,8 @@ def run_wholepath(args, rank, world, local_rank):
     def capture_only():
         pc = {}
         for bt, bv in passes:
-            ds.stream_capture(model, dev, bt, bv, opt, layers, precond, seq, lambda *a: (lambda pl: None), pc)
+            ds.stream_capture(model, dev, bt, bv, opt, layers, precond, seq, lambda *a: (lambda pl: None), pc,
+                              fold_scale=True)
 
     capture_only()
     c0, c1 = ev(), ev()

@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define OPUS_ABI_VERSION 2
+#define OPUS_ABI_VERSION 3
 
 #define OPUS_OK 0
 #define OPUS_ERR_INVALID 1     /* bad argument (maps to ValueError) */
@@ -150,6 +150,10 @@ OPUS_API int opus_build_sketch_table(const uint32_t* packed, const float* diag, 
  *         fixed-point shared-memory sketch so no bucket can overflow; <= 0
  *         sends every update to f32 global atomics instead (exact, slower).
  *   accumulate = 0 zeroes phi first.
+ *   alpha: f32 factor on every update (1 for the reference's values).  The
+ *         capture's per-sample scaling of dL/dZ by the batch size
+ *         (OPUS/layers/linear.py:118-119) can ride here instead of a pass
+ *         over dL/dZ.
  * Accuracy: each update is rounded to a power-of-two quantum of at most
  * 2^-(log2(2^31/max_bucket_load) - 3) times the largest |w G| of the
  * candidate's first tile in the CTA (~1e-6 relative for GPT-2 layers);
@@ -159,7 +163,7 @@ OPUS_API int opus_build_sketch_table(const uint32_t* packed, const float* diag, 
  */
 OPUS_API int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
                      int d_in, const void* table, int64_t table_entries, int64_t k, int max_bucket_load,
-                     int rows_div, float* phi, int accumulate, void* stream);
+                     int rows_div, float* phi, int accumulate, float alpha, void* stream);
 
 /*
  * G-ghost (projection off) — exact per-sample gradients for the similarity.

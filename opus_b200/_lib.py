@@ -36,7 +36,7 @@ SIGNATURES: dict[str, tuple] = {
     "opus_sketch_table_entries": (_c_i64, [_c_int, _c_int]),
     "opus_build_sketch_table": (_c_int, [_c_p, _c_p, _c_p, _c_f32, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "opus_sketch_gemm": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_i64, _c_int,
-                                  _c_int, _c_p, _c_int, _c_p]),
+                                  _c_int, _c_p, _c_int, _c_f32, _c_p]),
     "opus_ghost_gram": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f32, _c_p, _c_int,
                                  _c_p]),
     "opus_per_sample_grad": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_int, _c_p]),

@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_tiles, int unit, int cb_major,
                        int n_cb, int groups, int64_t k, int rows_div, int stages, int64_t k_sm, float cap,
                        int cap_log2, int* err, int dense, const float* __restrict__ dense_diag, int d_out,
-                       int d_in, int accumulate) {
+                       int d_in, int accumulate, float alpha) {
   using G = Stage<BK, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -227,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], PAIR ? 2 * kEpiThreads : kEpiThreads);  // both epilogues release the leader's
+      // one arrival per epilogue warp (both CTAs' warps on a pair's leader)
+      mbar_init(&tempty[a], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(epi_bar, kEpiThreads);
     mbar_init(drain_bar, 1);
@@ -431,8 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem_base + lane_addr + static_cast<uint32_t>(acc * kTileN) + j * kChunkCols, v);
         tmem_ld_wait();
         if (jj == kChunksPerWarp - 1) {
+          // the warp's accumulator reads are done: one lane releases the buffer
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
         }
         if (row0 >= d_out || c0 >= d_in) continue;  // the whole block lies outside the output
         if (lane == 0) bulk_wait_group_read<1>();
@@ -496,13 +499,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool scaled = false;    // a scale has been chosen for the current candidate
     bool bad = false;
     bool ok = true;
-    // release an accumulator to the MMA issuer (a pair's is the leader's barrier)
+    // release an accumulator to the MMA issuer (a pair's is the leader's barrier) once the
+    // whole warp is done with it: one arrival per warp
     const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
     auto release = [&](int a) {
-      if constexpr (PAIR)
-        mbar_arrive_cluster(tempty_lead + static_cast<uint32_t>(a) * 8u);
-      else
-        mbar_arrive(&tempty[a]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(tempty_lead + static_cast<uint32_t>(a) * 8u);
+        else
+          mbar_arrive(&tempty[a]);
+      }
     };
     for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
     for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok; ++tile) {
@@ -526,7 +534,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the accumulator rows are zeros and there is no table tile: release the accumulator only
       const int ob = PAIR ? 2 * walk.ob(tile) + (int)rank : walk.ob(tile);
       if (PAIR && ob >= n_ob_real) {
-        tc_fence_before();
         release(acc);
         if (++acc == 2) {
           acc = 0;
@@ -550,8 +557,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int p = 0; p < kPairsPerChunk; ++p) {
             const uint4 e = ent[p];
-            const float x0 = fabsf(__uint_as_float(v[2 * p]) * __uint_as_float(e.z));
-            const float x1 = fabsf(__uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w));
+            const float x0 = fabsf(__uint_as_float(v[2 * p]) * __uint_as_float(e.z) * alpha);
+            const float x1 = fabsf(__uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w) * alpha);
             if (x0 <= 3.0e38f) m = fmaxf(m, x0);   // finite values only
             if (x1 <= 3.0e38f) m = fmaxf(m, x1);
           }
@@ -590,18 +597,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[32];
         tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
         tmem_ld_wait();
-        if (jj == kChunksPerWarp - 1) {
-          // all of this thread's accumulator reads are done: release the buffer
-          tc_fence_before();
-          release(acc);
-        }
+        if (jj == kChunksPerWarp - 1) release(acc);  // the warp's accumulator reads are done
 #pragma unroll
         for (int p = 0; p < kPairsPerChunk; ++p) {
           const uint4 e = ent[p];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t bucket = h ? e.y : e.x;
-            const float x = __uint_as_float(v[2 * p + h]) * __uint_as_float(h ? e.w : e.z);
+            const float x = __uint_as_float(v[2 * p + h]) * __uint_as_float(h ? e.w : e.z) * alpha;
             if (bucket >= kk32) {
               bad = true;
               continue;
@@ -769,7 +772,7 @@ SmemPlan plan_smem_pair(int64_t k, bool sketch_on_chip, size_t stage, int pref_s
 // o-block pairs x column blocks.
 int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, int n_rows, int seq_len,
                 int d_out, int d_in, int64_t k, int max_bucket_load, int rows_div, float cap, int cap_log2,
-                int accumulate, cudaStream_t st) {
+                int accumulate, float alpha, cudaStream_t st) {
   // Pipeline, measured with interleaved launches at 24 and 128 rows: up to k = 65536 two
   // 64-token stages (32 KB) next to 40960 buckets beat three stages next to 32768 (1600 -> 6400:
   // 491 against 470 TFLOP/s at 24 rows); at k = 131072 three 32-token stages (16 KB) next to
@@ -809,7 +812,8 @@ int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, 
   OPUS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, tm_g, tm_a, tm_g /*no dense output*/,
                                    reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_op * n_cb, jp.unit,
                                    jp.cb_major, n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2,
-                                   err, /*dense*/ 0, static_cast<const float*>(nullptr), d_out, d_in, accumulate));
+                                   err, /*dense*/ 0, static_cast<const float*>(nullptr), d_out, d_in, accumulate,
+                                   alpha));
   ::opus::note_launch();
   return OPUS_OK;
 }
@@ -829,7 +833,8 @@ bool use_pairs(int d_out, int64_t k, int max_bucket_load) {
 
 extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
                                 int d_in, const void* table, int64_t table_entries_given, int64_t k,
-                                int max_bucket_load, int rows_div, float* phi, int accumulate, void* stream) {
+                                int max_bucket_load, int rows_div, float* phi, int accumulate, float alpha,
+                                void* stream) {
   if (dtype != OPUS_DTYPE_BF16)
     return set_error(OPUS_ERR_UNSUPPORTED,
                      "sketch_gemm: operands must be bf16 (split f32 operands into bf16 hi/lo with opus_split_bf16)");
@@ -887,7 +892,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   }
   if (use_pairs(d_out, k, max_bucket_load))
     return launch_pair(dLdZ, a, table, phi, n_rows, seq_len, d_out, d_in, k, max_bucket_load, rows_div, cap,
-                       cap_log2, accumulate, st);
+                       cap_log2, accumulate, alpha, st);
   const int stage_bytes = bk == 32 ? kStageBytes32 : kStageBytes64;
   if (max_bucket_load <= 0 && plan.k_sm > 0) {
     // No usable bound: every update goes to global f32 atomics; use the smem for stages.
@@ -910,8 +915,8 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   int* err = device_error_word();
   kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
       tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_tiles,
-      jp.unit, jp.cb_major, n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0, nullptr, d_out, d_in,
-      accumulate);
+      jp.unit, jp.cb_major, n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0,
+      nullptr, d_out, d_in, accumulate, alpha);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;
@@ -959,9 +964,9 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
   const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
   const JobPlan jp = plan_jobs(n_rows, d_out, d_in, ceil_div(d_out, kTileM), sm_count());
   int* err = device_error_word();
-  sketch_gemm_kernel<64, false><<<jp.grid, kThreads, plan.bytes, st>>>(tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len,
-                                                            n_tiles, jp.unit, jp.cb_major, n_cb, jp.groups, numel, 1, plan.stages, plan.k_sm, 0.0f, 0,
-                                                            err, /*dense*/ 1, diag, d_out, d_in, accumulate);
+  sketch_gemm_kernel<64, false><<<jp.grid, kThreads, plan.bytes, st>>>(
+      tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_tiles, jp.unit, jp.cb_major, n_cb, jp.groups, numel, 1,
+      plan.stages, plan.k_sm, 0.0f, 0, err, /*dense*/ 1, diag, d_out, d_in, accumulate, 1.0f);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;

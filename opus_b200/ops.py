@@ -141,13 +141,14 @@ MERGE_TOKENS = 16384
 
 def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int, rows_div: int = 1,
                 out: torch.Tensor | None = None, accumulate: bool = False,
-                max_bucket_load: int = 0) -> torch.Tensor:
-    """phi[b // rows_div] (+)= CountSketch(w o (dLdZ_b^T a_b)) for every candidate b.
+                max_bucket_load: int = 0, alpha: float = 1.0) -> torch.Tensor:
+    """phi[b // rows_div] (+)= alpha * CountSketch(w o (dLdZ_b^T a_b)) for every candidate b.
 
     dLdZ [B, T, d_out] and a [B, T, d_in] in bf16 (tensor cores directly) or
     f32 (split into bf16 hi/lo; hi*hi + hi*lo + lo*hi accumulated).
     max_bucket_load (see bucket_max_load) enables the fixed-point
     shared-memory sketch; 0 adds every update with f32 global atomics.
+    alpha multiplies every update in f32 (the per-sample scaling of dL/dZ).
     """
     _cuda(dLdZ, "dLdZ")
     _cuda(a, "a")
@@ -178,7 +179,7 @@ def sketch_gemm(dLdZ: torch.Tensor, a: torch.Tensor, table: torch.Tensor, k: int
     def launch(g: torch.Tensor, x: torch.Tensor, acc: bool) -> None:
         _lib.check(lib.opus_sketch_gemm(_ptr(g), _ptr(x), _lib.DTYPE_BF16, B, T, d_out, d_in, _ptr(table), n_entries,
                                         int(k), int(max_bucket_load), int(rows_div), _ptr(out), int(acc),
-                                        _stream(g)),
+                                        float(alpha), _stream(g)),
                    "opus_sketch_gemm")
 
     if dLdZ.dtype == torch.bfloat16 and a.dtype == torch.bfloat16:

@@ -249,10 +249,12 @@ def _random_windows(x, win_len, align_to=128, g=None):
 
 # ----------------------------------------------------------------- scoring core
 class _Pair:
-    __slots__ = ("p", "g_t", "a_t", "g_v", "a_v")
+    """One (dL/dZ, A) factor pair split into candidate and proxy rows; `scale` multiplies dL/dZ
+    (1 when the layer already applied its per-sample scaling)."""
+    __slots__ = ("p", "g_t", "a_t", "g_v", "a_v", "scale")
 
-    def __init__(self, p, g_t, a_t, g_v, a_v):
-        self.p, self.g_t, self.a_t, self.g_v, self.a_v = p, g_t, a_t, g_v, a_v
+    def __init__(self, p, g_t, a_t, g_v, a_v, scale=1.0):
+        self.p, self.g_t, self.a_t, self.g_v, self.a_v, self.scale = p, g_t, a_t, g_v, a_v, scale
 
 
 def capture_pairs(model, batch_train, validation_loader, trainable_layers, score_len=512, batch_val=None):
@@ -409,8 +411,25 @@ def _capture_forward(model, batch_train, validation_loader, trainable_layers, sc
     return loss, [trainable_layers[i] for i in keep], [raw[i] for i in keep], train_bs, val_bs
 
 
-def _layer_pairs(layer, zg, train_bs):
-    """(dL/dZ, A) factor pairs of one layer split into candidate / proxy halves (data_selection.py:413-445)."""
+def _plain_gclinear(layer) -> bool:
+    """A capture layer whose factors are this package's GCLinear ones: (dL/dZ * N, A)."""
+    from ..layers.linear import GCLinear
+    return isinstance(layer, GCLinear) and type(layer).pe_grad_gradcomp is GCLinear.pe_grad_gradcomp
+
+
+def _layer_pairs(layer, zg, train_bs, fold_scale=False):
+    """(dL/dZ, A) factor pairs of one layer split into candidate / proxy halves (data_selection.py:413-445).
+
+    fold_scale: for this package's GCLinear on 3-D inputs, hand over dL/dZ as
+    autograd gives it and the per-sample factor N (linear.py:118-119) as the
+    pair's scale, which the sketch kernel applies in f32, instead of a pass
+    over dL/dZ that writes dL/dZ * N.
+    """
+    if fold_scale and zg.dim() == 3 and _plain_gclinear(layer) and layer.layer_input is not None \
+            and layer.layer_input.dim() == 3:
+        g, a = zg.detach(), layer.layer_input.detach()
+        return [_Pair(getattr(layer, "weight", None), g[:train_bs], a[:train_bs], g[train_bs:], a[train_bs:],
+                      float(zg.shape[0]))]
     parts = layer.pe_grad_gradcomp(zg, per_sample=True)
     if isinstance(parts, tuple) and len(parts) == 2 and all(isinstance(x, torch.Tensor) for x in parts):
         parts = [parts]
@@ -430,13 +449,15 @@ class LayerPlan:
 
     g_t is the candidate dL/dZ after the Muon transform (if any); c is the
     float32 product C_t * layer_scale; exp_avg_sq / eps give the AdamW
-    diagonal folded into the candidate sketch table.
+    diagonal folded into the candidate sketch table; gscale is the factor
+    still owed to dL/dZ (its per-sample scaling, when the capture left it to
+    the sketch kernel), 1 otherwise.
     """
-    __slots__ = ("pid", "kind", "g_t", "a_t", "g_v", "a_v", "c", "exp_avg_sq", "eps")
+    __slots__ = ("pid", "kind", "g_t", "a_t", "g_v", "a_v", "c", "exp_avg_sq", "eps", "gscale")
 
-    def __init__(self, pid, kind, g_t, a_t, g_v, a_v, c, exp_avg_sq, eps):
+    def __init__(self, pid, kind, g_t, a_t, g_v, a_v, c, exp_avg_sq, eps, gscale=1.0):
         self.pid, self.kind, self.g_t, self.a_t, self.g_v, self.a_v = pid, kind, g_t, a_t, g_v, a_v
-        self.c, self.exp_avg_sq, self.eps = c, exp_avg_sq, eps
+        self.c, self.exp_avg_sq, self.eps, self.gscale = c, exp_avg_sq, eps, gscale
 
 
 class _PrecondTables:
@@ -487,7 +508,7 @@ class _PrecondTables:
         c = float(np.float32(scale * np.float32(layer_scale)))  # float32 C * ls, as the tensor product
         if v_sq is not None:
             v_sq = v_sq.detach().to(device=device, dtype=torch.float32)
-        return LayerPlan(pid, eff, g_t, pr.a_t, pr.g_v, pr.a_v, c, v_sq, eps)
+        return LayerPlan(pid, eff, g_t, pr.a_t, pr.g_v, pr.a_v, c, v_sq, eps, pr.scale)
 
 
 def plan_layers(pairs, optimizer, preconditioner, device):
@@ -607,7 +628,7 @@ def _score_and_similarity(model, device, batch_train, validation_loader, optimiz
 
 
 def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_layers, preconditioner, score_len,
-                   make_handler, precond: dict | None = None):
+                   make_handler, precond: dict | None = None, fold_scale: bool = False):
     """Capture forward, then one backward whose per-layer hooks hand each (dL/dZ, A) pair to a handler.
 
     The backward pass is asked only for the gradient of the first kept
@@ -620,7 +641,9 @@ def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_l
     loss does not reach, or no usable root): the caller then falls back to the
     batch capture.  precond: a dict that keeps the preconditioner state
     (Muon S matrices, AdamW scalars) across the passes of one round; it is
-    filled by the first pass that gets it.
+    filled by the first pass that gets it.  fold_scale: plans of this
+    package's GCLinear layers carry dL/dZ unscaled and its per-sample factor
+    as gscale (the handler must apply it).
     """
     loss, layers_kept, z_list, train_bs, val_bs = _capture_forward(
         model, dict(batch_train), None, trainable_layers, score_len, batch_val)
@@ -645,7 +668,7 @@ def stream_capture(model, device, batch_train, batch_val, optimizer, trainable_l
     def make_hook(li):
         def hook(grad):
             try:
-                pairs = _layer_pairs(layers_kept[li], grad, train_bs)
+                pairs = _layer_pairs(layers_kept[li], grad, train_bs, fold_scale)
                 if len(pairs) != _pairs_per_layer(layers_kept[li]):
                     bad.append(li)
                     return None
@@ -761,6 +784,31 @@ def _has_muon(optimizer, preconditioner) -> bool:
     return any(_group_kind(g) == "muon" for opt in _as_opt_list(optimizer) for g in opt.param_groups)
 
 
+def _adamw_table_bytes(trainable_layers, optimizer, preconditioner) -> int:
+    """Device bytes of the AdamW epilogue tables a round in passes keeps (one per AdamW pair).
+
+    The table holds 16 bytes per element pair of every 128 x 256 tile of the
+    layer (ops.sketch_table_entries); the other preconditioners use the
+    projector's cached sign tables.
+    """
+    if preconditioner not in ("adamw", "auto"):
+        return 0
+    p2o = _build_param2opt_map(_as_opt_list(optimizer))
+    total = 0
+    for layer in trainable_layers:
+        names = ("lora_A", "lora_B") if _pairs_per_layer(layer) == 2 else ("weight",)
+        for name in names:
+            p = getattr(layer, name, None)
+            if not isinstance(p, torch.Tensor) or p.dim() != 2:
+                continue
+            opt = p2o.get(p)
+            if opt is None or (preconditioner == "auto" and _group_kind(_find_group_for_param(opt, p)) != "adamw"):
+                continue
+            tiles = -(-p.shape[0] // 128) * -(-p.shape[1] // 256)
+            total += tiles * 128 * 256 * 8
+    return total
+
+
 def _use_passes(rows: int, trainable_layers, seq_len: int, device, model=None, muon: bool = True) -> bool:
     projector = get_projector()
     if projector is None or not projector.enabled:
@@ -799,10 +847,13 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
     n = batch_val["input_ids"].shape[0] if batch_val is not None else 0
     n_total = n if n_proxy_total is None else int(n_proxy_total)
     seq = min(batch_train["input_ids"].shape[1], score_len or 1 << 30)
-    reserve = 4 * k * (B + n) * _pairs(trainable_layers)
+    # kept across the passes: the candidate sketches, and each AdamW layer's epilogue table
+    # (the optimizer state does not move within a round, so one build serves every pass)
+    reserve = 4 * k * (B + n) * _pairs(trainable_layers) + _adamw_table_bytes(trainable_layers, optimizer,
+                                                                            preconditioner)
     step = rows_per_pass(trainable_layers, seq, device, reserve, model, _has_muon(optimizer, preconditioner))
     precond: dict = {}
-    st: dict = {}
+    st: dict = {"tables": {}}
 
     def rows_of(batch, lo, hi):
         return {key: v[lo:hi] for key, v in batch.items()}
@@ -825,14 +876,14 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
             def on_plan(pl):
                 g_v, a_v = (pl.g_v.unsqueeze(1), pl.a_v.unsqueeze(1)) if pl.g_v.dim() == 2 else (pl.g_v, pl.a_v)
                 if per_val:
-                    projector.sketch(g_v, a_v, pl.pid, out=st["taus"][pl.pid, lo:hi])
+                    projector.sketch(g_v, a_v, pl.pid, out=st["taus"][pl.pid, lo:hi], alpha=pl.gscale)
                 else:
                     projector.sketch(g_v, a_v, pl.pid, rows_div=g_v.shape[0], out=st["taus"][pl.pid:pl.pid + 1],
-                                     accumulate=True)
+                                     accumulate=True, alpha=pl.gscale)
             return on_plan
 
         if not stream_capture(model, device, empty_train, rows_of(batch_val, lo, hi), optimizer, trainable_layers,
-                              preconditioner, score_len, proxy_handler, precond):
+                              preconditioner, score_len, proxy_handler, precond, fold_scale=True):
             raise RuntimeError("capture in passes: a capture layer's backward hook did not fire")
     if reduce_targets is not None:
         if "taus" not in st:  # this rank holds no proxy rows: learn the layer count from the first candidate pass
@@ -855,7 +906,8 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
                 g_t, a_t = (pl.g_t.unsqueeze(1), pl.a_t.unsqueeze(1)) if pl.g_t.dim() == 2 else (pl.g_t, pl.a_t)
                 st["cs"][pl.pid] = pl.c
                 out = st["phis"][pl.pid, lo:hi] if keep_sketches else None
-                phi = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps, out=out)
+                phi = projector.sketch(g_t, a_t, pl.pid, exp_avg_sq=pl.exp_avg_sq, eps=pl.eps, out=out,
+                                       table_cache=st["tables"], alpha=pl.gscale)
                 if per_val:
                     ops.sketch_gram(phi, st["taus"][pl.pid], alpha=pl.c, out=score[lo:hi], accumulate=True)
                 elif n_total > 0:
@@ -864,7 +916,7 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
             return on_plan
 
         if not stream_capture(model, device, rows_of(batch_train, lo, hi), empty_val, optimizer, trainable_layers,
-                              preconditioner, score_len, cand_handler, precond):
+                              preconditioner, score_len, cand_handler, precond, fold_scale=True):
             raise RuntimeError("capture in passes: a capture layer's backward hook did not fire")
     return score, st.get("phis"), st.get("cs", []), st.get("taus")
 

@@ -148,14 +148,27 @@ class GradientProjector:
 
     def sketch(self, dLdZ: torch.Tensor, a: torch.Tensor, param_id: int, diag: torch.Tensor | None = None,
                exp_avg_sq: torch.Tensor | None = None, eps: float = 1e-8, rows_div: int = 1,
-               out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
-        """Per-sample sketches of [B, T, *] factors (rows_div > 1 sums groups of samples)."""
+               out: torch.Tensor | None = None, accumulate: bool = False,
+               table_cache: dict | None = None, alpha: float = 1.0) -> torch.Tensor:
+        """Per-sample sketches of [B, T, *] factors (rows_div > 1 sums groups of samples).
+
+        table_cache: a dict that keeps the preconditioned tables of this call's
+        parameter for later calls with the same diagonal (the passes of one
+        round); the caller owns it and drops it when the optimizer state moves.
+        alpha: f32 factor on the sketch (dL/dZ's per-sample scaling).
+        """
         B, T, d_out = dLdZ.shape
         d_in = a.shape[2]
         if diag is not None:
             diag = diag.to(device=dLdZ.device, dtype=torch.float32)
-        table, do_p, di_p = self.layer_table(d_out, d_in, param_id, dLdZ.device, diag=diag, exp_avg_sq=exp_avg_sq,
-                                             eps=eps)
+        cached = None if table_cache is None else table_cache.get(param_id)
+        if cached is not None:
+            table, do_p, di_p = cached
+        else:
+            table, do_p, di_p = self.layer_table(d_out, d_in, param_id, dLdZ.device, diag=diag,
+                                                 exp_avg_sq=exp_avg_sq, eps=eps)
+            if table_cache is not None and (diag is not None or exp_avg_sq is not None):
+                table_cache[param_id] = (table, do_p, di_p)
         if do_p != d_out:
             dLdZ = torch.nn.functional.pad(dLdZ, (0, do_p - d_out))
         if di_p != d_in:
@@ -163,7 +176,7 @@ class GradientProjector:
         # padded elements (bucket 0, weight 0) add exact zeros: they do not count toward the load
         load = self.max_bucket_load(d_out * d_in, param_id, dLdZ.device)
         return ops.sketch_gemm(dLdZ, a, table, self.sketch_dim, rows_div=rows_div, out=out, accumulate=accumulate,
-                               max_bucket_load=load)
+                               max_bucket_load=load, alpha=alpha)
 
     def clear_cache(self):
         """Drop every cached table (random_projection.py:195-198)."""

@@ -9,7 +9,7 @@ from opus_b200 import _lib
 
 def test_library_loads_and_reports_version():
     lib = _lib.load()
-    assert lib.opus_abi_version() == 2
+    assert lib.opus_abi_version() == 3
     assert _lib.last_error() == "" or isinstance(_lib.last_error(), str)
 
 
@@ -45,10 +45,10 @@ def test_argument_validation_without_device():
     """Entry points reject bad arguments before touching the device (status codes, message set)."""
     lib = _lib.load()
     rc = lib.opus_sketch_gemm(_null(), _null(), _lib.DTYPE_F32, 1, 1, 8, 8, _null(), 0, 16, 4, 1, _null(), 0,
-                              _null())
+                              1.0, _null())
     assert rc == _lib.OPUS_ERR_UNSUPPORTED and "bf16" in _lib.last_error()
     rc = lib.opus_sketch_gemm(_null(), _null(), _lib.DTYPE_BF16, -1, 1, 8, 8, _null(), 0, 16, 4, 1, _null(), 0,
-                              _null())
+                              1.0, _null())
     assert rc == _lib.OPUS_ERR_INVALID
     with pytest.raises(ValueError):
         _lib.check(rc, "opus_sketch_gemm")

@@ -559,3 +559,25 @@ def test_sketch_gemm_tile_walks_match_oracle(order, jobs, d_out, d_in, monkeypat
     rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, walk {order}/{jobs}")
     want_dense = orc.per_sample_grads(gn, an) * diag.cpu().numpy()[None]
     rel_close(dense.cpu().numpy().reshape(want_dense.shape), want_dense, 1e-5, f"dense, walk {order}/{jobs}")
+
+
+@pytest.mark.parametrize("pair", ["0", "1"])
+@pytest.mark.parametrize("k", [8192, 65536])
+def test_sketch_gemm_alpha_scales_every_update(pair, k, monkeypatch):
+    """alpha (the per-sample factor of dL/dZ) multiplies the sketch, to the fixed-point quantum (the scale of
+    each job's shared sketch follows the scaled values, so its grid moves with alpha) and the rounding of the
+    f32 sums (the L2 reductions and the per-job flushes add in no fixed order)."""
+    monkeypatch.setenv("OPUS_SKETCH_PAIR", pair)
+    B, T, d_out, d_in = 4, 80, 384, 512
+    torch.manual_seed(k)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 8, k)
+    table = ops.build_sketch_table(packed, d_out, d_in, exp_avg_sq=torch.full((d_out, d_in), 1e-4, device=DEV))
+    load = ops.bucket_max_load(packed, k)
+    one = ops.sketch_gemm(g, a, table, k, max_bucket_load=load)
+    four = ops.sketch_gemm(g, a, table, k, max_bucket_load=load, alpha=4.0)
+    tw = ops.sketch_gemm(g, a, table, k, max_bucket_load=load, alpha=24.0)
+    ops.check_device_error("sketch_gemm alpha")
+    rel_close(four.cpu().numpy(), 4 * one.cpu().numpy(), 1e-5, "alpha 4")
+    rel_close(tw.cpu().numpy(), 24 * one.cpu().numpy(), 1e-5, "alpha 24")

@@ -363,3 +363,31 @@ def test_score_shard_in_passes_matches_single_pass(monkeypatch):
     assert_close_scores(split[0].cpu().numpy(), one[0].cpu().numpy(), rtol=1e-4)
     assert_close_scores(split[1].cpu().numpy(), one[1].cpu().numpy(), rtol=1e-4)
     assert_close_scores(split[0].cpu().numpy(), g["scores"])
+
+
+@pytest.mark.parametrize("name", ["adamw_proj", "muon_proj"])
+def test_folded_row_scale_equals_scaled_dldz(name, monkeypatch):
+    """A round in passes with dL/dZ's per-sample factor applied by the sketch kernel (the default)
+    gives the values of the same round with the layer's own dL/dZ * N tensors."""
+    g = load_golden(f"wholepath_{name}")
+    model, opt, loader, batch = rebuild(g, device=DEV)
+    ds.initialize_projector(sketch_dim=1024, seed=42, device="cpu", enabled=True)
+    monkeypatch.setattr(ds, "CAPTURE_ROWS", 2)
+    layers = ds.find_GClayers(model)
+    args = (model, torch.device(DEV), batch, loader, opt, layers)
+    kw = dict(preconditioner=str(g["precond"]), score_len=128)
+    calls = []
+    real = ds._layer_pairs
+
+    def spy(layer, zg, train_bs, fold_scale=False):
+        out = real(layer, zg, train_bs, fold_scale)
+        calls.append(out[0].scale)
+        return out
+
+    monkeypatch.setattr(ds, "_layer_pairs", spy)
+    folded = ds.compute_GradProd_GC_per_iter(*args, **kw)
+    assert calls and all(s == 2.0 for s in calls)  # every GCLinear pair left its factor to the kernel
+    monkeypatch.setattr(ds, "_layer_pairs", lambda layer, zg, train_bs, fold_scale=False: real(layer, zg, train_bs))
+    scaled = ds.compute_GradProd_GC_per_iter(*args, **kw)
+    assert_close_scores(folded[0], scaled[0])
+    assert_close_scores(folded[1], scaled[1])

@@ -360,6 +360,22 @@ def test_capture_pass_planning(monkeypatch):
     assert not ds._has_muon([adam, muon], "sgd")
 
 
+def test_adamw_table_reserve_counts_adamw_pairs_only():
+    """The bytes a round in passes keeps for AdamW epilogue tables: 8 per element of every 128 x 256 tile."""
+    model = TinyLM(GCLinear)
+    layers = ds.find_GClayers(model)
+    params = [layer.weight for layer in layers]
+    want = sum(-(-p.shape[0] // 128) * -(-p.shape[1] // 256) * 128 * 256 * 8 for p in params)
+    adam = torch.optim.AdamW(model.parameters())
+    assert ds._adamw_table_bytes(layers, adam, "adamw") == want
+    assert ds._adamw_table_bytes(layers, adam, "auto") == want
+    assert ds._adamw_table_bytes(layers, adam, "sgd") == 0 and ds._adamw_table_bytes(layers, adam, "muon") == 0
+    muon = MuonLike(params[:1])
+    rest = torch.optim.AdamW([p for p in model.parameters() if p is not params[0]])
+    first = -(-params[0].shape[0] // 128) * -(-params[0].shape[1] // 256) * 128 * 256 * 8
+    assert ds._adamw_table_bytes(layers, [rest, muon], "auto") == want - first
+
+
 @pytest.mark.parametrize("rows,step", [(128, 29), (16, 29), (0, 8), (7, 1), (144, 24), (5, 100)])
 def test_pass_ranges_cover_rows_in_balanced_passes(rows, step):
     """As few passes as the step allows, contiguous, covering every row once, sizes within one."""
