@@ -702,10 +702,12 @@ struct JobPlan {
 //    launch with few rows (a pass of the whole path, proxies merged into long
 //    rows) still fills every SM;
 //  - d_in > d_out with up to 64 rows (the passes of the whole path): column
-//    block major, jobs cut at whole columns.  Each job then loads each of its
-//    wide activation tiles once and re-reads only the narrow dLdZ tiles, which
-//    every candidate in flight keeps in L2 (6400 -> 1600 at 24 rows: 418
-//    against 348 TFLOP/s).
+//    block major, jobs cut at whole columns while the rows have enough columns
+//    to fill every worker (tiles otherwise: one merged proxy row of 4096 ->
+//    1024 has 16 columns, 93 against 492 TFLOP/s).  Each job then loads each
+//    of its wide activation tiles once and re-reads only the narrow dLdZ
+//    tiles, which every candidate in flight keeps in L2 (6400 -> 1600 at 24
+//    rows: 418 against 348 TFLOP/s).
 // Each candidate's walk is split into `groups` jobs so that the rounds of jobs
 // over the SMs waste the least time: minimise ceil(jobs / SMs) x (tiles per
 // job + 1), the 1 standing for a job's fixed cost (its sketch flush and the
@@ -720,7 +722,7 @@ JobPlan plan_jobs(int n_rows, int d_out, int d_in, int n_ob, int workers) {
     if (strcmp(env, "cb") == 0) cb_major = 1;
     if (strcmp(env, "ob") == 0) cb_major = 0;
   }
-  bool lines = cb_major != 0;
+  bool lines = cb_major != 0 && (int64_t)n_rows * n_cb >= sms;
   if (const char* env = getenv("OPUS_SKETCH_JOBS")) {
     if (strcmp(env, "lines") == 0) lines = true;
     if (strcmp(env, "tiles") == 0) lines = false;
