@@ -7,14 +7,14 @@
 // w(o,c) = s(o,c) * D(o,c) from the precomputed table and adds it into bucket
 // h(o,c) of candidate b's sketch.  G_b is never written to HBM.
 //
-// Warp roles (320 threads, persistent, one CTA per SM; in a pair the MMA warp
-// of the second CTA stays idle):
+// Warp roles (448 threads, or 320 with 8 epilogue warps; persistent, one CTA
+// per SM; in a pair the MMA warp of the second CTA stays idle):
 //   warp 0      TMA producer: 3-D tile loads of dLdZ and a into a ring of
 //               shared-memory stages (128-byte swizzle, MN-major operands);
 //   warp 1      TMEM allocation + single-thread UMMA issue into one of two
 //               256-column accumulators (double-buffered against the epilogue);
-//   warps 2..9  epilogue: two warps per TMEM lane quarter, each taking half
-//               of the tile's 32-column chunks.
+//   warps 2..   epilogue: 8 or 12 warps, two or three per TMEM lane quarter,
+//               dealt the tile's 32- or 16-column chunks round-robin.
 //
 // Shared-memory sketch in 32-bit fixed point.  Float atomics on shared memory
 // are compare-and-swap loops on this hardware, integer adds are native, so
@@ -53,10 +53,13 @@
 namespace opus {
 namespace {
 
+// Epilogue warps: 8 (the dense epilogue, and the scatter's default) or 12.
+// Block size and the dense epilogue's chunking are those of 8.
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kChunksPerWarp = kChunksPerTile / (kEpiWarps / 4);  // 4
+constexpr int block_threads(int epi) { return 64 + 32 * epi; }
 constexpr int kHeadroomLog2 = 4;                     // first-tile max maps to cap / 16
 constexpr int kBoxMN = 64;                           // bf16 elements per 128-byte swizzle row
 constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
@@ -150,13 +153,13 @@ __device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatil
 
 // Add the fixed-point sketch of buckets [0, k) (scaled by 2^-scale_exp) into
 // dst and clear it.
-__device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int et, uint64_t* bar,
+__device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int et, int n_threads, uint64_t* bar,
                              uint32_t& phase, volatile int* abort_flag, int* err) {
   if (!epi_sync(bar, phase, abort_flag, err)) return false;
   const float inv = ldexpf(1.0f, -scale_exp);
   if ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     int4* s4 = reinterpret_cast<int4*>(sk);
-    for (int64_t i = et; i < k / 4; i += kEpiThreads) {
+    for (int64_t i = et; i < k / 4; i += n_threads) {
       const int4 q = s4[i];
       if (q.x | q.y | q.z | q.w) {
         red_add_v4(dst + 4 * i, (float)q.x * inv, (float)q.y * inv, (float)q.z * inv, (float)q.w * inv);
@@ -164,7 +167,7 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
       }
     }
   } else {
-    for (int64_t i = et; i < k; i += kEpiThreads) {
+    for (int64_t i = et; i < k; i += n_threads) {
       const int q = sk[i];
       if (q != 0) {
         atomicAdd(dst + i, (float)q * inv);
@@ -175,8 +178,8 @@ __device__ bool flush_sketch(int* sk, float* dst, int64_t k, int scale_exp, int 
   return epi_sync(bar, phase, abort_flag, err);
 }
 
-template <int BK, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BK, bool PAIR, int EPI>
+__global__ void __launch_bounds__(block_threads(EPI), 1)
     sketch_gemm_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_out,
                        const uint4* __restrict__ table, float* __restrict__ phi, int n_rows, int seq_len, int n_tiles, int unit, int cb_major,
@@ -228,9 +231,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       // one arrival per epilogue warp (both CTAs' warps on a pair's leader)
-      mbar_init(&tempty[a], PAIR ? 2 * kEpiWarps : kEpiWarps);
+      mbar_init(&tempty[a], PAIR ? 2 * EPI : EPI);
     }
-    mbar_init(epi_bar, kEpiThreads);
+    mbar_init(epi_bar, 32 * EPI);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     *tile_max_bits = 0;
@@ -249,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_relinquish();
     }
   }
-  for (int64_t i = threadIdx.x; i < k_sm; i += kThreads) sk[i] = 0;
+  for (int64_t i = threadIdx.x; i < k_sm; i += block_threads(EPI)) sk[i] = 0;
   tc_fence_before();
   __syncthreads();
   // both CTAs' barriers are initialised before any load, commit or arrival crosses the pair
@@ -372,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(drain_bar);
       mbar_wait(drain_bar, 0, nullptr, err, kDevTimeoutDrain);
     }
-  } else if (!PAIR && dense) {
+  } else if (!PAIR && EPI == kEpiWarps && dense) {
     // ------------------------------------------------- dense epilogue
     // Per-sample gradients: element (o, c) of G_b, times dense_diag[o, c]
     // when given, goes to phi[b, o * d_in + c].  Each warp stages its 32 rows
@@ -483,9 +486,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) bulk_wait_group<0>();  // every store has landed before the CTA exits
   } else {
     // ------------------------------------------------------------ epilogue
-    const int et = threadIdx.x - 64;          // 0..255
+    // EPI / 4 warps per TMEM lane quarter share a tile's chunks round-robin: 32-column chunks
+    // with 8 warps, 16-column chunks with 12 (fewer registers per thread, more warps to hide
+    // the latency of the table loads and of the updates).
+    constexpr int kGroups = EPI / 4;
+    constexpr int kCols = EPI == 8 ? 32 : 16;
+    constexpr int kChunks = kTileN / kCols;
+    constexpr int kPairs = kCols / 2;
+    const int et = threadIdx.x - 64;          // 0 .. 32 * EPI - 1
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;         // which 4 of the 8 column chunks
+    const int grp = (warp - 2) >> 2;          // chunks grp, grp + kGroups, ...
+    const int last_j = grp + ((kChunks - 1 - grp) / kGroups) * kGroups;  // this warp's last chunk
     const int r = q * 32 + lane;              // tile row owned by this thread
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t kk32 = static_cast<uint32_t>(k);
@@ -517,8 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = static_cast<int>(job / groups);
       float* out_row = phi + (int64_t)(b / rows_div) * k;
       if (smem_sketch && job != cur_job) {
-        if (cur_job >= 0 && !flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, epi_bar,
-                                          epi_phase, abort_flag, err)) {
+        if (cur_job >= 0 && !flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, 32 * EPI,
+                                          epi_bar, epi_phase, abort_flag, err)) {
           ok = false;
           break;
         }
@@ -543,19 +554,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint4* tp = table + ((int64_t)ob * n_cb + walk.cb(tile)) * kEntriesPerTile + r;
       const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
+      // chunk j: its table entries (column pairs j * kPairs ..) in flight, then its accumulator columns
+      auto load_chunk = [&](int j, uint4(&ent)[kPairs], uint32_t(&v)[kCols]) {
+#pragma unroll
+        for (int p = 0; p < kPairs; ++p) ent[p] = ld_table(tp + (j * kPairs + p) * kTileM, table_policy);
+        if constexpr (kCols == 32)
+          tmem_ld32(tmem_base + lane_addr + col0 + j * kCols, v);
+        else
+          tmem_ld16(tmem_base + lane_addr + col0 + j * kCols, v);
+        tmem_ld_wait();
+      };
       if (smem_sketch && !scaled) {
         // First tile of this candidate in this CTA: scale from max |w G| over the tile.
         float m = 0.0f;
-        for (int jj = 0; jj < kChunksPerWarp; ++jj) {
-          const int j = half * kChunksPerWarp + jj;
-          uint4 ent[kPairsPerChunk];
+        for (int j = grp; j < kChunks; j += kGroups) {
+          uint4 ent[kPairs];
+          uint32_t v[kCols];
+          load_chunk(j, ent, v);
 #pragma unroll
-          for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_table(tp + (j * kPairsPerChunk + p) * kTileM, table_policy);
-          uint32_t v[32];
-          tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int p = 0; p < kPairsPerChunk; ++p) {
+          for (int p = 0; p < kPairs; ++p) {
             const uint4 e = ent[p];
             const float x0 = fabsf(__uint_as_float(v[2 * p]) * __uint_as_float(e.z) * alpha);
             const float x1 = fabsf(__uint_as_float(v[2 * p + 1]) * __uint_as_float(e.w) * alpha);
@@ -588,18 +605,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float S = ldexpf(1.0f, scale_exp);
       const bool use_int = smem_sketch && scaled;
 #pragma unroll 1
-      for (int jj = 0; jj < kChunksPerWarp; ++jj) {
-        const int j = half * kChunksPerWarp + jj;
-        // all 16 table entries of the chunk in flight before the accumulator wait
-        uint4 ent[kPairsPerChunk];
+      for (int j = grp; j < kChunks; j += kGroups) {
+        uint4 ent[kPairs];
+        uint32_t v[kCols];
+        load_chunk(j, ent, v);
+        if (j == last_j) release(acc);  // the warp's accumulator reads are done
 #pragma unroll
-        for (int p = 0; p < kPairsPerChunk; ++p) ent[p] = ld_table(tp + (j * kPairsPerChunk + p) * kTileM, table_policy);
-        uint32_t v[32];
-        tmem_ld32(tmem_base + lane_addr + col0 + j * kChunkCols, v);
-        tmem_ld_wait();
-        if (jj == kChunksPerWarp - 1) release(acc);  // the warp's accumulator reads are done
-#pragma unroll
-        for (int p = 0; p < kPairsPerChunk; ++p) {
+        for (int p = 0; p < kPairs; ++p) {
           const uint4 e = ent[p];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -624,8 +636,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (ok && smem_sketch && cur_job >= 0)
-      flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, epi_bar, epi_phase, abort_flag,
-                   err);
+      flush_sketch(sk, phi + (cur_job / groups / rows_div) * k, k_sm, scale_exp, et, 32 * EPI, epi_bar, epi_phase,
+                   abort_flag, err);
     if (bad) record_device_error(err, kDevBadBucket);
   }
 
@@ -748,6 +760,17 @@ JobPlan plan_jobs(int n_rows, int d_out, int d_in, int n_ob, int workers) {
 
 using namespace opus;
 
+// Epilogue warps of the scatter launches.  The epilogue is latency-bound (table
+// loads and update issue), and 12 warps with 16-column chunks hide more of it
+// than 8 with 32-column chunks: interleaved launches at 24 and 128 rows gave
+// +7-10% on the GPT-2-XL shapes at k = 65536 (1600 -> 6400: 496 against 459
+// TFLOP/s) and +8% at 768 -> 3072, k = 16384; a pair with 32-token stages
+// (k > 65536) lost 2-5%, so it keeps 8.  OPUS_SKETCH_EPI_WARPS (8 or 12) forces one.
+int epilogue_warps(bool pair_short_stages) {
+  if (const char* env = getenv("OPUS_SKETCH_EPI_WARPS")) return atoi(env) == 12 ? 12 : 8;
+  return pair_short_stages ? 8 : 12;
+}
+
 // Shared memory of one CTA of a pair: stages of `stage` bytes (32 KB at 64
 // tokens, 16 KB at 32).  The whole sketch with as many stages (3 to 6) as fit;
 // otherwise `pref_stages` stages and the largest prefix of the buckets next to them.
@@ -789,7 +812,9 @@ int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, 
   if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small for CTA pairs");
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  auto kernel = bk == 32 ? sketch_gemm_kernel<32, true> : sketch_gemm_kernel<64, true>;
+  const int epi = epilogue_warps(bk == 32);
+  auto kernel = bk == 32 ? (epi == 12 ? sketch_gemm_kernel<32, true, 12> : sketch_gemm_kernel<32, true, 8>)
+                         : (epi == 12 ? sketch_gemm_kernel<64, true, 12> : sketch_gemm_kernel<64, true, 8>);
   OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   cudaLaunchAttribute attr[1];
@@ -799,7 +824,7 @@ int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, 
   attr[0].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(block_threads(epi), 1, 1);
   cfg.dynamicSmemBytes = plan.bytes;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -909,13 +934,15 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   }
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  auto kernel = bk == 32 ? sketch_gemm_kernel<32, false> : sketch_gemm_kernel<64, false>;
+  const int epi = epilogue_warps(false);
+  auto kernel = bk == 32 ? (epi == 12 ? sketch_gemm_kernel<32, false, 12> : sketch_gemm_kernel<32, false, 8>)
+                         : (epi == 12 ? sketch_gemm_kernel<64, false, 12> : sketch_gemm_kernel<64, false, 8>);
   OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
   const JobPlan jp = plan_jobs(n_rows, d_out, d_in, ceil_div(d_out, kTileM), sm_count());
   int* err = device_error_word();
-  kernel<<<jp.grid, kThreads, plan.bytes, st>>>(
+  kernel<<<jp.grid, block_threads(epi), plan.bytes, st>>>(
       tm_g, tm_a, tm_g /*no dense output*/, reinterpret_cast<const uint4*>(table), phi, n_rows, seq_len, n_tiles,
       jp.unit, jp.cb_major, n_cb, jp.groups, k, rows_div, plan.stages, plan.k_sm, cap, cap_log2, err, /*dense*/ 0,
       nullptr, d_out, d_in, accumulate, alpha);
@@ -961,12 +988,12 @@ extern "C" int opus_per_sample_grad(const void* dLdZ, const void* a, int dtype, 
   const SmemPlan plan = plan_smem(kStagingWords);
   if (plan.stages == 0 || plan.k_sm < kStagingWords)
     return set_error(OPUS_ERR_UNSUPPORTED, "per_sample_grad: shared memory too small");
-  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  OPUS_CUDA_TRY(cudaFuncSetAttribute(sketch_gemm_kernel<64, false, kEpiWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;
   const JobPlan jp = plan_jobs(n_rows, d_out, d_in, ceil_div(d_out, kTileM), sm_count());
   int* err = device_error_word();
-  sketch_gemm_kernel<64, false><<<jp.grid, kThreads, plan.bytes, st>>>(
+  sketch_gemm_kernel<64, false, kEpiWarps><<<jp.grid, kThreads, plan.bytes, st>>>(
       tm_g, tm_a, tm_out, nullptr, out, n_rows, seq_len, n_tiles, jp.unit, jp.cb_major, n_cb, jp.groups, numel, 1,
       plan.stages, plan.k_sm, 0.0f, 0, err, /*dense*/ 1, diag, d_out, d_in, accumulate, 1.0f);
   ::opus::note_launch();
