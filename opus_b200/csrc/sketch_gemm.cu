@@ -7,14 +7,14 @@
 // w(o,c) = s(o,c) * D(o,c) from the precomputed table and adds it into bucket
 // h(o,c) of candidate b's sketch.  G_b is never written to HBM.
 //
-// Warp roles (448 threads, or 320 with 8 epilogue warps; persistent, one CTA
-// per SM; in a pair the MMA warp of the second CTA stays idle):
+// Warp roles (64 + 32 x 8, 12 or 16 epilogue warps threads; persistent, one
+// CTA per SM; in a pair the MMA warp of the second CTA stays idle):
 //   warp 0      TMA producer: 3-D tile loads of dLdZ and a into a ring of
 //               shared-memory stages (128-byte swizzle, MN-major operands);
 //   warp 1      TMEM allocation + single-thread UMMA issue into one of two
 //               256-column accumulators (double-buffered against the epilogue);
-//   warps 2..   epilogue: 8 or 12 warps, two or three per TMEM lane quarter,
-//               dealt the tile's 32- or 16-column chunks round-robin.
+//   warps 2..   epilogue: 8, 12 or 16 warps, two to four per TMEM lane
+//               quarter, dealt the tile's 32-, 16- or 8-column chunks round-robin.
 //
 // Shared-memory sketch in 32-bit fixed point.  Float atomics on shared memory
 // are compare-and-swap loops on this hardware, integer adds are native, so
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
     // with 8 warps, 16-column chunks with 12 (fewer registers per thread, more warps to hide
     // the latency of the table loads and of the updates).
     constexpr int kGroups = EPI / 4;
-    constexpr int kCols = EPI == 8 ? 32 : 16;
+    constexpr int kCols = EPI == 8 ? 32 : (EPI == 12 ? 16 : 8);
     constexpr int kChunks = kTileN / kCols;
     constexpr int kPairs = kCols / 2;
     const int et = threadIdx.x - 64;          // 0 .. 32 * EPI - 1
@@ -560,8 +560,10 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
         for (int p = 0; p < kPairs; ++p) ent[p] = ld_table(tp + (j * kPairs + p) * kTileM, table_policy);
         if constexpr (kCols == 32)
           tmem_ld32(tmem_base + lane_addr + col0 + j * kCols, v);
-        else
+        else if constexpr (kCols == 16)
           tmem_ld16(tmem_base + lane_addr + col0 + j * kCols, v);
+        else
+          tmem_ld8(tmem_base + lane_addr + col0 + j * kCols, v);
         tmem_ld_wait();
       };
       if (smem_sketch && !scaled) {
@@ -761,14 +763,21 @@ JobPlan plan_jobs(int n_rows, int d_out, int d_in, int n_ob, int workers) {
 using namespace opus;
 
 // Epilogue warps of the scatter launches.  The epilogue is latency-bound (table
-// loads and update issue), and 12 warps with 16-column chunks hide more of it
-// than 8 with 32-column chunks: interleaved launches at 24 and 128 rows gave
-// +7-10% on the GPT-2-XL shapes at k = 65536 (1600 -> 6400: 496 against 459
-// TFLOP/s) and +8% at 768 -> 3072, k = 16384; a pair with 32-token stages
-// (k > 65536) lost 2-5%, so it keeps 8.  OPUS_SKETCH_EPI_WARPS (8 or 12) forces one.
-int epilogue_warps(bool pair_short_stages) {
-  if (const char* env = getenv("OPUS_SKETCH_EPI_WARPS")) return atoi(env) == 12 ? 12 : 8;
-  return pair_short_stages ? 8 : 12;
+// loads and update issue), and more warps on narrower chunks hide more of it
+// (interleaved launches at 24 and 128 rows, TFLOP/s for 8 / 12 / 16 warps):
+//   pairs on 64-token stages, k = 65536: 1600 -> 6400 at 24 rows 459 / 495 / 521,
+//     6400 -> 1600 432 / 473 / 511: 16 warps (8-column chunks);
+//   one CTA: 768 -> 3072 at k = 16384, 128 rows 772 / 849 / 861, 1024 -> 4096 at
+//     k = 32768 752 / 749 / 719: 12 warps (16-column chunks);
+//   pairs on 32-token stages (k > 65536): 2048 -> 6144 at 24 rows 450 / 438 / 429: 8.
+// OPUS_SKETCH_EPI_WARPS (8, 12 or 16) forces one.
+int epilogue_warps(bool pair, bool short_stages) {
+  if (const char* env = getenv("OPUS_SKETCH_EPI_WARPS")) {
+    const int w = atoi(env);
+    return w == 12 || w == 16 ? w : 8;
+  }
+  if (!pair) return 12;
+  return short_stages ? 8 : 16;
 }
 
 // Shared memory of one CTA of a pair: stages of `stage` bytes (32 KB at 64
@@ -812,9 +821,11 @@ int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, 
   if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small for CTA pairs");
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  const int epi = epilogue_warps(bk == 32);
-  auto kernel = bk == 32 ? (epi == 12 ? sketch_gemm_kernel<32, true, 12> : sketch_gemm_kernel<32, true, 8>)
-                         : (epi == 12 ? sketch_gemm_kernel<64, true, 12> : sketch_gemm_kernel<64, true, 8>);
+  const int epi = epilogue_warps(true, bk == 32);
+  auto kernel = bk == 32 ? (epi == 16 ? sketch_gemm_kernel<32, true, 16>
+                             : epi == 12 ? sketch_gemm_kernel<32, true, 12> : sketch_gemm_kernel<32, true, 8>)
+                         : (epi == 16 ? sketch_gemm_kernel<64, true, 16>
+                             : epi == 12 ? sketch_gemm_kernel<64, true, 12> : sketch_gemm_kernel<64, true, 8>);
   OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   cudaLaunchAttribute attr[1];
@@ -934,9 +945,11 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   }
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  const int epi = epilogue_warps(false);
-  auto kernel = bk == 32 ? (epi == 12 ? sketch_gemm_kernel<32, false, 12> : sketch_gemm_kernel<32, false, 8>)
-                         : (epi == 12 ? sketch_gemm_kernel<64, false, 12> : sketch_gemm_kernel<64, false, 8>);
+  const int epi = epilogue_warps(false, false);
+  auto kernel = bk == 32 ? (epi == 16 ? sketch_gemm_kernel<32, false, 16>
+                             : epi == 12 ? sketch_gemm_kernel<32, false, 12> : sketch_gemm_kernel<32, false, 8>)
+                         : (epi == 16 ? sketch_gemm_kernel<64, false, 16>
+                             : epi == 12 ? sketch_gemm_kernel<64, false, 12> : sketch_gemm_kernel<64, false, 8>);
   OPUS_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(plan.bytes)));
   const int n_cb = ceil_div(d_in, kTileN), n_tiles = ceil_div(d_out, kTileM) * n_cb;

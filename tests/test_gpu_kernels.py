@@ -583,12 +583,14 @@ def test_sketch_gemm_alpha_scales_every_update(pair, k, monkeypatch):
     rel_close(tw.cpu().numpy(), 24 * one.cpu().numpy(), 1e-5, "alpha 24")
 
 
+@pytest.mark.parametrize("epi", ["8", "12", "16"])
 @pytest.mark.parametrize("pair", ["0", "1"])
 @pytest.mark.parametrize("B,T,d_out,d_in,k", [(3, 100, 384, 512, 8192), (2, 130, 520, 264, 1000),
                                               (4, 64, 256, 1024, 65536), (2, 70, 640, 384, 131072)])
-def test_sketch_gemm_twelve_epilogue_warps_match_oracle(B, T, d_out, d_in, k, pair, monkeypatch):
-    """The scatter with 12 epilogue warps (16-column chunks dealt round-robin), one CTA and pairs."""
-    monkeypatch.setenv("OPUS_SKETCH_EPI_WARPS", "12")
+def test_sketch_gemm_epilogue_widths_match_oracle(B, T, d_out, d_in, k, pair, epi, monkeypatch):
+    """The scatter with 8, 12 or 16 epilogue warps (32-, 16- or 8-column chunks dealt round-robin),
+    one CTA and pairs."""
+    monkeypatch.setenv("OPUS_SKETCH_EPI_WARPS", epi)
     monkeypatch.setenv("OPUS_SKETCH_PAIR", pair)
     torch.manual_seed(B * 31 + d_out)
     g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
@@ -597,7 +599,7 @@ def test_sketch_gemm_twelve_epilogue_warps_match_oracle(B, T, d_out, d_in, k, pa
     diag = torch.rand(d_out, d_in, device=DEV) * 1e-3 + 1e-6
     table = ops.build_sketch_table(packed, d_out, d_in, diag=diag)
     phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=ops.bucket_max_load(packed, k))
-    ops.check_device_error("sketch_gemm, 12 epilogue warps")
+    ops.check_device_error(f"sketch_gemm, {epi} epilogue warps")
     want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k,
                                      diag=diag.cpu().numpy())
-    rel_close(phi.cpu().numpy(), want, 1e-4, "phi, 12 epilogue warps")
+    rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, {epi} epilogue warps")
