@@ -60,6 +60,7 @@ constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kChunksPerWarp = kChunksPerTile / (kEpiWarps / 4);  // 4
 constexpr int block_threads(int epi) { return 64 + 32 * epi; }
+
 constexpr int kHeadroomLog2 = 4;                     // first-tile max maps to cap / 16
 constexpr int kBoxMN = 64;                           // bf16 elements per 128-byte swizzle row
 constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
@@ -230,8 +231,9 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      // one arrival per epilogue warp (both CTAs' warps on a pair's leader)
-      mbar_init(&tempty[a], PAIR ? 2 * EPI : EPI);
+      // one arrival per epilogue warp of this CTA; a pair's leader also counts the one
+      // arrival that relays the second CTA's release
+      mbar_init(&tempty[a], PAIR && rank == 0 ? EPI + 1 : EPI);
     }
     mbar_init(epi_bar, 32 * EPI);
     mbar_init(drain_bar, 1);
@@ -374,6 +376,28 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
       else
         umma_commit(drain_bar);
       mbar_wait(drain_bar, 0, nullptr, err, kDevTimeoutDrain);
+    } else if (PAIR && lane == 0) {
+      // The second CTA's epilogue warps release an accumulator on this CTA's own barrier
+      // (CTA-scope arrivals); this thread, which has no memory operations of its own in
+      // flight, forwards each completed release to the leader with one cluster-scope arrival.
+      // (Sixteen cluster-scope arrivals, one per epilogue warp, each waited for that warp's
+      // L2 reductions in flight: 552 against 578 TFLOP/s at 1600 -> 6400, 128 rows.)
+      const uint32_t lead = mapa_shared(smem_u32(tempty), 0);
+      int acc = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
+      for (int u = job_tile_begin(job, groups, n_tiles, unit); u < job_tile_end(job, groups, n_tiles, unit) && ok; ++u) {
+        if (!mbar_wait(&tempty[acc], aph, abort_flag, err, kDevTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_cluster(lead + static_cast<uint32_t>(acc) * 8u);
+        if (++acc == 2) {
+          acc = 0;
+          aph ^= 1;
+        }
+      }
     }
   } else if (!PAIR && EPI == kEpiWarps && dense) {
     // ------------------------------------------------- dense epilogue
@@ -510,18 +534,12 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
     bool scaled = false;    // a scale has been chosen for the current candidate
     bool bad = false;
     bool ok = true;
-    // release an accumulator to the MMA issuer (a pair's is the leader's barrier) once the
-    // whole warp is done with it: one arrival per warp
-    const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
+    // release an accumulator to the MMA issuer once the whole warp is done with it: one
+    // arrival per warp on this CTA's barrier (a pair's second CTA: relayed by its MMA warp)
     auto release = [&](int a) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        if constexpr (PAIR)
-          mbar_arrive_cluster(tempty_lead + static_cast<uint32_t>(a) * 8u);
-        else
-          mbar_arrive(&tempty[a]);
-      }
+      if (lane == 0) mbar_arrive(&tempty[a]);
     };
     for (int64_t job = worker; job < n_jobs && ok; job += n_workers)
     for (int tile = job_tile_begin(job, groups, n_tiles, unit); tile < job_tile_end(job, groups, n_tiles, unit) && ok; ++tile) {
