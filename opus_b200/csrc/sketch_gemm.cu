@@ -874,17 +874,19 @@ int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, 
   return OPUS_OK;
 }
 
-// CTA pairs serve sketches that do not fit one CTA's shared memory next to its
-// stages (k > 32768) with a fixed-point bound, on layers of two o-blocks or
-// more: each CTA then stages half of a tile's activation columns, and the
-// shared memory saved holds more of the sketch (40960 or 45056 buckets against
-// 32768), so fewer updates go to L2.  Below that the one-CTA kernel is faster
-// (768 -> 3072 at k = 16384: 702 against 663 TFLOP/s at 24 rows).
+// CTA pairs, on layers of two o-blocks or more with a fixed-point bound: each
+// CTA stages half of a tile's activation columns (a third less operand traffic
+// per SM), and for sketches larger than one CTA's shared memory (k > 32768) the
+// memory saved holds more of the sketch (40960 or 45056 buckets against
+// 32768), so fewer updates go to L2.  With 16 epilogue warps they also win
+// where the whole sketch fits (k = 32768, 64 rows: 1024 -> 1024 659 against 530
+// TFLOP/s, 1024 -> 4096 850 against 735); at k = 16384 only with many rows
+// (768 -> 3072: 931 against 897 at 256 rows, 739 against 801 at 64).
 // OPUS_SKETCH_PAIR=1 or 0 forces either.
-bool use_pairs(int d_out, int64_t k, int max_bucket_load) {
+bool use_pairs(int d_out, int64_t k, int max_bucket_load, int n_rows) {
   if (ceil_div(d_out, kTileM) < 2) return false;
   if (const char* env = getenv("OPUS_SKETCH_PAIR")) return strcmp(env, "1") == 0;
-  return max_bucket_load > 0 && k > 32768;
+  return max_bucket_load > 0 && (k > 16384 || n_rows >= 256);
 }
 
 extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int n_rows, int seq_len, int d_out,
@@ -946,7 +948,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
       }
     }
   }
-  if (use_pairs(d_out, k, max_bucket_load))
+  if (use_pairs(d_out, k, max_bucket_load, n_rows))
     return launch_pair(dLdZ, a, table, phi, n_rows, seq_len, d_out, d_in, k, max_bucket_load, rows_div, cap,
                        cap_log2, accumulate, alpha, st);
   const int stage_bytes = bk == 32 ? kStageBytes32 : kStageBytes64;
