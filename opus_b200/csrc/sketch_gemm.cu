@@ -785,16 +785,17 @@ using namespace opus;
 // (interleaved launches at 24 and 128 rows, TFLOP/s for 8 / 12 / 16 warps):
 //   pairs on 64-token stages, k = 65536: 1600 -> 6400 at 24 rows 459 / 495 / 521,
 //     6400 -> 1600 432 / 473 / 511: 16 warps (8-column chunks);
-//   one CTA: 768 -> 3072 at k = 16384, 128 rows 772 / 849 / 861, 1024 -> 4096 at
-//     k = 32768 752 / 749 / 719: 12 warps (16-column chunks);
+//   one CTA with the whole sketch next to three stages or more (k <= 16384): 768 -> 3072
+//     at 64 rows 734 / 799 / 815, 768 -> 768 486 / 531 / 545: 16 warps; with two stages
+//     next to the sketch (1024 -> 4096 at k = 32768, 128 rows 752 / 749 / 719): 12;
 //   pairs on 32-token stages (k > 65536): 2048 -> 6144 at 24 rows 450 / 438 / 429: 8.
 // OPUS_SKETCH_EPI_WARPS (8, 12 or 16) forces one.
-int epilogue_warps(bool pair, bool short_stages) {
+int epilogue_warps(bool pair, bool short_stages, bool deep_pipeline) {
   if (const char* env = getenv("OPUS_SKETCH_EPI_WARPS")) {
     const int w = atoi(env);
     return w == 12 || w == 16 ? w : 8;
   }
-  if (!pair) return 12;
+  if (!pair) return deep_pipeline ? 16 : 12;
   return short_stages ? 8 : 16;
 }
 
@@ -839,7 +840,7 @@ int launch_pair(const void* dLdZ, const void* a, const void* table, float* phi, 
   if (plan.stages == 0) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_gemm: shared memory too small for CTA pairs");
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  const int epi = epilogue_warps(true, bk == 32);
+  const int epi = epilogue_warps(true, bk == 32, plan.stages >= 3);
   auto kernel = bk == 32 ? (epi == 16 ? sketch_gemm_kernel<32, true, 16>
                              : epi == 12 ? sketch_gemm_kernel<32, true, 12> : sketch_gemm_kernel<32, true, 8>)
                          : (epi == 16 ? sketch_gemm_kernel<64, true, 16>
@@ -965,7 +966,7 @@ extern "C" int opus_sketch_gemm(const void* dLdZ, const void* a, int dtype, int 
   }
   CUtensorMap tm_g, tm_a;
   if (int rc = encode_operands(dLdZ, a, n_rows, seq_len, d_out, d_in, &tm_g, &tm_a, bk)) return rc;
-  const int epi = epilogue_warps(false, false);
+  const int epi = epilogue_warps(false, false, plan.stages >= 3 && plan.k_sm >= k);
   auto kernel = bk == 32 ? (epi == 16 ? sketch_gemm_kernel<32, false, 16>
                              : epi == 12 ? sketch_gemm_kernel<32, false, 12> : sketch_gemm_kernel<32, false, 8>)
                          : (epi == 16 ? sketch_gemm_kernel<64, false, 16>
