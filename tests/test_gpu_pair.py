@@ -35,6 +35,8 @@ PAIR_SHAPES = [
     (4, 64, 256, 1024, 65536),     # sketch larger than shared memory
     (2, 70, 640, 384, 131072),     # five o-blocks, k = 131072
     (5, 33, 1024, 256, 16384),     # many rows, short sequences
+    (3, 1, 256, 512, 32768),       # one token per row: a single, mostly zero-filled k-block
+    (2, 65, 384, 256, 65536),      # one token past a 64-token stage
 ]
 
 
