@@ -257,6 +257,18 @@ OPUS_API int opus_ghost_score(const void* a, const void* dLdZ, int dtype, int n_
 OPUS_API int opus_sketch_dot(const float* phi, const float* tau, int n_rows, int64_t k, float alpha, float* score,
                     int accumulate, void* stream);
 
+/*
+ * The same summed over layers in one launch:
+ *   score[b] (+)= sum_l alphas[l] * phi[l][b,:] . tau[l][:]
+ * phi[l] is the [n_rows, k] f32 block at phi + l * layer_stride (floats),
+ * tau[l] the k floats at tau + l * k, alphas [n_layers] f32 on the device.
+ * The scores of a round whose per-layer candidate sketches are kept for the
+ * similarity: the per-layer score terms of compute_GradProd_GC_per_iter
+ * (OPUS/train/data_selection.py:509-536), summed over its layer loop.
+ */
+OPUS_API int opus_sketch_dot_layers(const float* phi, int64_t layer_stride, const float* tau, const float* alphas,
+                           int n_layers, int n_rows, int64_t k, float* score, int accumulate, void* stream);
+
 /* out[i,j] (+)= alpha * phi_a[i,:] . phi_b[j,:]; out is [rows_a, rows_b]
  * (data_selection.py:523 per_val, 579 + 587-588 similarity). */
 OPUS_API int opus_sketch_gram(const float* phi_a, int rows_a, const float* phi_b, int rows_b, int64_t k, float alpha,

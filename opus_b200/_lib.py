@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "opus_ghost_score": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_f32, _c_p, _c_int,
                                   _c_p]),
     "opus_sketch_dot": (_c_int, [_c_p, _c_p, _c_int, _c_i64, _c_f32, _c_p, _c_int, _c_p]),
+    "opus_sketch_dot_layers": (_c_int, [_c_p, _c_i64, _c_p, _c_p, _c_int, _c_int, _c_i64, _c_p, _c_int, _c_p]),
     "opus_sketch_gram": (_c_int, [_c_p, _c_int, _c_p, _c_int, _c_i64, _c_f32, _c_p, _c_int, _c_p]),
     "opus_boltzmann_select": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_f64, _c_p, _c_p, _c_p]),
     "opus_greedy_select": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_p, _c_p]),

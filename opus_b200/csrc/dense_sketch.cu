@@ -292,13 +292,23 @@ constexpr int kDotChunk = 8192;
 constexpr int kDotThreads = 256;
 constexpr int kDotVec = kDotChunk / 4 / kDotThreads;  // 8 float4 per thread
 
+// Several layers in one launch: CTA (layer, row, chunk) reads phi from layer l's
+// block (phi + l * layer_stride) and tau[l], and adds alphas[l] (a device array,
+// or `alpha` when null) times its partial dot to score[row].
 __global__ void __launch_bounds__(kDotThreads) sketch_dot_kernel(const float* __restrict__ phi,
-                                                                 const float* __restrict__ tau, int64_t k,
-                                                                 int n_chunks, float alpha, float* __restrict__ score) {
-  const int64_t row = blockIdx.x / n_chunks;
-  const int64_t c0 = (int64_t)(blockIdx.x % n_chunks) * kDotChunk;
+                                                                 const float* __restrict__ tau_all, int64_t k,
+                                                                 int n_chunks, float alpha, float* __restrict__ score,
+                                                                 int n_rows, int64_t layer_stride,
+                                                                 const float* __restrict__ alphas) {
+  const int64_t per_layer = (int64_t)n_rows * n_chunks;
+  const int64_t layer = blockIdx.x / per_layer;
+  const int64_t in_layer = blockIdx.x % per_layer;
+  const int64_t row = in_layer / n_chunks;
+  const int64_t c0 = (int64_t)(in_layer % n_chunks) * kDotChunk;
   const int64_t c1 = min(k, c0 + kDotChunk);
-  const float* p = phi + row * k;
+  const float* p = phi + layer * layer_stride + row * k;
+  const float* tau = tau_all + layer * k;
+  if (alphas != nullptr) alpha = alphas[layer];
   float acc = 0.0f;
   if ((k & 3) == 0) {
     const float4* p4 = reinterpret_cast<const float4*>(p);
@@ -432,7 +442,31 @@ int opus_sketch_dot(const float* phi, const float* tau, int n_rows, int64_t k, f
   const int64_t n_chunks = (k + kDotChunk - 1) / kDotChunk;
   const int64_t grid = (int64_t)n_rows * n_chunks;
   if (grid > 0x7fffffff) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_dot: too many rows");
-  sketch_dot_kernel<<<(int)grid, kDotThreads, 0, st>>>(phi, tau, k, (int)n_chunks, alpha, score);
+  sketch_dot_kernel<<<(int)grid, kDotThreads, 0, st>>>(phi, tau, k, (int)n_chunks, alpha, score, n_rows, 0,
+                                                         nullptr);
+  ::opus::note_launch();
+  OPUS_CUDA_TRY(cudaGetLastError());
+  return OPUS_OK;
+}
+
+int opus_sketch_dot_layers(const float* phi, int64_t layer_stride, const float* tau, const float* alphas,
+                           int n_layers, int n_rows, int64_t k, float* score, int accumulate, void* stream) {
+  if (n_rows < 0 || n_layers < 0 || k <= 0 || layer_stride < (int64_t)n_rows * k)
+    return set_error(OPUS_ERR_INVALID, "sketch_dot_layers: bad sizes");
+  if (n_rows == 0) return OPUS_OK;
+  if (!score || (n_layers > 0 && (!phi || !tau || !alphas)))
+    return set_error(OPUS_ERR_INVALID, "sketch_dot_layers: NULL pointer");
+  if ((k & 3) == 0 && (((reinterpret_cast<uintptr_t>(phi) | reinterpret_cast<uintptr_t>(tau)) & 15) != 0 ||
+                       (layer_stride & 3) != 0))
+    return set_error(OPUS_ERR_INVALID, "sketch_dot_layers: phi, tau and the layer stride must be 16-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (!accumulate) OPUS_CUDA_TRY(cudaMemsetAsync(score, 0, (size_t)n_rows * sizeof(float), st));
+  if (n_layers == 0) return OPUS_OK;
+  const int64_t n_chunks = (k + kDotChunk - 1) / kDotChunk;
+  const int64_t grid = (int64_t)n_layers * n_rows * n_chunks;
+  if (grid > 0x7fffffff) return set_error(OPUS_ERR_UNSUPPORTED, "sketch_dot_layers: too many rows");
+  sketch_dot_kernel<<<(int)grid, kDotThreads, 0, st>>>(phi, tau, k, (int)n_chunks, 1.0f, score, n_rows,
+                                                         layer_stride, alphas);
   ::opus::note_launch();
   OPUS_CUDA_TRY(cudaGetLastError());
   return OPUS_OK;

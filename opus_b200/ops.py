@@ -407,6 +407,30 @@ def sketch_dot(phi: torch.Tensor, tau: torch.Tensor, alpha: float = 1.0, out: to
     return out
 
 
+def sketch_dot_layers(phis: torch.Tensor, taus: torch.Tensor, alphas: torch.Tensor,
+                      out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """out[b] (+)= sum_l alphas[l] * phis[l, b] . taus[l], every layer in one launch.
+
+    phis [L, B, k] (each layer's [B, k] block contiguous; the layer stride may be
+    larger, as for rows [lo, hi) of a longer buffer), taus [L, k], alphas [L] f32.
+    """
+    _cuda(phis, "phis")
+    if phis.dim() != 3 or phis.stride(2) != 1 or phis.stride(1) != phis.shape[2]:
+        raise ValueError("phis must be [L, B, k] with contiguous [B, k] blocks")
+    L, B, k = phis.shape
+    taus = _contig(taus.to(torch.float32))
+    alphas = _contig(alphas.to(device=phis.device, dtype=torch.float32))
+    if taus.shape != (L, k) or alphas.numel() != L:
+        raise ValueError(f"taus must be [{L}, {k}] and alphas [{L}]")
+    if out is None:
+        out = torch.empty(B, dtype=torch.float32, device=phis.device)
+        accumulate = False
+    _lib.check(_lib.load().opus_sketch_dot_layers(_ptr(phis), int(phis.stride(0)), _ptr(taus), _ptr(alphas), L, B,
+                                                 k, _ptr(out), int(accumulate), _stream(phis)),
+               "opus_sketch_dot_layers")
+    return out
+
+
 def sketch_gram(phi_a: torch.Tensor, phi_b: torch.Tensor | None = None, alpha: float = 1.0,
                 out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
     _cuda(phi_a, "phi_a")

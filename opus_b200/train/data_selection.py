@@ -910,7 +910,7 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
                                        table_cache=st["tables"], alpha=pl.gscale)
                 if per_val:
                     ops.sketch_gram(phi, st["taus"][pl.pid], alpha=pl.c, out=score[lo:hi], accumulate=True)
-                elif n_total > 0:
+                elif n_total > 0 and not keep_sketches:
                     ops.sketch_dot(phi, st["taus"][pl.pid], alpha=pl.c / n_total, out=score[lo:hi],
                                    accumulate=True)
             return on_plan
@@ -918,6 +918,10 @@ def capture_in_passes(model, device, batch_train, batch_val, optimizer, trainabl
         if not stream_capture(model, device, rows_of(batch_train, lo, hi), empty_val, optimizer, trainable_layers,
                               preconditioner, score_len, cand_handler, precond, fold_scale=True):
             raise RuntimeError("capture in passes: a capture layer's backward hook did not fire")
+    if keep_sketches and not per_val and n_total > 0 and "phis" in st:
+        # the kept sketches give every layer's score term in one launch (not one per layer and pass)
+        alphas = torch.tensor([c / n_total for c in st["cs"]], dtype=torch.float32, device=device)
+        ops.sketch_dot_layers(st["phis"], st["taus"], alphas, out=score, accumulate=True)
     return score, st.get("phis"), st.get("cs", []), st.get("taus")
 
 

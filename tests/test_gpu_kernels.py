@@ -603,3 +603,25 @@ def test_sketch_gemm_epilogue_widths_match_oracle(B, T, d_out, d_in, k, pair, ep
     want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k,
                                      diag=diag.cpu().numpy())
     rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, {epi} epilogue warps")
+
+
+@pytest.mark.parametrize("L,B,k,rows", [(5, 7, 65536, (2, 9)), (3, 4, 1000, (0, 4)), (1, 1, 8192, (0, 1))])
+def test_sketch_dot_layers_matches_per_layer_dots(L, B, k, rows):
+    """Every layer's score term in one launch == per-layer sketch_dot == float64, on a row slice of a
+    longer buffer (the layer stride is the whole buffer's rows)."""
+    torch.manual_seed(L * B + k)
+    lo, hi = rows
+    full = torch.randn(L, hi + 3, k, device=DEV)
+    phis = full[:, lo:hi]
+    taus = torch.randn(L, k, device=DEV)
+    alphas = torch.rand(L, device=DEV) + 0.5
+    got = ops.sketch_dot_layers(phis, taus, alphas)
+    ops.check_device_error("sketch_dot_layers")
+    per = torch.zeros(hi - lo, device=DEV)
+    for l in range(L):
+        ops.sketch_dot(phis[l].contiguous(), taus[l], alpha=float(alphas[l]), out=per, accumulate=True)
+    want = (phis.double() * taus.double()[:, None, :]).sum(-1).mul(alphas.double()[:, None]).sum(0)
+    rel_close(got.cpu().numpy(), want.cpu().numpy(), 1e-5, "sketch_dot_layers")
+    rel_close(per.cpu().numpy(), want.cpu().numpy(), 1e-5, "per-layer sketch_dot")
+    acc = ops.sketch_dot_layers(phis, taus, alphas, out=got.clone(), accumulate=True)
+    rel_close(acc.cpu().numpy(), 2 * want.cpu().numpy(), 1e-5, "accumulate")
