@@ -48,8 +48,8 @@ UNIT = "candidates/s"
 WORKLOAD = "isolated single-layer operator: 256 seqs x 1024 tokens, d_in 768 -> d_out 3072, k=16384, AdamW diag"
 # dram__bytes_read.sum + dram__bytes_write.sum per sketch_gemm launch of the operator workload: a value
 # recorded from an ncu capture (the file named below), not measured by this run
-SKETCH_GEMM_DRAM_BYTES = 3.20e9
-SKETCH_GEMM_TRAFFIC_SOURCE = "profiles/kernels_c2.md: ncu capture of the operator bench, mean of two launches"
+SKETCH_GEMM_DRAM_BYTES = 3.93e9
+SKETCH_GEMM_TRAFFIC_SOURCE = "profiles/kernels_c2.md: ncu capture of the operator bench (CTA pair kernel), mean of two launches"
 # The same for the whole-path workloads: DRAM bytes of the sketch_gemm launches of one step, from an ncu
 # capture of a smaller case scaled by rows (the file named in each entry); recorded values, not measured here
 WHOLE_SKETCH_TRAFFIC: dict = {
