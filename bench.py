@@ -1052,14 +1052,15 @@ def run_wholepath(args, rank, world, local_rank):
     held = torch.cuda.memory_allocated(dev)
     launches0 = ops.kernel_launches()
     mem0 = torch.cuda.memory_stats(dev)
-    s0, s1 = ev(), ev()
+    marks = [ev() for _ in range(args.steps + 1)]  # step boundaries: a slow step shows in step_ms
+    s0, s1 = marks[0], marks[-1]
     with ClockSampler(local_rank) as clk, _lib.KernelTimer() as timer:
         s0.record()
-        for _ in range(args.steps):
+        for i in range(args.steps):
             torch.cuda.nvtx.range_push("timed_round")  # ncu --nvtx --nvtx-include timed_round/ selects it
             idx = select(buf)
             torch.cuda.nvtx.range_pop()
-        s1.record()
+            marks[i + 1].record()
         torch.cuda.synchronize()
     launches = ops.kernel_launches() - launches0
     mem1 = torch.cuda.memory_stats(dev)
@@ -1073,6 +1074,7 @@ def run_wholepath(args, rank, world, local_rank):
     sel_ms = s0.elapsed_time(s1) / args.steps
     gemm_ms = kern.get("opus_sketch_gemm", (0, 0.0))[1] / args.steps
     sel_ms, gemm_ms_max = max_over_ranks(sel_ms, gemm_ms)
+    step_ms = max_over_ranks(*(marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)))
     stage_ms = {name.replace("opus_", ""): round(ms / args.steps, 3) for name, (_, ms) in sorted(kern.items())}
     stage_calls = {name.replace("opus_", ""): n // args.steps for name, (n, _) in sorted(kern.items())}
 
@@ -1164,8 +1166,8 @@ def run_wholepath(args, rank, world, local_rank):
 
     p_lin = capture_layer_weights(cfg)
     flops = 2.0 * seq * p_lin * (nc + npx)  # every candidate's and proxy's per-sample gradient, once per layer
-    return {"cfg": cfg, "ms": sel_ms, "gemm_ms": gemm_ms_max, "flops": flops, "stage_ms": stage_ms,
-            "stage_calls": stage_calls, "capture_ms": cap_ms, "train_ms": train_ms, "e2e": e2e,
+    return {"cfg": cfg, "ms": sel_ms, "step_ms": step_ms, "gemm_ms": gemm_ms_max, "flops": flops,
+            "stage_ms": stage_ms, "stage_calls": stage_calls, "capture_ms": cap_ms, "train_ms": train_ms, "e2e": e2e,
             "clocks": clk.summary(), "launches": launches, "parity": parity, "peak_gb": peak / 1e9,
             "allocator": allocator,
             "rows_per_pass": step, "kept": int(kept.shape[0])}
@@ -1358,6 +1360,7 @@ def emit_wholepath(args, res, world):
                                                 "tokens, gradients accumulated), then AdamW; same model, no "
                                                 "gradient all-reduce")},
             "overhead_pct_of_step": round(100.0 * res["ms"] / res["train_ms"], 1),
+            "step_ms": [round(x, 2) for x in res["step_ms"]],  # each timed step, max over ranks
             "capture_ms": round(res["capture_ms"], 2), "train_step_ms": round(res["train_ms"], 2),
             "stage_ms": res["stage_ms"], "stage_calls_per_step": res["stage_calls"],
             "selection_peak_gb_above_model": round(res["peak_gb"], 2), "allocator_in_timed_region": res["allocator"],
