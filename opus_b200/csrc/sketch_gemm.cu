@@ -520,7 +520,6 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
     const int et = threadIdx.x - 64;          // 0 .. 32 * EPI - 1
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
     const int grp = (warp - 2) >> 2;          // chunks grp, grp + kGroups, ...
-    const int last_j = grp + ((kChunks - 1 - grp) / kGroups) * kGroups;  // this warp's last chunk
     const int r = q * 32 + lane;              // tile row owned by this thread
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t kk32 = static_cast<uint32_t>(k);
@@ -570,8 +569,12 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
         }
         continue;
       }
-      const uint4* tp = table + ((int64_t)ob * n_cb + walk.cb(tile)) * kEntriesPerTile + r;
+      const int cb = walk.cb(tile);
+      const uint4* tp = table + ((int64_t)ob * n_cb + cb) * kEntriesPerTile + r;
       const uint32_t col0 = static_cast<uint32_t>(acc * kTileN);
+      // chunks that hold a column below d_in, none if this warp's 32 rows lie past d_out: the
+      // table pads the rest with bucket 0 and weight 0, whose updates add nothing
+      const int n_live = ob * kTileM + q * 32 >= d_out ? 0 : min(kChunks, ceil_div(d_in - cb * kTileN, kCols));
       // chunk j: its table entries (column pairs j * kPairs ..) in flight, then its accumulator columns
       auto load_chunk = [&](int j, uint4(&ent)[kPairs], uint32_t(&v)[kCols]) {
 #pragma unroll
@@ -587,7 +590,7 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
       if (smem_sketch && !scaled) {
         // First tile of this candidate in this CTA: scale from max |w G| over the tile.
         float m = 0.0f;
-        for (int j = grp; j < kChunks; j += kGroups) {
+        for (int j = grp; j < n_live; j += kGroups) {
           uint4 ent[kPairs];
           uint32_t v[kCols];
           load_chunk(j, ent, v);
@@ -624,12 +627,13 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
       }
       const float S = ldexpf(1.0f, scale_exp);
       const bool use_int = smem_sketch && scaled;
+      if (grp >= n_live) release(acc);  // nothing of this tile to scatter for this warp
 #pragma unroll 1
-      for (int j = grp; j < kChunks; j += kGroups) {
+      for (int j = grp; j < n_live; j += kGroups) {
         uint4 ent[kPairs];
         uint32_t v[kCols];
         load_chunk(j, ent, v);
-        if (j == last_j) release(acc);  // the warp's accumulator reads are done
+        if (j + kGroups >= n_live) release(acc);  // the warp's accumulator reads are done
 #pragma unroll
         for (int p = 0; p < kPairs; ++p) {
           const uint4 e = ent[p];
