@@ -605,6 +605,29 @@ def test_sketch_gemm_epilogue_widths_match_oracle(B, T, d_out, d_in, k, pair, ep
     rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, {epi} epilogue warps")
 
 
+@pytest.mark.parametrize("epi", ["8", "12", "16"])
+@pytest.mark.parametrize("pair", ["0", "1"])
+@pytest.mark.parametrize("d_out,d_in", [(296, 520), (224, 504), (1600, 1600), (136, 264)])
+def test_sketch_gemm_padded_edges_match_oracle(d_out, d_in, pair, epi, monkeypatch):
+    """Edges of the padded tiles the scatter skips: a last o-block whose second TMEM lane quarter
+    holds 8 real rows (296 = 2*128 + 40) or whose last quarter holds none (224 = 128 + 96), and
+    a last column block with 8 real columns (520, 264) or 248 (504)."""
+    monkeypatch.setenv("OPUS_SKETCH_EPI_WARPS", epi)
+    monkeypatch.setenv("OPUS_SKETCH_PAIR", pair)
+    B, T, k = 2, 70, 65536
+    torch.manual_seed(d_out * 3 + d_in)
+    g = (torch.randn(B, T, d_out, device=DEV) * 1e-3).bfloat16()
+    a = torch.randn(B, T, d_in, device=DEV).bfloat16()
+    h, s, packed = cuda_tables(d_out * d_in, 11, k)
+    diag = torch.rand(d_out, d_in, device=DEV) * 1e-3 + 1e-6
+    table = ops.build_sketch_table(packed, d_out, d_in, diag=diag)
+    phi = ops.sketch_gemm(g, a, table, k, max_bucket_load=ops.bucket_max_load(packed, k))
+    ops.check_device_error(f"sketch_gemm padded edges, {epi} epilogue warps")
+    want = orc.project_full_gradient(g.float().cpu().numpy(), a.float().cpu().numpy(), h, s, k,
+                                     diag=diag.cpu().numpy())
+    rel_close(phi.cpu().numpy(), want, 1e-4, f"phi, padded edges, {epi} epilogue warps")
+
+
 @pytest.mark.parametrize("L,B,k,rows", [(5, 7, 65536, (2, 9)), (3, 4, 1000, (0, 4)), (1, 1, 8192, (0, 1))])
 def test_sketch_dot_layers_matches_per_layer_dots(L, B, k, rows):
     """Every layer's score term in one launch == per-layer sketch_dot == float64, on a row slice of a
