@@ -53,15 +53,15 @@
 namespace opus {
 namespace {
 
-// Epilogue warps: 8 (the dense epilogue, and the scatter's default) or 12.
-// Block size and the dense epilogue's chunking are those of 8.
+// Epilogue warps: 8 (the dense epilogue), 12 or 16 (the scatter; 16 by default).
+// kThreads and the dense epilogue's chunking are those of 8.
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kChunksPerWarp = kChunksPerTile / (kEpiWarps / 4);  // 4
 constexpr int block_threads(int epi) { return 64 + 32 * epi; }
 
-constexpr int kHeadroomLog2 = 4;                     // first-tile max maps to cap / 16
+constexpr int kHeadroomLog2 = 4;                     // sampled first-tile max maps to cap / 16
 constexpr int kBoxMN = 64;                           // bf16 elements per 128-byte swizzle row
 constexpr int kUmmaK = 16;                           // K of one kind::f16 MMA
 constexpr int kGBoxes = kTileM / kBoxMN;             // 2 boxes for the 128 weight rows
@@ -588,9 +588,13 @@ __global__ void __launch_bounds__(block_threads(EPI), 1)
         tmem_ld_wait();
       };
       if (smem_sketch && !scaled) {
-        // First tile of this candidate in this CTA: scale from max |w G| over the tile.
+        // First tile of this job: scale from max |w G| over a sample of the tile, the first
+        // live chunk of every warp (1/8 of the tile with 16 warps).  The sample's maximum is at
+        // most the tile's, so the scale is at least as fine as a whole-tile one; a value more
+        // than 16 times the sample's maximum takes the exact f32 path.
         float m = 0.0f;
-        for (int j = grp; j < n_live; j += kGroups) {
+        if (grp < n_live) {
+          const int j = grp;
           uint4 ent[kPairs];
           uint32_t v[kCols];
           load_chunk(j, ent, v);
