@@ -155,9 +155,10 @@ OPUS_API int opus_build_sketch_table(const uint32_t* packed, const float* diag, 
  *         (OPUS/layers/linear.py:118-119) can ride here instead of a pass
  *         over dL/dZ.
  * Accuracy: each update is rounded to a power-of-two quantum of at most
- * 2^-(log2(2^31/max_bucket_load) - 3) times the largest |w G| of the
- * candidate's first tile in the CTA (~1e-6 relative for GPT-2 layers);
- * larger, NaN or Inf updates are added exactly in f32.
+ * 2^-(log2(2^31/max_bucket_load) - 3) times the largest |w G| of a sample
+ * of the job's first tile in the CTA, itself at most the tile's largest
+ * (~1e-6 relative for GPT-2 layers); larger, NaN or Inf updates are added
+ * exactly in f32.
  * Replaces GradientProjector.project_full_gradient
  * (OPUS/train/random_projection.py:134-193) on 3-D inputs.
  */

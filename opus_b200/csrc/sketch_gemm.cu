@@ -18,15 +18,15 @@
 //
 // Shared-memory sketch in 32-bit fixed point.  Float atomics on shared memory
 // are compare-and-swap loops on this hardware, integer adds are native, so
-// the CTA-private sketch of the current candidate holds int32 buckets at a
-// power-of-two scale S chosen from the candidate's first tile in this CTA
-// (max |w G| maps to cap/16).  cap = 2^31 / (largest bucket load of the
+// the CTA-private sketch of the current job holds int32 buckets at a
+// power-of-two scale S chosen from a sample of the job's first tile (each
+// epilogue warp's first live chunk; the sample's max |w G| maps to cap/16).  cap = 2^31 / (largest bucket load of the
 // layer) bounds every admitted update, so no bucket can overflow whatever the
 // data; an update above cap (or NaN/Inf, or any update before a scale could
 // be chosen) goes straight to the f32 output row with a global atomic add.
 // The sketch is converted back to f32 and added to the output row (vector
 // reductions) whenever the candidate changes.  Quantisation error per update
-// is at most (max |w G| of the first tile) * 2^-(log2(cap) - 4 + 1), i.e.
+// is at most (max |w G| of the sample) * 2^-(log2(cap) - 4 + 1), i.e.
 // ~1e-6 of the tile maximum for the GPT-2 layer shapes.  When the k buckets
 // do not fit next to two pipeline stages (k > 32768), the sketch covers the
 // largest prefix of them that does (32768 buckets) and the updates of the
@@ -751,7 +751,7 @@ struct JobPlan {
 // Each candidate's walk is split into `groups` jobs so that the rounds of jobs
 // over the SMs waste the least time: minimise ceil(jobs / SMs) x (tiles per
 // job + 1), the 1 standing for a job's fixed cost (its sketch flush and the
-// scale pass over its first tile), preferring larger jobs on ties.
+// scale pass over a sample of its first tile), preferring larger jobs on ties.
 // OPUS_SKETCH_ORDER=ob|cb and OPUS_SKETCH_JOBS=tiles|lines force either choice.
 JobPlan plan_jobs(int n_rows, int d_out, int d_in, int n_ob, int workers) {
   const int sms = workers;  // CTAs, or CTA pairs, that take jobs
