@@ -8,13 +8,15 @@
 // h(o,c) of candidate b's sketch.  G_b is never written to HBM.
 //
 // Warp roles (64 + 32 x 8, 12 or 16 epilogue warps threads; persistent, one
-// CTA per SM; in a pair the MMA warp of the second CTA stays idle):
+// CTA per SM; in a pair the MMA warp of the second CTA issues no MMA and
+// forwards its epilogue's accumulator releases to the leader):
 //   warp 0      TMA producer: 3-D tile loads of dLdZ and a into a ring of
 //               shared-memory stages (128-byte swizzle, MN-major operands);
 //   warp 1      TMEM allocation + single-thread UMMA issue into one of two
 //               256-column accumulators (double-buffered against the epilogue);
 //   warps 2..   epilogue: 8, 12 or 16 warps, two to four per TMEM lane
-//               quarter, dealt the tile's 32-, 16- or 8-column chunks round-robin.
+//               quarter, dealt the tile's 32-, 16- or 8-column chunks round-robin;
+//               chunks past d_in and lane quarters past d_out are skipped.
 //
 // Shared-memory sketch in 32-bit fixed point.  Float atomics on shared memory
 // are compare-and-swap loops on this hardware, integer adds are native, so
@@ -29,8 +31,8 @@
 // is at most (max |w G| of the sample) * 2^-(log2(cap) - 4 + 1), i.e.
 // ~1e-6 of the tile maximum for the GPT-2 layer shapes.  When the k buckets
 // do not fit next to two pipeline stages (k > 32768), the sketch covers the
-// largest prefix of them that does (32768 buckets) and the updates of the
-// other buckets are f32 global atomic adds.
+// largest prefix of them that does (32768 buckets for one CTA, 40960 or 45056
+// for a pair) and the updates of the other buckets are f32 global atomic adds.
 //
 // CTA pairs (sketches larger than one CTA's shared memory): a cluster of two
 // CTAs computes 256 x 256 tiles with tcgen05.mma.cta_group::2.  Each CTA
